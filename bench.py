@@ -1,0 +1,393 @@
+#!/usr/bin/env python
+"""Benchmark of the int4 / int8 weight-only dequant-matvec hot path on B200.
+
+Workload (one step): one decode token through LAYERS=32 resident int4 MLP
+pairs — for each layer, up [4096 x 11008] then down [11008 x 4096], group-64
+scales, M=1 activation row, fp32 accumulation. 32 distinct weight copies
+(1.63 GB) are streamed per step, so every matvec reads HBM, not L2 (126 MB).
+Each step is one CUDA-graph replay of the 64 launches.
+
+  value    algorithmic GB/s over the device-timed region (CUDA events, max over
+           ranks), bytes per matvec = codes + scales + x + out (each once)
+  e2e      the same bytes through the C-ABI MatVec entry point (tq_matvec) with
+           host buffers: every call copies x host->device and out device->host
+  roofline the matvec kernel's achieved GB/s (per-launch CUDA events inside the
+           timed graph) against the measured HBM copy bandwidth
+  cpu_baseline  the CPU oracle (AVX2 restatement of quant4_simd.go with the
+           reference's worker split) on the host cores, bounded sample
+
+`--impl reference` times the reference's CPU implementation of the path (the
+oracle's AVX2 restatement; the Go reference cannot be built here) on the same
+config. Under torchrun (N>1) every rank streams its own copy of the workload
+(replicas, weak scaling); the kernels exchange nothing.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "int8/int4 dequant-matvec HBM GB/s (% of peak); decode tokens/s at 1/2/4/8 GPU"
+K_UP, N_UP = 4096, 11008
+LAYERS = 32
+FALLBACK_HBM_GBS = 6650.0
+WORKLOAD = ("int4 g64 MLP pair (up 4096x11008 + down 11008x4096), M=1, fp32 accumulate; "
+            "32 resident layer copies streamed per step")
+
+
+def algo_bytes(bits: int, rows: int, cols: int, m: int) -> int:
+    """Codes + scales + x + out, each counted once."""
+    codes = rows * cols if bits == 8 else rows * cols // 2
+    scales = cols * 4 if bits == 8 else ((rows + 63) // 64) * cols * 4
+    return codes + scales + 4 * m * rows + 4 * m * cols
+
+
+def pair_bytes(m: int = 1) -> int:
+    return algo_bytes(4, K_UP, N_UP, m) + algo_bytes(4, N_UP, K_UP, m)
+
+
+def load_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, index: int, period: float = 0.01):
+        self.index, self.period = index, period
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for b, name in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml"}
+
+
+# ---------------------------------------------------------------------------
+# CPU side (oracle): the reference's algorithm on the host cores
+# ---------------------------------------------------------------------------
+
+def cpu_pairs(npairs: int, seed: int = 1):
+    from oracle import oracle as O
+    pairs = []
+    for l in range(npairs):
+        up = O.quantize4(O.synth((K_UP, N_UP), seed, 2 * l, 0.02))
+        down = O.quantize4(O.synth((N_UP, K_UP), seed, 2 * l + 1, 0.02))
+        pairs.append((up, down))
+    x_up = O.synth((K_UP,), seed, 1000, 1.0)
+    x_down = O.synth((N_UP,), seed, 1001, 1.0)
+    return pairs, x_up, x_down
+
+
+def cpu_pair_pass(pairs, x_up, x_down, l):
+    from oracle import oracle as O
+    (qu, su), (qd, sd) = pairs[l % len(pairs)]
+    O.q4_matmul(qu, su, K_UP, N_UP, x_up, O.AVX2)
+    O.q4_matmul(qd, sd, N_UP, K_UP, x_down, O.AVX2)
+
+
+def cpu_baseline(seconds: float = 8.0):
+    """Oracle AVX2 MatVec on all host threads, 2 alternating pairs (100 MB,
+    beyond the last-level cache), run for about `seconds`."""
+    from oracle import oracle as O
+    threads = O.set_threads(0)
+    pairs, xu, xd = cpu_pairs(2)
+    for l in range(2):
+        cpu_pair_pass(pairs, xu, xd, l)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        cpu_pair_pass(pairs, xu, xd, n)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(pair_bytes() * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} MLP-pair passes (up+down, M=1) over 2 alternating resident pairs (101.7 MB), "
+                      f"{dt:.1f} s, oracle AVX2 restatement of quant4_simd.go with the reference worker split"}
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    threads = O.set_threads(0)
+    pairs, xu, xd = cpu_pairs(2)
+    for w in range(max(args.warmup, 1)):
+        cpu_pair_pass(pairs, xu, xd, w)
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        cpu_pair_pass(pairs, xu, xd, s)
+    dt = time.perf_counter() - t0
+    value = pair_bytes() * args.steps / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Irwin-Hall normal: weights std 0.02, activations std 1)",
+        "config": bench_config(),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "each step = one MLP pair (up+down, M=1), alternating between 2 resident "
+                                   "pairs (101.7 MB); the Go reference cannot be built here (no Go "
+                                   "toolchain), so its AVX2 kernel runs as the oracle's C restatement"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def bench_config():
+    return {"workload": WORKLOAD.replace("32 resident", f"{LAYERS} resident"), "weights": "int4 group-64 (QuantizeMatrix4 layout)", "m": 1,
+            "layers_per_step": LAYERS, "bytes_per_step": pair_bytes() * LAYERS,
+            "l2": f"inputs larger than L2: {pair_bytes() * LAYERS / 1e9:.2f} GB of weights streamed per step",
+            "launch": "one CUDA graph replay per step"}
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+
+def run_gpu(args, rank: int, world: int):
+    import torch
+    import torch.distributed as dist
+
+    from tensai_b200 import _lib
+    from tensai_b200 import quant as Q
+
+    dev = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(dev)
+    L = _lib.load()
+    _lib.check(L.tq_set_device(dev))
+
+    # Resident weights: generated and quantized on the device.
+    handles = []
+    tmp = torch.empty(K_UP * N_UP, device="cuda", dtype=torch.float32)
+    for l in range(LAYERS):
+        for j, (r, c) in enumerate(((K_UP, N_UP), (N_UP, K_UP))):
+            w = tmp.view(r, c)
+            Q.synth_dev(w, 1, 2 * l + j, 0.02)
+            handles.append(Q.quantize_dev(w, 4))
+    torch.cuda.synchronize()
+    del tmp
+    x_up = torch.empty(1, K_UP, device="cuda")
+    x_dn = torch.empty(1, N_UP, device="cuda")
+    Q.synth_dev(x_up, 1, 1000, 1.0)
+    Q.synth_dev(x_dn, 1, 1001, 1.0)
+    o_up = torch.empty(1, N_UP, device="cuda")
+    o_dn = torch.empty(1, K_UP, device="cuda")
+
+    stream = torch.cuda.Stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    mm = L.tq_matmul_dev
+    xu, xd, ou, od = (ctypes.c_void_p(t.data_ptr()) for t in (x_up, x_dn, o_up, o_dn))
+
+    def step(ev=None):
+        for l in range(LAYERS):
+            for j in range(2):
+                h = handles[2 * l + j]
+                if ev is not None:
+                    ev[2 * (2 * l + j)].record(stream)
+                rc = mm(h, xu if j == 0 else xd, ou if j == 0 else od, 1, sp)
+                if ev is not None:
+                    ev[2 * (2 * l + j) + 1].record(stream)
+                if rc:
+                    _lib.check(rc)
+
+    with torch.cuda.stream(stream):
+        step()  # configures kernels outside capture
+    torch.cuda.synchronize()
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+    # The last timed step runs the same 64 launches eagerly with an event pair
+    # around each one: per-launch kernel durations (events recorded inside a
+    # graph cannot be timed).
+    kev = [torch.cuda.Event(enable_timing=True) for _ in range(4 * LAYERS)]
+
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps - 1):
+                graph.replay()
+            step(kev)
+            end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    kernel_ms = [kev[2 * i].elapsed_time(kev[2 * i + 1]) for i in range(2 * LAYERS)]
+
+    ms_t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    bytes_step = pair_bytes() * LAYERS
+    value = bytes_step * world * args.steps / (ms_max * 1e-3) / 1e9
+
+    # End to end through the C-ABI MatVec (host buffers, synchronous calls).
+    from oracle import oracle as O  # noqa: F401  (seeded host inputs only)
+    hx_up = x_up.cpu().numpy().reshape(-1).copy()
+    hx_dn = x_dn.cpu().numpy().reshape(-1).copy()
+    ho_up = np.empty(N_UP, np.float32)
+    ho_dn = np.empty(K_UP, np.float32)
+    pv = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    e2e_steps = max(1, min(args.steps, 20))
+
+    def e2e_step():
+        for l in range(LAYERS):
+            _lib.check(L.tq_matvec(handles[2 * l], pv(hx_up), K_UP, pv(ho_up), N_UP))
+            _lib.check(L.tq_matvec(handles[2 * l + 1], pv(hx_dn), N_UP, pv(ho_dn), K_UP))
+
+    e2e_step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_value = bytes_step * world * e2e_steps / float(e2e_t.item()) / 1e9
+
+    if rank == 0:
+        peak, peak_src = load_peak()
+        per_launch = pair_bytes() / 2  # up and down carry the same algorithmic bytes
+        kavg = statistics.mean(kernel_ms)
+        achieved = per_launch / (kavg * 1e-3) / 1e9
+        traffic = load_traffic().get("qmv_int4_m1_mlp_pair")
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Irwin-Hall normal: weights std 0.02, activations std 1)",
+            "config": bench_config(),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "frac_of_8tbs": round(achieved / 8000.0, 4),
+                         "traffic": traffic, "kernel": "qmv_kernel<4,1,*> (int4 dequant-matvec, M=1)",
+                         "kernel_us_mean": round(kavg * 1e3, 3),
+                         "algorithmic_bytes_per_launch": per_launch},
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": LAYERS * 4 * (K_UP + N_UP),
+                    "d2h_bytes_per_step": LAYERS * 4 * (N_UP + K_UP),
+                    "api": "tq_matvec (host x/out, synchronous), the MatVec drop-in", "steps": e2e_steps},
+            "gpu_launches": args.steps * 2 * LAYERS,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    del graph
+    for h in handles:
+        Q.free(h)
+
+
+def main():
+    global LAYERS
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)  # >= 2: the last step carries the per-launch events
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="resident MLP pairs per step (default 32 = 1.63 GB; small values for profiling)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.steps = max(args.steps, 2)
+    LAYERS = max(1, args.layers)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        run_gpu(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,159 @@
+/*
+ * tensai_cuda.h — C ABI of libtensai_cuda.so, the B200 (sm_100a) backend for
+ * tensai's weight-only quantized inference path (github.com/mattn/tensai).
+ *
+ * The Go package reaches this library the way wgpu.go reaches wgpu-native:
+ * purego.Dlopen + RegisterLibFunc (wgpu_dlopen.go:9-11, wgpu.go:292-357),
+ * no cgo. Every entry point therefore takes only scalars and plain pointers,
+ * returns an int status (0 = success, negative = error), never aborts the
+ * process, and leaves a human-readable message in tq_last_error() on the
+ * calling thread. Messages for argument errors repeat the reference's own
+ * wording ("tensai: ..."), so the Go shim can return them unchanged.
+ *
+ * Threading: every entry point is thread-safe. Host-pointer calls run on a
+ * per-thread, per-device CUDA stream with per-thread staging buffers; matrix
+ * handles are read-only after creation and may be shared across threads.
+ * Freeing a handle while another thread computes with it is a caller error,
+ * as using a freed GPUTensor is in the reference (wgputensor.go:676-686).
+ *
+ * Ownership: the library copies codes and scales into device memory at
+ * upload/quantize time and keeps them resident in HBM until tq_free.
+ */
+#ifndef TENSAI_CUDA_H
+#define TENSAI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TQ_EXPORT __attribute__((visibility("default")))
+#else
+#define TQ_EXPORT
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TQ_ABI_VERSION 1
+
+/* Status codes. */
+#define TQ_OK 0
+#define TQ_ERR_ARG (-1)         /* bad argument (null pointer, negative size, odd int4 column count) */
+#define TQ_ERR_SHAPE (-2)       /* x/out lengths do not match the matrix */
+#define TQ_ERR_HANDLE (-3)      /* unknown or freed handle */
+#define TQ_ERR_CUDA (-4)        /* a CUDA runtime call failed; message has the CUDA error string */
+#define TQ_ERR_NOMEM (-5)       /* device or pinned allocation failed */
+#define TQ_ERR_UNSUPPORTED (-6) /* no sm_100 device, or a size beyond a documented limit */
+#define TQ_ERR_TIMEOUT (-7)     /* a kernel gave up a bounded wait (see tq_device_status) */
+
+/* Library version gate, as wgpu.go:292-313 checks wgpu-native's version. */
+TQ_EXPORT int tq_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+TQ_EXPORT const char *tq_last_error(void);
+
+/* Number of visible CUDA devices; selects the device that later calls on
+ * this thread create handles on (default 0). */
+TQ_EXPORT int tq_device_count(int *n);
+TQ_EXPORT int tq_set_device(int device);
+
+/* ---- quantized matrices ------------------------------------------------- */
+
+/* Uploads an int8 QMatrix: q = QMatrix.Q (rows*cols bytes, row-major; the
+ * reference's 16 pad bytes are not read), scale = QMatrix.Scale (cols).
+ * Replaces: type QMatrix (quant.go:29-33), made resident for MatVec. */
+TQ_EXPORT int tq_q8_upload(const int8_t *q, const float *scale, int rows, int cols, uint64_t *handle);
+
+/* Uploads an int4 Q4Matrix: q = Q4Matrix.Q (rows*cols/2 bytes, byte (i,j)
+ * holding column j in its low nibble and column j+cols/2 in its high one),
+ * scale = Q4Matrix.Scale (ceil(rows/64)*cols, group-major).
+ * Replaces: type Q4Matrix (quant4.go:20-24). cols must be even. */
+TQ_EXPORT int tq_q4_upload(const uint8_t *q, const float *scale, int rows, int cols, uint64_t *handle);
+
+/* Quantizes a host float32 matrix [rows][cols] on the device and writes the
+ * reference's exact byte layout back: q gets rows*cols (+16 zero pad) bytes,
+ * scale gets cols floats. Bit-exact with QuantizeMatrix (quant.go:37-72). */
+TQ_EXPORT int tq_quantize8(const float *w, int rows, int cols, int8_t *q, float *scale);
+
+/* As tq_quantize8 for QuantizeMatrix4 (quant4.go:28-89): q gets
+ * rows*cols/2 (+16 zero pad) bytes, scale gets ceil(rows/64)*cols floats.
+ * Odd cols -> TQ_ERR_ARG, "tensai: quantize4 needs an even column count, got N"
+ * (quant4.go:29-31). */
+TQ_EXPORT int tq_quantize4(const float *w, int rows, int cols, uint8_t *q, float *scale);
+
+/* Quantizes a DEVICE float32 matrix [rows][cols] (row-major, on the current
+ * device) straight into a new resident handle, with no host round trip:
+ * the quantize-on-load path of _example/qwen/model.go:126-140 kept on the GPU.
+ * stream: a cudaStream_t (NULL = legacy default stream). The handle is ready
+ * for use on that stream; the call does not synchronize. */
+TQ_EXPORT int tq_quantize8_dev(const float *w, int rows, int cols, void *stream, uint64_t *handle);
+TQ_EXPORT int tq_quantize4_dev(const float *w, int rows, int cols, void *stream, uint64_t *handle);
+
+/* bits (8 or 4), rows, cols of a handle. Any output pointer may be NULL. */
+TQ_EXPORT int tq_matrix_info(uint64_t handle, int *bits, int *rows, int *cols);
+
+/* Copies a handle's codes and scales back in the reference layout (the same
+ * sizes tq_quantize8/4 write, including the 16 zero pad bytes). */
+TQ_EXPORT int tq_download(uint64_t handle, void *q, float *scale);
+
+/* Releases the device copy. Freeing 0 or an already freed handle is a no-op,
+ * as GPUTensor.Free is idempotent (wgputensor.go:676-686). */
+TQ_EXPORT int tq_free(uint64_t handle);
+
+/* ---- compute ------------------------------------------------------------ */
+
+/* out = x @ W for one activation row, host buffers, synchronous.
+ * Replaces: (*QMatrix).MatVec (quant.go:77-103) and (*Q4Matrix).MatVec
+ * (quant4.go:93-119). x_len must equal rows and out_len cols, else
+ * TQ_ERR_SHAPE with the reference's message
+ * "tensai: qmatvec shape mismatch: x=%d out=%d, want %dx%d" (quant.go:79)
+ * or "tensai: q4matvec ..." (quant4.go:95). out is overwritten. */
+TQ_EXPORT int tq_matvec(uint64_t handle, const float *x, size_t x_len, float *out, size_t out_len);
+
+/* out[m][cols] = x[m][rows] @ W for m activation rows, host buffers,
+ * synchronous. The reference has no batched call: this equals m MatVec calls
+ * (quant.go:77, applied per row). m <= 8 runs on the CUDA-core kernels. */
+TQ_EXPORT int tq_matmul(uint64_t handle, const float *x, float *out, int m);
+
+/* As tq_matmul with DEVICE pointers (x: m*rows floats, out: m*cols floats,
+ * on the handle's device), enqueued on stream (a cudaStream_t; NULL = legacy
+ * default stream). Does not synchronize. The library keeps a small scratch
+ * per (device, stream), created on the first call on that stream, so that
+ * first call must not happen inside a CUDA-graph capture; graphs holding
+ * these launches must not be replayed concurrently with each other. */
+TQ_EXPORT int tq_matmul_dev(uint64_t handle, const float *x, float *out, int m, void *stream);
+
+/* Selects the GPU kernel behind tq_matvec / tq_matmul / tq_matmul_dev for
+ * m <= 8 (process-wide): 0 = tensor-core integer MMA (default: weights used as
+ * stored, activations split into exact int8 digit planes); 1 = CUDA-core
+ * fp32 FMA. Both are GPU implementations with the same contract; there is no
+ * CPU path. */
+TQ_EXPORT int tq_set_matvec_kernel(int which);
+
+/* ---- synthetic inputs ----------------------------------------------------- */
+
+/* Fills n floats on the current device with the seeded generator the CPU
+ * oracle uses (Irwin-Hall(12) normal with standard deviation sigma; element i
+ * depends only on (seed, stream_id, i)). Stand-in for RandomMatrix
+ * (tensor.go:269-277) and NormFloat64 activations, bit-identical on host and
+ * device. cuda_stream: a cudaStream_t or NULL. */
+TQ_EXPORT int tq_synth_dev(float *out, size_t n, uint64_t seed, uint64_t stream_id, float sigma, void *cuda_stream);
+
+/* Waits for all work on the current device, then returns and clears its
+ * status bits: bit 0 (TQ_STATUS_TIMEOUT = 1) means a kernel gave up waiting
+ * for a weight copy (bounded at 2 s) and its output is invalid. The host-
+ * pointer calls check this themselves and return TQ_ERR_TIMEOUT. */
+TQ_EXPORT int tq_device_status(unsigned *bits);
+
+/* ---- host-side fault injection (tests) ------------------------------------ */
+
+/* Makes the next n device allocations made by this library fail with
+ * TQ_ERR_NOMEM, so error paths can be tested without touching the GPU. */
+TQ_EXPORT int tq_debug_fail_allocs(int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TENSAI_CUDA_H */

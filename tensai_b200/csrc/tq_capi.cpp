@@ -1,0 +1,505 @@
+// tq_capi.cpp — the C ABI of libtensai_cuda.so (declared in
+// include/tensai_cuda.h): handle table, argument checks with the reference's
+// error wording, per-thread streams and staging, and dispatch to the kernels.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <map>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "../../include/tensai_cuda.h"
+#include "tq_common.cuh"
+#include "tq_internal.h"
+
+namespace {
+
+thread_local std::string t_err;
+thread_local int t_device = 0;
+std::atomic<int> g_fail_allocs{0};
+
+std::mutex g_mu;
+std::unordered_map<uint64_t, std::shared_ptr<Handle>> g_handles;
+uint64_t g_next_handle = 1;
+
+// Per-thread, per-device context for the host-pointer entry points.
+struct ThreadCtx {
+    cudaStream_t stream = nullptr;
+    float *d_x = nullptr, *d_out = nullptr;
+    size_t d_x_cap = 0, d_out_cap = 0;
+    float *h_x = nullptr, *h_out = nullptr; // pinned staging
+    size_t h_x_cap = 0, h_out_cap = 0;
+};
+thread_local std::unordered_map<int, ThreadCtx> t_ctx;
+
+// Matvec scratch, one per (device, stream): kernels on one stream run in
+// order, so they may share it; kernels on different streams never do.
+std::mutex g_scratch_mu;
+std::map<std::pair<int, cudaStream_t>, TqScratch> g_scratch;
+
+} // namespace
+
+int tq_fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_err = buf;
+    return code;
+}
+
+int tq_cuda_fail(cudaError_t e, const char *what) {
+    cudaGetLastError(); // clear a sticky-free error so the next call starts clean
+    return tq_fail(e == cudaErrorMemoryAllocation ? TQ_ERR_NOMEM : TQ_ERR_CUDA, "tensai: %s: %s (%s)", what,
+                   cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+cudaError_t tq_dev_malloc(void **p, size_t bytes) {
+    int f = g_fail_allocs.load();
+    while (f > 0) {
+        if (g_fail_allocs.compare_exchange_weak(f, f - 1)) {
+            *p = nullptr;
+            return cudaErrorMemoryAllocation;
+        }
+    }
+    return cudaMalloc(p, bytes ? bytes : 1);
+}
+
+static ThreadCtx *ctx_for(int device) { return &t_ctx[device]; }
+
+// The scratch of (device, stream), created and cleared on first use; the first
+// matvec on a stream must therefore not be inside a CUDA-graph capture.
+static int scratch_for(int device, cudaStream_t st, TqScratch *out) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    auto key = std::make_pair(device, st);
+    auto it = g_scratch.find(key);
+    if (it != g_scratch.end()) {
+        *out = it->second;
+        return TQ_OK;
+    }
+    TqScratch s{nullptr, nullptr, nullptr, nullptr};
+    const size_t words = TQ_MAX_TILES + 32; // arrival counters, then the status word
+    cudaError_t e = tq_dev_malloc((void **)&s.partial, TQ_SCRATCH_PARTIAL_FLOATS * sizeof(float));
+    if (e == cudaSuccess) e = tq_dev_malloc((void **)&s.counters, words * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemsetAsync(s.counters, 0, words * sizeof(unsigned), st);
+    if (e == cudaSuccess) e = tq_dev_malloc((void **)&s.planes, TQ_SCRATCH_PLANES_BYTES);
+    s.status = s.counters + TQ_MAX_TILES;
+    if (e != cudaSuccess) {
+        if (s.partial) cudaFree(s.partial);
+        if (s.counters) cudaFree(s.counters);
+        if (s.planes) cudaFree(s.planes);
+        return tq_cuda_fail(e, "matvec scratch allocation");
+    }
+    g_scratch[key] = s;
+    *out = s;
+    return TQ_OK;
+}
+
+// Reads and clears a scratch's status word (synchronous on st).
+static cudaError_t read_status(const TqScratch &scr, cudaStream_t st, unsigned *out) {
+    unsigned v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, scr.status, sizeof v, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess && v) e = cudaMemsetAsync(scr.status, 0, sizeof v, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    *out |= v;
+    return e;
+}
+
+// 0: tensor-core matvec (tq_igemv.cu, default); 1: CUDA-core matvec (tq_matvec.cu).
+std::atomic<int> g_matvec_kernel{0};
+
+static cudaError_t launch_matvec(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
+                                 cudaStream_t st) {
+    return g_matvec_kernel.load() == 1 ? tq_launch_matvec(m, x, out, M, scr, st)
+                                       : tq_launch_igemv(m, x, out, M, scr, st);
+}
+
+static int ensure_stream(ThreadCtx *c) {
+    if (!c->stream) {
+        cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) return tq_cuda_fail(e, "stream create");
+    }
+    return TQ_OK;
+}
+
+static int grow_dev(float **p, size_t *cap, size_t floats) {
+    if (*cap >= floats) return TQ_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = tq_dev_malloc((void **)p, floats * sizeof(float));
+    if (e != cudaSuccess) return tq_cuda_fail(e, "device staging allocation");
+    *cap = floats;
+    return TQ_OK;
+}
+
+static int grow_host(float **p, size_t *cap, size_t floats) {
+    if (*cap >= floats) return TQ_OK;
+    if (*p) cudaFreeHost(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMallocHost((void **)p, floats * sizeof(float));
+    if (e != cudaSuccess) return tq_cuda_fail(e, "pinned staging allocation");
+    *cap = floats;
+    return TQ_OK;
+}
+
+static std::shared_ptr<Handle> lookup(uint64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_handles.find(h);
+    return it == g_handles.end() ? nullptr : it->second;
+}
+
+std::shared_ptr<Handle> tq_lookup_checked(uint64_t h, int *rc) {
+    auto p = lookup(h);
+    *rc = p ? TQ_OK : tq_fail(TQ_ERR_HANDLE, "tensai: invalid or freed matrix handle %llu", (unsigned long long)h);
+    return p;
+}
+
+static int check_dims(int bits, int rows, int cols) {
+    if (rows < 0 || cols < 0) return tq_fail(TQ_ERR_ARG, "tensai: negative matrix shape %dx%d", rows, cols);
+    if (bits == 4 && cols % 2 != 0)
+        return tq_fail(TQ_ERR_ARG, "tensai: quantize4 needs an even column count, got %d", cols);
+    if (tq_tiles(bits, cols) > TQ_MAX_TILES)
+        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: %d columns exceed the supported %d", cols,
+                       TQ_MAX_TILES * TQ_TILE_BYTES * (bits == 8 ? 1 : 2));
+    if ((long long)rows * tq_row_bytes(bits, cols) > (1ll << 40))
+        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: matrix %dx%d too large", rows, cols);
+    return TQ_OK;
+}
+
+// Allocates a device matrix on the calling thread's device and clears it on
+// stream st (ordered before whatever the caller enqueues next on st).
+static int alloc_matrix(int bits, int rows, int cols, TqMatrixDev *m, cudaStream_t st) {
+    std::memset(m, 0, sizeof *m);
+    m->bits = bits;
+    m->rows = rows;
+    m->cols = cols;
+    m->tiles = tq_tiles(bits, cols);
+    m->units = tq_units(rows);
+    const size_t cbytes = tq_code_bytes(bits, rows, cols);
+    const size_t sfloats = tq_scale_floats(bits, rows, cols);
+    cudaError_t e = tq_dev_malloc((void **)&m->codes, cbytes);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "code allocation");
+    e = tq_dev_malloc((void **)&m->scale, sfloats * sizeof(float));
+    if (e != cudaSuccess) {
+        cudaFree(m->codes);
+        m->codes = nullptr;
+        return tq_cuda_fail(e, "scale allocation");
+    }
+    if ((e = cudaMemsetAsync(m->codes, 0, cbytes, st)) != cudaSuccess ||
+        (e = cudaMemsetAsync(m->scale, 0, sfloats * sizeof(float), st)) != cudaSuccess) {
+        cudaFree(m->codes);
+        cudaFree(m->scale);
+        return tq_cuda_fail(e, "matrix clear");
+    }
+    return TQ_OK;
+}
+
+static void release_matrix(TqMatrixDev *m) {
+    if (m->codes) cudaFree(m->codes);
+    if (m->scale) cudaFree(m->scale);
+    m->codes = nullptr;
+    m->scale = nullptr;
+}
+
+static uint64_t register_handle(int device, const TqMatrixDev &m) {
+    auto h = std::make_shared<Handle>();
+    h->device = device;
+    h->m = m;
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint64_t id = g_next_handle++;
+    g_handles[id] = h;
+    return id;
+}
+
+// Host reference layout <-> tiled device layout: one copy into a temporary
+// device buffer in the reference layout, then a re-layout kernel (and the
+// reverse for downloads). Synchronous.
+static size_t ref_scale_floats(const TqMatrixDev &m) { return m.bits == 8 ? (size_t)m.cols : (size_t)m.units * m.cols; }
+
+static cudaError_t copy_in(const TqMatrixDev &m, const void *q, const float *scale) {
+    const size_t qb = (size_t)m.rows * tq_row_bytes(m.bits, m.cols), sf = ref_scale_floats(m);
+    if (qb == 0) return cudaSuccess;
+    uint8_t *tmp = nullptr;
+    cudaError_t e = tq_dev_malloc((void **)&tmp, qb + sf * sizeof(float) + 16);
+    if (e != cudaSuccess) return e;
+    float *tscale = reinterpret_cast<float *>(tmp + ((qb + 15) & ~(size_t)15));
+    e = cudaMemcpy(tmp, q, qb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(tscale, scale, sf * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = tq_launch_to_tiled(m, tmp, tscale, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    return e;
+}
+
+static cudaError_t copy_out(const TqMatrixDev &m, void *q, float *scale) {
+    const size_t qb = (size_t)m.rows * tq_row_bytes(m.bits, m.cols), sf = ref_scale_floats(m);
+    std::memset((uint8_t *)q + qb, 0, 16); // the reference's pad bytes
+    if (qb == 0) {
+        if (sf) std::memset(scale, 0, sf * sizeof(float));
+        return cudaSuccess;
+    }
+    uint8_t *tmp = nullptr;
+    cudaError_t e = tq_dev_malloc((void **)&tmp, qb + sf * sizeof(float) + 16);
+    if (e != cudaSuccess) return e;
+    float *tscale = reinterpret_cast<float *>(tmp + ((qb + 15) & ~(size_t)15));
+    e = tq_launch_from_tiled(m, tmp, tscale, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(q, tmp, qb, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(scale, tscale, sf * sizeof(float), cudaMemcpyDeviceToHost);
+    cudaFree(tmp);
+    return e;
+}
+
+static int set_thread_device() {
+    cudaError_t e = cudaSetDevice(t_device);
+    return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "set device");
+}
+
+extern "C" {
+
+int tq_version(void) { return TQ_ABI_VERSION; }
+
+const char *tq_last_error(void) { return t_err.c_str(); }
+
+int tq_device_count(int *n) {
+    if (!n) return tq_fail(TQ_ERR_ARG, "tensai: null output pointer");
+    cudaError_t e = cudaGetDeviceCount(n);
+    if (e != cudaSuccess) {
+        *n = 0;
+        return tq_cuda_fail(e, "device count");
+    }
+    return TQ_OK;
+}
+
+int tq_set_device(int device) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "device count");
+    if (device < 0 || device >= n) return tq_fail(TQ_ERR_ARG, "tensai: device %d out of range (have %d)", device, n);
+    cudaDeviceProp prop;
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return tq_cuda_fail(e, "device properties");
+    if (prop.major != 10)
+        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: device %d is sm_%d%d; this library is built for sm_100a", device,
+                       prop.major, prop.minor);
+    t_device = device;
+    return set_thread_device();
+}
+
+static int upload(int bits, const void *q, const float *scale, int rows, int cols, uint64_t *handle) {
+    if (!handle || (!q && rows && cols) || (!scale && cols)) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    int rc = check_dims(bits, rows, cols);
+    if (rc) return rc;
+    if ((rc = set_thread_device())) return rc;
+    TqMatrixDev m;
+    if ((rc = alloc_matrix(bits, rows, cols, &m, nullptr))) return rc;
+    cudaError_t e = copy_in(m, q, scale);
+    if (e != cudaSuccess) {
+        release_matrix(&m);
+        return tq_cuda_fail(e, "upload");
+    }
+    *handle = register_handle(t_device, m);
+    return TQ_OK;
+}
+
+int tq_q8_upload(const int8_t *q, const float *scale, int rows, int cols, uint64_t *handle) {
+    return upload(8, q, scale, rows, cols, handle);
+}
+
+int tq_q4_upload(const uint8_t *q, const float *scale, int rows, int cols, uint64_t *handle) {
+    return upload(4, q, scale, rows, cols, handle);
+}
+
+static int quantize_dev(int bits, const float *w, int rows, int cols, void *stream, uint64_t *handle) {
+    if (!handle || (!w && rows && cols)) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    int rc = check_dims(bits, rows, cols);
+    if (rc) return rc;
+    if ((rc = set_thread_device())) return rc;
+    TqMatrixDev m;
+    if ((rc = alloc_matrix(bits, rows, cols, &m, (cudaStream_t)stream))) return rc;
+    cudaError_t e = tq_launch_quantize(m, w, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        release_matrix(&m);
+        return tq_cuda_fail(e, "quantize launch");
+    }
+    *handle = register_handle(t_device, m);
+    return TQ_OK;
+}
+
+int tq_quantize8_dev(const float *w, int rows, int cols, void *stream, uint64_t *handle) {
+    return quantize_dev(8, w, rows, cols, stream, handle);
+}
+
+int tq_quantize4_dev(const float *w, int rows, int cols, void *stream, uint64_t *handle) {
+    return quantize_dev(4, w, rows, cols, stream, handle);
+}
+
+static int quantize_host(int bits, const float *w, int rows, int cols, void *q, float *scale) {
+    if (!q || !scale || (!w && rows && cols)) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    int rc = check_dims(bits, rows, cols);
+    if (rc) return rc;
+    if ((rc = set_thread_device())) return rc;
+    float *dw = nullptr;
+    cudaError_t e = tq_dev_malloc((void **)&dw, sizeof(float) * (size_t)rows * cols);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "weight staging allocation");
+    if (rows && cols) e = cudaMemcpy(dw, w, sizeof(float) * (size_t)rows * cols, cudaMemcpyHostToDevice);
+    uint64_t h = 0;
+    if (e == cudaSuccess) {
+        rc = quantize_dev(bits, dw, rows, cols, nullptr, &h);
+    } else {
+        rc = tq_cuda_fail(e, "weight upload");
+    }
+    if (rc == TQ_OK) {
+        auto p = lookup(h);
+        e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = copy_out(p->m, q, scale);
+        if (e != cudaSuccess) rc = tq_cuda_fail(e, "quantize");
+        tq_free(h);
+    }
+    cudaFree(dw);
+    return rc;
+}
+
+int tq_quantize8(const float *w, int rows, int cols, int8_t *q, float *scale) {
+    return quantize_host(8, w, rows, cols, q, scale);
+}
+
+int tq_quantize4(const float *w, int rows, int cols, uint8_t *q, float *scale) {
+    return quantize_host(4, w, rows, cols, q, scale);
+}
+
+int tq_matrix_info(uint64_t handle, int *bits, int *rows, int *cols) {
+    int rc;
+    auto p = tq_lookup_checked(handle, &rc);
+    if (!p) return rc;
+    if (bits) *bits = p->m.bits;
+    if (rows) *rows = p->m.rows;
+    if (cols) *cols = p->m.cols;
+    return TQ_OK;
+}
+
+int tq_download(uint64_t handle, void *q, float *scale) {
+    if (!q || !scale) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    int rc;
+    auto p = tq_lookup_checked(handle, &rc);
+    if (!p) return rc;
+    cudaError_t e = cudaSetDevice(p->device);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = copy_out(p->m, q, scale);
+    return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "download");
+}
+
+int tq_free(uint64_t handle) {
+    std::shared_ptr<Handle> p;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_handles.find(handle);
+        if (it == g_handles.end()) return TQ_OK;
+        p = it->second;
+        g_handles.erase(it);
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(p->device);
+    cudaDeviceSynchronize(); // no kernel of any stream may still read the codes
+    release_matrix(&p->m);
+    cudaSetDevice(prev);
+    return TQ_OK;
+}
+
+int tq_matmul_dev(uint64_t handle, const float *x, float *out, int m, void *stream) {
+    int rc;
+    auto p = tq_lookup_checked(handle, &rc);
+    if (!p) return rc;
+    if (m < 0) return tq_fail(TQ_ERR_ARG, "tensai: negative row count %d", m);
+    if (m && ((!x && p->m.rows) || (!out && p->m.cols))) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    cudaError_t e = cudaSetDevice(p->device);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "set device");
+    TqScratch scr;
+    if ((rc = scratch_for(p->device, (cudaStream_t)stream, &scr))) return rc;
+    e = launch_matvec(p->m, x, out, m, scr, (cudaStream_t)stream);
+    return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "matmul launch");
+}
+
+int tq_matmul(uint64_t handle, const float *x, float *out, int m) {
+    int rc;
+    auto p = tq_lookup_checked(handle, &rc);
+    if (!p) return rc;
+    if (m < 0) return tq_fail(TQ_ERR_ARG, "tensai: negative row count %d", m);
+    if (m == 0) return TQ_OK;
+    if ((!x && p->m.rows) || (!out && p->m.cols)) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    cudaError_t e = cudaSetDevice(p->device);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "set device");
+    ThreadCtx *c = ctx_for(p->device);
+    if ((rc = ensure_stream(c))) return rc;
+    const size_t nx = (size_t)m * p->m.rows, no = (size_t)m * p->m.cols;
+    if ((rc = grow_dev(&c->d_x, &c->d_x_cap, nx)) || (rc = grow_dev(&c->d_out, &c->d_out_cap, no)) ||
+        (rc = grow_host(&c->h_x, &c->h_x_cap, nx)) || (rc = grow_host(&c->h_out, &c->h_out_cap, no)))
+        return rc;
+    TqScratch scr;
+    if ((rc = scratch_for(p->device, c->stream, &scr))) return rc;
+    std::memcpy(c->h_x, x, nx * sizeof(float));
+    e = cudaMemcpyAsync(c->d_x, c->h_x, nx * sizeof(float), cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = launch_matvec(p->m, c->d_x, c->d_out, m, scr, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->h_out, c->d_out, no * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "matmul");
+    unsigned status = 0;
+    if ((e = read_status(scr, c->stream, &status)) != cudaSuccess) return tq_cuda_fail(e, "status read");
+    if (status & TQ_STATUS_TIMEOUT)
+        return tq_fail(TQ_ERR_TIMEOUT, "tensai: a kernel timed out waiting for its weight copies");
+    std::memcpy(out, c->h_out, no * sizeof(float));
+    return TQ_OK;
+}
+
+int tq_matvec(uint64_t handle, const float *x, size_t x_len, float *out, size_t out_len) {
+    int rc;
+    auto p = tq_lookup_checked(handle, &rc);
+    if (!p) return rc;
+    if (x_len != (size_t)p->m.rows || out_len != (size_t)p->m.cols)
+        return tq_fail(TQ_ERR_SHAPE, "tensai: %s shape mismatch: x=%zu out=%zu, want %dx%d",
+                       p->m.bits == 8 ? "qmatvec" : "q4matvec", x_len, out_len, p->m.rows, p->m.cols);
+    return tq_matmul(handle, x, out, 1);
+}
+
+int tq_synth_dev(float *out, size_t n, uint64_t seed, uint64_t stream_id, float sigma, void *cuda_stream) {
+    if (!out && n) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    cudaError_t e = tq_launch_synth(out, n, seed, stream_id, sigma, (cudaStream_t)cuda_stream);
+    return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "synth launch");
+}
+
+int tq_device_status(unsigned *bits) {
+    if (!bits) return tq_fail(TQ_ERR_ARG, "tensai: null output pointer");
+    *bits = 0;
+    cudaError_t e = cudaSetDevice(t_device);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return tq_cuda_fail(e, "device synchronize");
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    for (auto &kv : g_scratch) {
+        if (kv.first.first != t_device) continue;
+        if ((e = read_status(kv.second, kv.first.second, bits)) != cudaSuccess) return tq_cuda_fail(e, "status read");
+    }
+    return TQ_OK;
+}
+
+int tq_set_matvec_kernel(int which) {
+    if (which != 0 && which != 1) return tq_fail(TQ_ERR_ARG, "tensai: matvec kernel must be 0 or 1, got %d", which);
+    g_matvec_kernel.store(which);
+    return TQ_OK;
+}
+
+int tq_debug_fail_allocs(int n) {
+    g_fail_allocs.store(n < 0 ? 0 : n);
+    return TQ_OK;
+}
+
+} // extern "C"

@@ -1,0 +1,98 @@
+// tq_common.cuh — shared definitions for the tensai B200 library.
+//
+// Device layout of a quantized matrix (one per handle, resident in HBM).
+// rowBytes = cols (int8) or cols/2 (int4): the length of a row of the
+// reference's Q (quant.go:31, quant4.go:144). The matrix is cut into column
+// tiles of 128 bytes and units of 64 rows (an int4 unit is one scale group);
+// tiles = ceil(rowBytes/128), units = ceil(rows/64).
+//   codes : tiled. Item (t, u) = the 64 x 128 byte block of rows 64u.. and row
+//           bytes 128t.., stored contiguously at byte offset (t*units + u)*8192.
+//           Inside an item, row r occupies bytes [128r, 128r+128) with its
+//           sixteen 16-byte chunks permuted: chunk c sits at chunk position
+//           c ^ (r % 8). That is the tensor cores' 128-byte-swizzled,
+//           MN-major shared-memory operand layout, so an item copied verbatim
+//           into shared memory is a ready UMMA A operand (128 columns x 64 K).
+//           Padding rows and bytes are zero. Each item is one 8 KB contiguous
+//           read, and a run of consecutive items is one contiguous range of
+//           HBM.
+//   scale : int8 -> [tiles*128] floats, scale[j] = Scale[j] (quant.go:32).
+//           int4 -> per item 256 floats at (t*units + u)*256: [0,128) hold the
+//           reference's Scale[u*cols + 128t + c] (low-nibble columns) and
+//           [128,256) hold Scale[u*cols + cols/2 + 128t + c] (high-nibble
+//           columns), c < 128 (quant4.go:38, :56).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define TQ_GROUP 64        // rows per int4 scale group (q4Group, quant4.go:12)
+#define TQ_TILE_BYTES 128  // bytes of a code row per item
+#define TQ_ITEM_BYTES (TQ_TILE_BYTES * TQ_GROUP)
+#define TQ_MAX_TILES 8192  // rowBytes <= 1 MiB
+#define TQ_MAX_CTAS 256    // persistent matvec grid <= 256 CTAs
+#define TQ_STATUS_TIMEOUT 1u // a kernel gave up waiting on an mbarrier
+
+// Scratch for the matvec's cross-CTA tile reduction: partial sums of tiles
+// shared by several CTAs, and one arrival counter per column tile (zero at
+// rest; the last arriving CTA re-arms it). One scratch per stream.
+struct TqScratch {
+    float *partial;     // TQ_SCRATCH_PARTIAL_FLOATS
+    unsigned *counters; // TQ_MAX_TILES
+    unsigned *status;   // TQ_STATUS_* bits set by kernels on this stream
+    uint8_t *planes;    // TQ_SCRATCH_PLANES_BYTES: activation digit planes of a matvec
+};
+#define TQ_SCRATCH_PARTIAL_FLOATS ((size_t)2 * TQ_MAX_CTAS * 8 * 8 * 32)
+#define TQ_SCRATCH_PLANES_BYTES ((size_t)8 << 20) // 2304 B per 64 rows: K <= 233,000
+
+struct TqMatrixDev {
+    int bits;       // 8 or 4
+    int rows;       // K
+    int cols;       // N
+    int tiles;      // ceil(rowBytes/128)
+    int units;      // ceil(rows/64) (= scale groups for int4)
+    uint8_t *codes; // tiles*units*8192 bytes, tiled (see above)
+    float *scale;   // see above
+};
+
+#ifdef __CUDACC__
+#define TQ_HD __host__ __device__ __forceinline__
+#else
+#define TQ_HD inline
+#endif
+
+// Byte position of (row r, byte c) inside an item: 128-byte swizzle.
+TQ_HD int tq_item_offset(int r, int c) { return r * TQ_TILE_BYTES + ((((c >> 4) ^ (r & 7)) << 4) | (c & 15)); }
+// Byte b of code row i in the tiled layout.
+TQ_HD size_t tq_code_offset(int units, int i, int b) {
+    return ((size_t)(b / TQ_TILE_BYTES) * units + i / TQ_GROUP) * TQ_ITEM_BYTES +
+           tq_item_offset(i % TQ_GROUP, b % TQ_TILE_BYTES);
+}
+// int4 scale of group u, run hi (0 = low-nibble columns, 1 = high), column pair p.
+TQ_HD size_t tq_scale4_offset(int units, int u, int hi, int p) {
+    return ((size_t)(p / TQ_TILE_BYTES) * units + u) * (2 * TQ_TILE_BYTES) + hi * TQ_TILE_BYTES + (p % TQ_TILE_BYTES);
+}
+
+static inline int tq_row_bytes(int bits, int cols) { return bits == 8 ? cols : cols / 2; }
+static inline int tq_tiles(int bits, int cols) { return (tq_row_bytes(bits, cols) + TQ_TILE_BYTES - 1) / TQ_TILE_BYTES; }
+static inline int tq_units(int rows) { return (rows + TQ_GROUP - 1) / TQ_GROUP; }
+static inline size_t tq_code_bytes(int bits, int rows, int cols) {
+    return (size_t)tq_tiles(bits, cols) * tq_units(rows) * TQ_ITEM_BYTES;
+}
+static inline size_t tq_scale_floats(int bits, int rows, int cols) {
+    const size_t t = (size_t)tq_tiles(bits, cols);
+    return bits == 8 ? t * TQ_TILE_BYTES : t * tq_units(rows) * 2 * TQ_TILE_BYTES;
+}
+
+// Kernel launchers (defined in the .cu files). All return cudaError_t of the
+// launch; none synchronizes.
+cudaError_t tq_launch_synth(float *out, size_t n, uint64_t seed, uint64_t stream, float sigma, cudaStream_t st);
+cudaError_t tq_launch_quantize(const TqMatrixDev &m, const float *w, cudaStream_t st);
+// Reference layout (rows x rowBytes codes, reference Scale) <-> device layout,
+// both sides in device memory.
+cudaError_t tq_launch_to_tiled(const TqMatrixDev &m, const uint8_t *ref_q, const float *ref_scale, cudaStream_t st);
+cudaError_t tq_launch_from_tiled(const TqMatrixDev &m, uint8_t *ref_q, float *ref_scale, cudaStream_t st);
+cudaError_t tq_launch_matvec(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
+                             cudaStream_t st);
+cudaError_t tq_launch_igemv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
+                            cudaStream_t st);

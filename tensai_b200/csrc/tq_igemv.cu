@@ -1,0 +1,609 @@
+// tq_igemv.cu — weight-only int8 / int4 matvec (M <= 8 activation rows) on the
+// 5th-generation tensor cores with exact integer products.
+//
+// Computes out[m][j] = sum_i x[m][i] * W[i][j], the product of qmatvecCols
+// (quant_simd.go:12-48) and q4matvecCols (quant4_simd.go:17-57), without
+// dequantizing the weights:
+//
+//   * The codes are the UMMA A operand as stored: int8 codes are signed 8-bit
+//     integers already; int4 codes expand to unsigned bytes n = nibble
+//     (0..15) by one mask (low run) or shift+mask (high run), in place.
+//   * Per 64-row unit (an int4 scale group) and activation row m, x is scaled
+//     by a power of two 2^e_m (exact) so |x|/2^e < 64, and split into four
+//     signed 7-bit digits: x/2^e = b0 + b1/128 + b2/128^2 + b3/128^3 + r with
+//     |r| <= 2^-22. The digits are the UMMA B operand (N = 4M columns,
+//     padded to 16 or 32).
+//   * tcgen05.mma.kind::i8 forms D_p = sum_i code_i * b_p,i exactly in int32
+//     in tensor memory (128 weight columns x N, one MMA per 32 rows).
+//   * The epilogue rebuilds the unit's dot product in fp32:
+//       int8: v = 2^e * sum_p D_p 128^-p                  (acc += v)
+//       int4: v = 2^e * sum_p (D_p - 8 sum_i b_p,i) 128^-p (acc = fma(v, scale_g, acc))
+//     and int8 multiplies by the column scale at the end (quant.go:120).
+//   Only the digit truncation (<= 2^-22 of the unit's largest |x|) and the
+//   fp32 rebuild round, so the result is at least as accurate as the
+//   reference's fp32 accumulation.
+//
+// Two launches per call, chained with programmatic dependent launch:
+//   planes_kernel  one CTA per 64-row unit: the unit's digit planes in the
+//                  UMMA B layout plus its 2^e and digit sums, into scratch.
+//   igemv_kernel   starts streaming weights at once (they depend on nothing),
+//                  and waits for the planes (griddepcontrol.wait) only before
+//                  loading them, touching scratch or writing the output.
+// igemv schedule: one persistent CTA per SM takes an equal contiguous slice of
+// the tile-major item list (stream-K; an item = 128 code bytes x 64 rows =
+// 8 KB of contiguous, pre-swizzled HBM). Warp roles:
+//   warp 0     producer: per item one cp.async.bulk of the codes and one of
+//              the unit's planes block, into a ring of stages
+//   warp 1     owns the tensor memory; lane 0 issues the MMAs
+//   warps 2-3  int4 only: nibble -> byte expansion of the A operand
+//   warps 4-7  epilogue: tcgen05.ld of the accumulators, scale folding,
+//              per-tile output (tiles shared with other CTAs reduce through
+//              scratch partials; the last CTA to arrive adds them in CTA
+//              order, so results are bit-reproducible)
+// Every mbarrier wait is bounded (2 s); a timeout sets TQ_STATUS_TIMEOUT and a
+// CTA-wide abort flag that turns all later waits into no-ops, so a fault
+// ends the kernel instead of hanging it.
+#include <cuda.h>
+
+#include "tq_common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kItem = TQ_ITEM_BYTES; // 8192
+constexpr int kRows = TQ_GROUP;      // 64
+constexpr int kCols = TQ_TILE_BYTES; // 128
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+template <int M> struct Planes {
+    static constexpr int N = 4 * M <= 16 ? 16 : 32; // UMMA N: digit planes, padded
+    static constexpr int KSTEP_B = (N / 8) * 256;   // B bytes per 32-row MMA step
+    static constexpr int BBYTES = 2 * KSTEP_B;      // B bytes per unit
+    static constexpr int META = 256;                // 2^e[8] floats, then digit sums [8][4] ints
+    static constexpr int UB = BBYTES + META;        // planes block per unit (16-byte multiple)
+};
+
+template <int BITS, int M> struct Cfg {
+    using PL = Planes<M>;
+    static constexpr int N = PL::N;
+    static constexpr int KSTEP_B = PL::KSTEP_B;
+    static constexpr int UB = PL::UB;
+    static constexpr int ABYTES = BITS == 8 ? kItem : 2 * kItem; // s8/u8 A tiles per item
+    static constexpr int STAGES = BITS == 8 ? 8 : 4;
+    static constexpr int TCOLS = 128;                 // tensor memory columns allocated
+    static constexpr int ACC = BITS == 8 ? N : 2 * N; // accumulator columns per item
+    // shared memory (bytes; the A ring is 1024-aligned for the 128-byte swizzle)
+    static constexpr int P_OFF = 0;                                  // int4: packed codes ring
+    static constexpr int P_BYTES = BITS == 8 ? 0 : STAGES * kItem;
+    static constexpr int A_OFF = P_OFF + P_BYTES;                    // A operand ring
+    static constexpr int A_BYTES = STAGES * ABYTES;
+    static constexpr int B_OFF = A_OFF + A_BYTES;                    // planes blocks ring (B operand + meta)
+    static constexpr int B_BYTES = STAGES * UB;
+    static constexpr int BAR_OFF = (B_OFF + B_BYTES + 15) & ~15;     // mbarriers
+    static constexpr int NBARS = 3 * STAGES + 4;
+    static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;             // tmem base, flags
+    static constexpr int SMEM = MISC_OFF + 32 + 1024;                // + alignment slack
+    static_assert(ACC * 2 <= TCOLS, "two accumulator buffers must fit the allocation");
+};
+
+struct IgParams {
+    const uint8_t *codes;
+    const float *scale;
+    const uint8_t *planes; // [units][UB]
+    float *out;
+    float *partial;
+    unsigned *counters;
+    unsigned *status;
+    long long items;
+    int rows, cols, half, units, tiles;
+};
+
+// ---- PTX helpers ------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait on phase `parity`; on timeout (or if the CTA already aborted)
+// sets the abort flag and returns false.
+__device__ __noinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *status) {
+    if (*abort) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 64; i++)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (global_ns() - t0 > kWaitNs) {
+            atomicOr(status, TQ_STATUS_TIMEOUT);
+            *abort = 1;
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// UMMA shared-memory descriptor: start, leading/stride byte offsets, version 1
+// (sm_100), layout type (0 = no swizzle, 2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(dtmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 16 columns of 32-bit accumulators (this warp's lane quarter).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ long long item_start(long long items, int c, int ctas) { return items * c / ctas; }
+
+// Instruction descriptor of tcgen05.mma.kind::i8: D s32, A = codes (s8 for
+// int8, u8 for int4; MN-major), B = digits (s8, K-major), M = 128, N.
+template <int BITS, int N> __device__ __forceinline__ uint32_t idesc_i8() {
+    return (2u << 4) | ((BITS == 8 ? 1u : 0u) << 7) | (1u << 10) | (1u << 15) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(128 >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// planes_kernel: digit planes of x for one 64-row unit per CTA (64 threads,
+// thread t = row t of the unit). For activation row m: 2^e_m with
+// max_i |x_m,i| in [2^(e_m+5), 2^(e_m+6)), digits b_q of x/2^e_m (round to
+// nearest even, remainder times 128), written as B[n = 4m+q][k = t] in the
+// UMMA K-major no-swizzle layout: byte (n, k) of 32-row step j sits at
+// j*KSTEP_B + (n/8)*256 + (k%32/16)*128 + (n%8)*16 + k%16.
+// ---------------------------------------------------------------------------
+template <int M>
+__global__ void __launch_bounds__(64) planes_kernel(const float *__restrict__ x, int rows, uint8_t *__restrict__ planes) {
+    using PL = Planes<M>;
+    __shared__ float red_max[2][M];
+    __shared__ int red_sum[2][M][4];
+    pdl_trigger();
+    pdl_wait(); // x is produced by the previous kernel on the stream
+    const int u = blockIdx.x, t = threadIdx.x, w = t >> 5, lane = t & 31;
+    uint8_t *B = planes + (size_t)u * PL::UB;
+    float *meta = reinterpret_cast<float *>(B + PL::BBYTES);
+    const int row = u * kRows + t;
+    float v[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        v[m] = row < rows ? x[(size_t)m * rows + row] : 0.f;
+        float mx = fabsf(v[m]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) red_max[w][m] = mx;
+    }
+    __syncthreads();
+    const int kk = t & 31, j = t >> 5;
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        const float mx = fmaxf(red_max[0][m], red_max[1][m]);
+        int e = 0;
+        if (mx > 0.f) frexpf(mx, &e); // mx = f * 2^e, f in [0.5, 1)
+        float r = mx > 0.f ? ldexpf(v[m], 6 - e) : 0.f; // exact: |r| < 64
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float di = rintf(r);
+            const int d = (int)di;
+            r = (r - di) * 128.0f; // exact
+            const int n = m * 4 + q;
+            B[j * PL::KSTEP_B + (n >> 3) * 256 + (kk >> 4) * 128 + (n & 7) * 16 + (kk & 15)] = (uint8_t)(int8_t)d;
+            int sum = d;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) red_sum[w][m][q] = sum;
+        }
+        if (t == 0) meta[m] = mx > 0.f ? ldexpf(1.0f, e - 6) : 0.f;
+    }
+    __syncthreads();
+    if (t < 4 * M) {
+        const int m = t >> 2, q = t & 3;
+        reinterpret_cast<int *>(meta)[8 + m * 4 + q] = red_sum[0][m][q] + red_sum[1][m][q];
+    }
+}
+
+template <int BITS, int M>
+__global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
+    using C = Cfg<BITS, M>;
+    constexpr int S = C::STAGES, N = C::N;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *full = bars, *afull = bars + S, *empty = bars + 2 * S, *accfull = bars + 3 * S, *accempty = accfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
+    volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
+    int *lastflag = reinterpret_cast<int *>(smem + C::MISC_OFF + 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, c = blockIdx.x;
+    const long long i0 = item_start(p.items, c, G), i1 = item_start(p.items, c + 1, G);
+    const int nitems = (int)(i1 - i0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&afull[s], 1);
+            mbar_init(&empty[s], 2); // MMA completion + epilogue done with the stage's meta
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&accfull[b], 1);
+            mbar_init(&accempty[b], 1);
+        }
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(C::TCOLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            auto codes_dst = [&](int s) { return smem + (BITS == 8 ? C::A_OFF + s * C::ABYTES : C::P_OFF + s * kItem); };
+            auto planes_src = [&](int k) { return p.planes + (size_t)((i0 + k) % p.units) * C::UB; };
+            // The first S items' codes depend on nothing: stream them before the
+            // planes (written by the preceding kernel) are known to be ready.
+            const int pre = nitems < S ? nitems : S;
+            for (int k = 0; k < pre; k++) {
+                mbar_arrive_expect_tx(&full[k], kItem + C::UB);
+                bulk_load(codes_dst(k), p.codes + (i0 + k) * (long long)kItem, kItem, &full[k]);
+            }
+            pdl_wait();
+            for (int k = 0; k < pre; k++) bulk_load(smem + C::B_OFF + k * C::UB, planes_src(k), C::UB, &full[k]);
+            for (int k = pre; k < nitems; k++) {
+                const int s = k % S;
+                if (!wait_bar(&empty[s], ((k / S) & 1) ^ 1, abort, p.status)) continue;
+                mbar_arrive_expect_tx(&full[s], kItem + C::UB);
+                bulk_load(codes_dst(s), p.codes + (i0 + k) * (long long)kItem, kItem, &full[s]);
+                bulk_load(smem + C::B_OFF + s * C::UB, planes_src(k), C::UB, &full[s]);
+            }
+            pdl_trigger(); // every load is issued: the next kernel may start its prologue
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_i8<BITS, N>();
+            for (int k = 0; k < nitems; k++) {
+                const int s = k % S, b = k & 1;
+                const bool ok_a = BITS == 8 ? wait_bar(&full[s], (k / S) & 1, abort, p.status)
+                                            : wait_bar(&afull[s], (k / S) & 1, abort, p.status);
+                const bool ok_c = wait_bar(&accempty[b], ((k >> 1) & 1) ^ 1, abort, p.status);
+                if (!(ok_a && ok_c)) continue;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(smem + C::A_OFF + s * C::ABYTES);
+                const uint32_t b0 = smem_u32(smem + C::B_OFF + s * C::UB);
+                const uint32_t d0 = tbase + (uint32_t)(b * C::ACC);
+#pragma unroll
+                for (int j = 0; j < 2; j++) { // two 32-row K steps
+                    const uint64_t bd = umma_desc(b0 + j * C::KSTEP_B, 128, 256, 0);
+                    umma_i8(d0, umma_desc(a0 + j * 4096, kItem, 1024, 2), bd, idesc, j);
+                    if (BITS == 4) umma_i8(d0 + N, umma_desc(a0 + kItem + j * 4096, kItem, 1024, 2), bd, idesc, j);
+                }
+                umma_commit(&empty[s]);
+                umma_commit(&accfull[b]);
+            }
+        }
+    } else if (warp < 4) {
+        // ---------------- int4: nibbles -> bytes, position for position ----------------
+        if (BITS == 4) {
+            const int t = threadIdx.x - 64;
+            for (int k = 0; k < nitems; k++) {
+                const int s = k % S;
+                const bool ok = wait_bar(&full[s], (k / S) & 1, abort, p.status);
+                if (ok) {
+                    const uint4 *P = reinterpret_cast<const uint4 *>(smem + C::P_OFF + s * kItem);
+                    uint4 *Alo = reinterpret_cast<uint4 *>(smem + C::A_OFF + s * C::ABYTES);
+                    uint4 *Ahi = reinterpret_cast<uint4 *>(smem + C::A_OFF + s * C::ABYTES + kItem);
+#pragma unroll
+                    for (int q = t; q < kItem / 16; q += 64) {
+                        const uint4 w = P[q];
+                        Alo[q] = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+                        Ahi[q] = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu,
+                                            (w.z >> 4) & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
+                    }
+                }
+                fence_proxy_async(); // generic-proxy writes of A become visible to the tensor cores
+                named_sync(2, 64);
+                if (t == 0) mbar_arrive(&afull[s]);
+            }
+        }
+    } else {
+        // ---------------- epilogue (TMEM lanes 32*(warp%4) .. +31) ----------------
+        pdl_wait(); // scratch and the output may still be in use by the previous kernel
+        const int q4 = warp & 3;
+        const int col = q4 * 32 + lane; // tile column of this thread (int4: pair index in each run)
+        const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
+        float acc[2][M];
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int m = 0; m < M; m++) acc[h][m] = 0.f;
+        for (int k = 0; k < nitems; k++) {
+            const long long it = i0 + k;
+            const int tile = (int)(it / p.units);
+            const int s = k % S, b = k & 1;
+            float wlo = 1.f, whi = 1.f;
+            if (BITS == 4) {
+                wlo = __ldg(p.scale + it * (2 * kCols) + col);
+                whi = __ldg(p.scale + it * (2 * kCols) + kCols + col);
+            }
+            bool ok = wait_bar(&accfull[b], (k >> 1) & 1, abort, p.status);
+            // The stage's meta arrived with full[s]; the stage cannot be refilled
+            // before this warpgroup releases it below.
+            ok = wait_bar(&full[s], (k / S) & 1, abort, p.status) && ok;
+            ok = __all_sync(0xffffffffu, ok);
+            tc_fence_after();
+            const float *meta = reinterpret_cast<const float *>(smem + C::B_OFF + s * C::UB + Planes<M>::BBYTES);
+            float scl[M];
+            int bsum[M][4];
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                scl[m] = meta[m];
+#pragma unroll
+                for (int q = 0; q < 4; q++) bsum[m][q] = reinterpret_cast<const int *>(meta)[8 + m * 4 + q];
+            }
+            int dlo[N], dhi[N];
+            if (ok) {
+#pragma unroll
+                for (int c0 = 0; c0 < N; c0 += 16)
+                    tmem_ld16(lane_base + (uint32_t)(b * C::ACC + c0), *reinterpret_cast<int(*)[16]>(&dlo[c0]));
+                if (BITS == 4) {
+#pragma unroll
+                    for (int c0 = 0; c0 < N; c0 += 16)
+                        tmem_ld16(lane_base + (uint32_t)(b * C::ACC + N + c0), *reinterpret_cast<int(*)[16]>(&dhi[c0]));
+                }
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int n = 0; n < N; n++) dlo[n] = dhi[n] = 0;
+            }
+            tc_fence_before();
+            named_sync(1, 128);
+            if (threadIdx.x == 128) {
+                mbar_arrive(&accempty[b]);
+                mbar_arrive(&empty[s]);
+            }
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                float vlo, vhi;
+                if (BITS == 8) {
+                    vlo = (float)dlo[m * 4 + 3];
+                    vlo = fmaf(vlo, 0.0078125f, (float)dlo[m * 4 + 2]);
+                    vlo = fmaf(vlo, 0.0078125f, (float)dlo[m * 4 + 1]);
+                    vlo = fmaf(vlo, 0.0078125f, (float)dlo[m * 4 + 0]);
+                    acc[0][m] = fmaf(vlo, scl[m], acc[0][m]);
+                } else {
+                    vlo = (float)(dlo[m * 4 + 3] - 8 * bsum[m][3]);
+                    vhi = (float)(dhi[m * 4 + 3] - 8 * bsum[m][3]);
+#pragma unroll
+                    for (int q = 2; q >= 0; q--) {
+                        vlo = fmaf(vlo, 0.0078125f, (float)(dlo[m * 4 + q] - 8 * bsum[m][q]));
+                        vhi = fmaf(vhi, 0.0078125f, (float)(dhi[m * 4 + q] - 8 * bsum[m][q]));
+                    }
+                    acc[0][m] = fmaf(vlo * scl[m], wlo, acc[0][m]);
+                    acc[1][m] = fmaf(vhi * scl[m], whi, acc[1][m]);
+                }
+            }
+            // ---- tile segment end: write or reduce ----
+            const bool seg_end = (k + 1 == nitems) || ((it + 1) % p.units == 0);
+            if (seg_end) {
+                const long long t0 = (long long)tile * p.units, t1 = t0 + p.units;
+                int cf = (int)(t0 * G / p.items);
+                while (cf + 1 < G && item_start(p.items, cf + 1, G) <= t0) cf++;
+                while (cf > 0 && item_start(p.items, cf, G) > t0) cf--;
+                int cl = (int)((t1 - 1) * G / p.items);
+                while (cl + 1 < G && item_start(p.items, cl + 1, G) <= t1 - 1) cl++;
+                while (cl > 0 && item_start(p.items, cl, G) > t1 - 1) cl--;
+                constexpr int SL = (BITS == 8 ? 1 : 2) * M * kCols; // partial entries per tile
+                bool write = true;
+                if (cf != cl) {
+                    const int slot = 2 * c + (i0 >= t0 ? 0 : 1);
+                    float *dst = p.partial + (size_t)slot * SL;
+#pragma unroll
+                    for (int h = 0; h < (BITS == 8 ? 1 : 2); h++)
+#pragma unroll
+                        for (int m = 0; m < M; m++) dst[(h * M + m) * kCols + col] = acc[h][m];
+                    __threadfence();
+                    named_sync(1, 128);
+                    if (threadIdx.x == 128) {
+                        const unsigned prev = atomicAdd(&p.counters[tile], 1u);
+                        *lastflag = prev == (unsigned)(cl - cf);
+                        if (*lastflag) p.counters[tile] = 0;
+                    }
+                    named_sync(1, 128);
+                    write = *lastflag != 0;
+                    if (write) {
+                        __threadfence();
+#pragma unroll
+                        for (int h = 0; h < (BITS == 8 ? 1 : 2); h++)
+#pragma unroll
+                            for (int m = 0; m < M; m++) acc[h][m] = 0.f;
+                        for (int cc = cf; cc <= cl; cc++) {
+                            const int sl = 2 * cc + (item_start(p.items, cc, G) >= t0 ? 0 : 1);
+                            const float *src = p.partial + (size_t)sl * SL;
+#pragma unroll
+                            for (int h = 0; h < (BITS == 8 ? 1 : 2); h++)
+#pragma unroll
+                                for (int m = 0; m < M; m++) acc[h][m] += __ldcg(src + (h * M + m) * kCols + col);
+                        }
+                    }
+                    named_sync(1, 128); // lastflag is rewritten by the next shared tile
+                }
+                if (write) {
+                    const int base = tile * kCols + col; // byte index in the reference row
+                    if (BITS == 8) {
+                        if (base < p.cols) {
+                            const float sc = __ldg(p.scale + base);
+#pragma unroll
+                            for (int m = 0; m < M; m++) p.out[(size_t)m * p.cols + base] = acc[0][m] * sc;
+                        }
+                    } else if (base < p.half) {
+#pragma unroll
+                        for (int m = 0; m < M; m++) {
+                            p.out[(size_t)m * p.cols + base] = acc[0][m];
+                            p.out[(size_t)m * p.cols + p.half + base] = acc[1][m];
+                        }
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int m = 0; m < M; m++) acc[h][m] = 0.f;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(C::TCOLS) : "memory");
+    }
+}
+
+template <int BITS, int M>
+cudaError_t launch_ig(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st) {
+    using C = Cfg<BITS, M>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static int configured[64] = {};
+    static int sm_count[64] = {};
+    if (dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(igemv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        configured[dev] = 1;
+    }
+    IgParams prm;
+    prm.codes = mat.codes;
+    prm.scale = mat.scale;
+    prm.planes = scr.planes;
+    prm.out = out;
+    prm.partial = scr.partial;
+    prm.counters = scr.counters;
+    prm.status = scr.status;
+    prm.rows = mat.rows;
+    prm.cols = mat.cols;
+    prm.half = mat.cols / 2;
+    prm.units = mat.units;
+    prm.tiles = mat.tiles;
+    prm.items = (long long)mat.tiles * mat.units;
+    const int sms = sm_count[dev];
+    if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS) return cudaErrorInvalidValue;
+    const int ctas = (int)(prm.items < sms ? prm.items : sms);
+    if ((size_t)mat.units * C::UB > TQ_SCRATCH_PLANES_BYTES) return cudaErrorInvalidValue;
+    // Both launches may begin before their predecessor on the stream ends
+    // (programmatic dependent launch); each waits on griddepcontrol.wait
+    // before touching data the predecessor produces.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(mat.units);
+    cfg.blockDim = dim3(64);
+    e = cudaLaunchKernelEx(&cfg, planes_kernel<M>, x, mat.rows, scr.planes);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    return cudaLaunchKernelEx(&cfg, igemv_kernel<BITS, M>, prm);
+}
+
+template <int BITS>
+cudaError_t ig_dispatch(const TqMatrixDev &mat, const float *x, float *out, int M, const TqScratch &scr,
+                        cudaStream_t st) {
+    switch (M) {
+    case 1: return launch_ig<BITS, 1>(mat, x, out, scr, st);
+    case 2: return launch_ig<BITS, 2>(mat, x, out, scr, st);
+    case 3: return launch_ig<BITS, 3>(mat, x, out, scr, st);
+    case 4: return launch_ig<BITS, 4>(mat, x, out, scr, st);
+    case 5: return launch_ig<BITS, 5>(mat, x, out, scr, st);
+    case 6: return launch_ig<BITS, 6>(mat, x, out, scr, st);
+    case 7: return launch_ig<BITS, 7>(mat, x, out, scr, st);
+    default: return launch_ig<BITS, 8>(mat, x, out, scr, st);
+    }
+}
+
+} // namespace
+
+// Tensor-core matvec for up to 8 activation rows (larger M in 8-row launches).
+cudaError_t tq_launch_igemv(const TqMatrixDev &mat, const float *x, float *out, int M, const TqScratch &scr,
+                            cudaStream_t st) {
+    if (M <= 0 || mat.cols == 0) return cudaSuccess;
+    if (mat.rows == 0) return cudaMemsetAsync(out, 0, sizeof(float) * (size_t)M * mat.cols, st);
+    for (int m0 = 0; m0 < M; m0 += 8) {
+        const int mm = M - m0 < 8 ? M - m0 : 8;
+        const float *xm = x + (size_t)m0 * mat.rows;
+        float *om = out + (size_t)m0 * mat.cols;
+        cudaError_t e =
+            mat.bits == 8 ? ig_dispatch<8>(mat, xm, om, mm, scr, st) : ig_dispatch<4>(mat, xm, om, mm, scr, st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
