@@ -15,7 +15,7 @@
 //     padded to 16 or 32).
 //   * tcgen05.mma.kind::i8 forms D_p = sum_i code_i * b_p,i exactly in int32
 //     in tensor memory (128 weight columns x N, one MMA per 32 rows).
-//   * The epilogue rebuilds the unit's dot product in fp32:
+//   * The epilogue rebuilds each unit's dot product in fp32:
 //       int8: v = 2^e * sum_p D_p 128^-p                  (acc += v)
 //       int4: v = 2^e * sum_p (D_p - 8 sum_i b_p,i) 128^-p (acc = fma(v, scale_g, acc))
 //     and int8 multiplies by the column scale at the end (quant.go:120).
@@ -29,17 +29,25 @@
 //   igemv_kernel   starts streaming weights at once (they depend on nothing),
 //                  and waits for the planes (griddepcontrol.wait) only before
 //                  loading them, touching scratch or writing the output.
-// igemv schedule: one persistent CTA per SM takes an equal contiguous slice of
-// the tile-major item list (stream-K; an item = 128 code bytes x 64 rows =
-// 8 KB of contiguous, pre-swizzled HBM). Warp roles:
-//   warp 0     producer: per item one cp.async.bulk of the codes and one of
-//              the unit's planes block, into a ring of stages
-//   warp 1     owns the tensor memory; lane 0 issues the MMAs
-//   warps 2-3  int4 only: nibble -> byte expansion of the A operand
-//   warps 4-7  epilogue: tcgen05.ld of the accumulators, scale folding,
-//              per-tile output (tiles shared with other CTAs reduce through
-//              scratch partials; the last CTA to arrive adds them in CTA
-//              order, so results are bit-reproducible)
+//
+// igemv schedule. The codes sit in HBM as 8 KB items (128 code bytes x 64
+// rows), tile-major. One persistent CTA per SM takes an equal contiguous
+// slice of the item list (stream-K, balanced to +-1 item). The slice is walked
+// as batches of up to NU consecutive units of one column tile (contiguous in
+// HBM): one bulk copy of the codes and one of the B planes per batch, one
+// MMA-issuer wait and one commit per batch, so the tensor-core control cost is
+// amortized over 8 MMAs. Warp roles (14 warps):
+//   warp 0      producer: bulk copies into a ring of code stages
+//   warp 1      owns the tensor memory; lane 0 issues the MMAs
+//   warps 2-5   int4 only: nibble -> byte expansion into operand stages
+//   warps 6-13  epilogue, two warpgroups taking alternate batches: tcgen05.ld
+//               of the accumulators, scale folding, per-tile output. Tiles
+//               shared with other CTAs reduce through scratch partials; the
+//               last CTA to arrive adds them in CTA order, so results are
+//               bit-reproducible.
+// One commit per batch lands on done[b % DR]; the producer (stage reuse), the
+// expansion warps (operand-stage reuse) and the epilogue (accumulators ready)
+// all wait on it for their own batch index.
 // Every mbarrier wait is bounded (2 s); a timeout sets TQ_STATUS_TIMEOUT and a
 // CTA-wide abort flag that turns all later waits into no-ops, so a fault
 // ends the kernel instead of hanging it.
@@ -49,47 +57,64 @@
 
 namespace {
 
-constexpr int kThreads = 256;
 constexpr int kItem = TQ_ITEM_BYTES; // 8192
 constexpr int kRows = TQ_GROUP;      // 64
 constexpr int kCols = TQ_TILE_BYTES; // 128
+constexpr int kExpWarps = 4;         // warps 2..5
+constexpr int kEpiWarp0 = 2 + kExpWarps;
+constexpr int kEpiThreads = 128; // one epilogue warpgroup
+constexpr int kThreads = (kEpiWarp0 + 8) * 32;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
+// Planes buffer of one call: B blocks [units][BBYTES], then meta [units][MB]
+// (2^e per row m, then the four digit sums per row m, as ints).
 template <int M> struct Planes {
-    static constexpr int N = 4 * M <= 16 ? 16 : 32; // UMMA N: digit planes, padded
-    static constexpr int KSTEP_B = (N / 8) * 256;   // B bytes per 32-row MMA step
-    static constexpr int BBYTES = 2 * KSTEP_B;      // B bytes per unit
-    static constexpr int META = 256;                // 2^e[8] floats, then digit sums [8][4] ints
-    static constexpr int UB = BBYTES + META;        // planes block per unit (16-byte multiple)
+    static constexpr int N = 4 * M <= 16 ? 16 : 32;    // UMMA N: digit planes, padded
+    static constexpr int KSTEP_B = (N / 8) * 256;      // B bytes per 32-row MMA step
+    static constexpr int BBYTES = 2 * KSTEP_B;         // B bytes per unit
+    static constexpr int MB = (M * 20 + 15) / 16 * 16; // meta bytes per unit
 };
 
 template <int BITS, int M> struct Cfg {
     using PL = Planes<M>;
     static constexpr int N = PL::N;
     static constexpr int KSTEP_B = PL::KSTEP_B;
-    static constexpr int UB = PL::UB;
-    static constexpr int ABYTES = BITS == 8 ? kItem : 2 * kItem; // s8/u8 A tiles per item
-    static constexpr int STAGES = BITS == 8 ? 8 : 4;
-    static constexpr int TCOLS = 128;                 // tensor memory columns allocated
-    static constexpr int ACC = BITS == 8 ? N : 2 * N; // accumulator columns per item
-    // shared memory (bytes; the A ring is 1024-aligned for the 128-byte swizzle)
-    static constexpr int P_OFF = 0;                                  // int4: packed codes ring
-    static constexpr int P_BYTES = BITS == 8 ? 0 : STAGES * kItem;
-    static constexpr int A_OFF = P_OFF + P_BYTES;                    // A operand ring
-    static constexpr int A_BYTES = STAGES * ABYTES;
-    static constexpr int B_OFF = A_OFF + A_BYTES;                    // planes blocks ring (B operand + meta)
-    static constexpr int B_BYTES = STAGES * UB;
-    static constexpr int BAR_OFF = (B_OFF + B_BYTES + 15) & ~15;     // mbarriers
-    static constexpr int NBARS = 3 * STAGES + 4;
-    static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;             // tmem base, flags
-    static constexpr int SMEM = MISC_OFF + 32 + 1024;                // + alignment slack
-    static_assert(ACC * 2 <= TCOLS, "two accumulator buffers must fit the allocation");
+    static constexpr int BB = PL::BBYTES;
+    static constexpr int NU = BITS == 8 ? 4 : 2;    // units per batch
+    static constexpr int H = BITS == 8 ? 1 : 2;     // column runs per unit (int4: low, high nibbles)
+    static constexpr int ACC = H * N;               // accumulator columns per unit
+    static constexpr int BACC = NU * ACC;           // per batch
+    static constexpr int NBUF = 4 * BACC <= 512 ? 4 : 2; // accumulator buffers
+    static constexpr int TCOLS = NBUF * BACC <= 128 ? 128 : (NBUF * BACC <= 256 ? 256 : 512);
+    // code stage    [codes NU x 8 KB | B planes NU x BB]; int8: the codes are the A operand.
+    // operand stage [NU x (A lo 8 KB | A hi 8 KB)] (int4 only).
+    static constexpr int CSTRIDE = (NU * (kItem + BB) + 1023) & ~1023;
+    static constexpr int OSTRIDE = NU * 2 * kItem;
+    static constexpr int OST = BITS == 8 ? 0 : 2;
+    static constexpr int RED_BYTES = 2 * M * kCols * 4;   // warpgroup 1 -> 0 partial sums
+    static constexpr int MSLOTS = 6;                      // prefetched meta batches per warpgroup
+    static constexpr int META_BYTES = 2 * MSLOTS * NU * PL::MB;
+    static constexpr int FIXED = RED_BYTES + META_BYTES + 512 + 1024;
+    static constexpr int BUDGET = 227 * 1024 - FIXED - OST * OSTRIDE;
+    static constexpr int CST = BUDGET / CSTRIDE < 12 ? BUDGET / CSTRIDE : 12; // code stages
+    static constexpr int DR = (CST > NBUF ? CST : NBUF) + 2;                  // done-barrier ring
+    static constexpr int O_OFF = 0;
+    static constexpr int C_OFF = OST * OSTRIDE;
+    static constexpr int RED_OFF = C_OFF + CST * CSTRIDE;
+    static constexpr int META_OFF = RED_OFF + RED_BYTES;
+    static constexpr int BAR_OFF = (META_OFF + META_BYTES + 15) & ~15;
+    static constexpr int NBARS = CST + OST + DR + NBUF;
+    static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+    static constexpr int SMEM = MISC_OFF + 32 + 1024;
+    static_assert(NBUF * BACC <= TCOLS && TCOLS <= 512, "accumulators must fit tensor memory");
+    static_assert(CST >= 4, "too few code stages");
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
 struct IgParams {
     const uint8_t *codes;
     const float *scale;
-    const uint8_t *planes; // [units][UB]
+    const uint8_t *planes; // B blocks [units][BB], then meta [units][MB]
     float *out;
     float *partial;
     unsigned *counters;
@@ -143,6 +168,10 @@ __device__ __noinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile i
             return false;
         }
     }
+}
+// Fast path inline (phase already complete), bounded slow path out of line.
+__device__ __forceinline__ bool wait_fast(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *status) {
+    return mbar_try_wait(bar, parity) || wait_bar(bar, parity, abort, status);
 }
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(
@@ -206,15 +235,16 @@ template <int BITS, int N> __device__ __forceinline__ uint32_t idesc_i8() {
 // j*KSTEP_B + (n/8)*256 + (k%32/16)*128 + (n%8)*16 + k%16.
 // ---------------------------------------------------------------------------
 template <int M>
-__global__ void __launch_bounds__(64) planes_kernel(const float *__restrict__ x, int rows, uint8_t *__restrict__ planes) {
+__global__ void __launch_bounds__(64) planes_kernel(const float *__restrict__ x, int rows, int units,
+                                                   uint8_t *__restrict__ planes) {
     using PL = Planes<M>;
     __shared__ float red_max[2][M];
     __shared__ int red_sum[2][M][4];
     pdl_trigger();
     pdl_wait(); // x is produced by the previous kernel on the stream
     const int u = blockIdx.x, t = threadIdx.x, w = t >> 5, lane = t & 31;
-    uint8_t *B = planes + (size_t)u * PL::UB;
-    float *meta = reinterpret_cast<float *>(B + PL::BBYTES);
+    uint8_t *B = planes + (size_t)u * PL::BBYTES;
+    float *meta = reinterpret_cast<float *>(planes + (size_t)units * PL::BBYTES + (size_t)u * PL::MB);
     const int row = u * kRows + t;
     float v[M];
 #pragma unroll
@@ -250,37 +280,69 @@ __global__ void __launch_bounds__(64) planes_kernel(const float *__restrict__ x,
     __syncthreads();
     if (t < 4 * M) {
         const int m = t >> 2, q = t & 3;
-        reinterpret_cast<int *>(meta)[8 + m * 4 + q] = red_sum[0][m][q] + red_sum[1][m][q];
+        reinterpret_cast<int *>(meta)[M + m * 4 + q] = red_sum[0][m][q] + red_sum[1][m][q];
     }
 }
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// The batch sequence of one CTA: up to NU consecutive units of one tile.
+struct BatchWalk {
+    int tile, unit, left, units;
+    __device__ __forceinline__ int next(int NU) { // units in the next batch (0 = done)
+        int n = units - unit;
+        if (n > NU) n = NU;
+        if (n > left) n = left;
+        return n;
+    }
+    __device__ __forceinline__ bool advance(int n) { // true if the tile segment ended
+        unit += n;
+        left -= n;
+        if (unit == units) {
+            unit = 0;
+            tile++;
+            return true;
+        }
+        return left == 0;
+    }
+};
 
 template <int BITS, int M>
 __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
     using C = Cfg<BITS, M>;
-    constexpr int S = C::STAGES, N = C::N;
+    using PL = Planes<M>;
+    constexpr int CS = C::CST, OS = C::OST, DR = C::DR, NB = C::NBUF, NU = C::NU, H = C::H, N = C::N;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
-    uint64_t *full = bars, *afull = bars + S, *empty = bars + 2 * S, *accfull = bars + 3 * S, *accempty = accfull + 2;
+    uint64_t *cfull = bars, *ofull = bars + CS, *done = ofull + OS, *accempty = done + DR;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::MISC_OFF);
     volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4);
-    int *lastflag = reinterpret_cast<int *>(smem + C::MISC_OFF + 8);
+    volatile int *lastflag = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 8);
+    auto cstage = [&](int k) { return smem + C::C_OFF + (k % CS) * C::CSTRIDE; };
+    auto ostage = [&](int k) { return smem + C::O_OFF + (k % (OS ? OS : 1)) * C::OSTRIDE; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, c = blockIdx.x;
     const long long i0 = item_start(p.items, c, G), i1 = item_start(p.items, c + 1, G);
-    const int nitems = (int)(i1 - i0);
+    const BatchWalk walk0{(int)(i0 / p.units), (int)(i0 % p.units), (int)(i1 - i0), p.units};
+    int nbatches = 0;
+    {
+        BatchWalk w = walk0;
+        for (int n; (n = w.next(NU)) > 0; w.advance(n)) nbatches++;
+    }
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&afull[s], 1);
-            mbar_init(&empty[s], 2); // MMA completion + epilogue done with the stage's meta
-        }
-        for (int b = 0; b < 2; b++) {
-            mbar_init(&accfull[b], 1);
-            mbar_init(&accempty[b], 1);
-        }
+        for (int s = 0; s < CS; s++) mbar_init(&cfull[s], 1);
+        for (int s = 0; s < OS; s++) mbar_init(&ofull[s], 1);
+        for (int s = 0; s < DR; s++) mbar_init(&done[s], 1);
+        for (int b = 0; b < NB; b++) mbar_init(&accempty[b], 1);
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -298,23 +360,33 @@ __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
     if (warp == 0) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            auto codes_dst = [&](int s) { return smem + (BITS == 8 ? C::A_OFF + s * C::ABYTES : C::P_OFF + s * kItem); };
-            auto planes_src = [&](int k) { return p.planes + (size_t)((i0 + k) % p.units) * C::UB; };
-            // The first S items' codes depend on nothing: stream them before the
-            // planes (written by the preceding kernel) are known to be ready.
-            const int pre = nitems < S ? nitems : S;
+            // The first CS batches' codes depend on nothing: stream them before
+            // the planes (written by the preceding kernel) are known to be ready.
+            BatchWalk w = walk0;
+            const int pre = nbatches < CS ? nbatches : CS;
             for (int k = 0; k < pre; k++) {
-                mbar_arrive_expect_tx(&full[k], kItem + C::UB);
-                bulk_load(codes_dst(k), p.codes + (i0 + k) * (long long)kItem, kItem, &full[k]);
+                const int n = w.next(NU);
+                const long long it = (long long)w.tile * p.units + w.unit;
+                mbar_arrive_expect_tx(&cfull[k], n * (kItem + C::BB));
+                bulk_load(cstage(k), p.codes + it * kItem, n * kItem, &cfull[k]);
+                w.advance(n);
             }
             pdl_wait();
-            for (int k = 0; k < pre; k++) bulk_load(smem + C::B_OFF + k * C::UB, planes_src(k), C::UB, &full[k]);
-            for (int k = pre; k < nitems; k++) {
-                const int s = k % S;
-                if (!wait_bar(&empty[s], ((k / S) & 1) ^ 1, abort, p.status)) continue;
-                mbar_arrive_expect_tx(&full[s], kItem + C::UB);
-                bulk_load(codes_dst(s), p.codes + (i0 + k) * (long long)kItem, kItem, &full[s]);
-                bulk_load(smem + C::B_OFF + s * C::UB, planes_src(k), C::UB, &full[s]);
+            w = walk0;
+            for (int k = 0; k < nbatches; k++) {
+                const int n = w.next(NU);
+                const long long it = (long long)w.tile * p.units + w.unit;
+                if (k >= pre) {
+                    // stage k % CS last held batch k - CS
+                    if (!wait_fast(&done[(k - CS) % DR], ((k - CS) / DR) & 1, abort, p.status)) {
+                        w.advance(n);
+                        continue;
+                    }
+                    mbar_arrive_expect_tx(&cfull[k % CS], n * (kItem + C::BB));
+                    bulk_load(cstage(k), p.codes + it * kItem, n * kItem, &cfull[k % CS]);
+                }
+                bulk_load(cstage(k) + NU * kItem, p.planes + (size_t)w.unit * C::BB, n * C::BB, &cfull[k % CS]);
+                w.advance(n);
             }
             pdl_trigger(); // every load is issued: the next kernel may start its prologue
         }
@@ -322,130 +394,188 @@ __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = idesc_i8<BITS, N>();
-            for (int k = 0; k < nitems; k++) {
-                const int s = k % S, b = k & 1;
-                const bool ok_a = BITS == 8 ? wait_bar(&full[s], (k / S) & 1, abort, p.status)
-                                            : wait_bar(&afull[s], (k / S) & 1, abort, p.status);
-                const bool ok_c = wait_bar(&accempty[b], ((k >> 1) & 1) ^ 1, abort, p.status);
+            BatchWalk w = walk0;
+            for (int k = 0; k < nbatches; k++) {
+                const int n = w.next(NU);
+                w.advance(n);
+                const int buf = k % NB;
+                const bool ok_a = BITS == 8 ? wait_fast(&cfull[k % CS], (k / CS) & 1, abort, p.status)
+                                            : wait_fast(&ofull[k % (OS ? OS : 1)], (k / (OS ? OS : 1)) & 1, abort, p.status);
+                const bool ok_c = wait_fast(&accempty[buf], ((k / NB) & 1) ^ 1, abort, p.status);
                 if (!(ok_a && ok_c)) continue;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(smem + C::A_OFF + s * C::ABYTES);
-                const uint32_t b0 = smem_u32(smem + C::B_OFF + s * C::UB);
-                const uint32_t d0 = tbase + (uint32_t)(b * C::ACC);
+                const uint32_t asb = smem_u32(BITS == 8 ? cstage(k) : ostage(k));
+                const uint32_t bsb = smem_u32(cstage(k) + NU * kItem);
+                const uint32_t d0 = tbase + (uint32_t)(buf * C::BACC);
+                for (int j = 0; j < n; j++) {
 #pragma unroll
-                for (int j = 0; j < 2; j++) { // two 32-row K steps
-                    const uint64_t bd = umma_desc(b0 + j * C::KSTEP_B, 128, 256, 0);
-                    umma_i8(d0, umma_desc(a0 + j * 4096, kItem, 1024, 2), bd, idesc, j);
-                    if (BITS == 4) umma_i8(d0 + N, umma_desc(a0 + kItem + j * 4096, kItem, 1024, 2), bd, idesc, j);
-                }
-                umma_commit(&empty[s]);
-                umma_commit(&accfull[b]);
-            }
-        }
-    } else if (warp < 4) {
-        // ---------------- int4: nibbles -> bytes, position for position ----------------
-        if (BITS == 4) {
-            const int t = threadIdx.x - 64;
-            for (int k = 0; k < nitems; k++) {
-                const int s = k % S;
-                const bool ok = wait_bar(&full[s], (k / S) & 1, abort, p.status);
-                if (ok) {
-                    const uint4 *P = reinterpret_cast<const uint4 *>(smem + C::P_OFF + s * kItem);
-                    uint4 *Alo = reinterpret_cast<uint4 *>(smem + C::A_OFF + s * C::ABYTES);
-                    uint4 *Ahi = reinterpret_cast<uint4 *>(smem + C::A_OFF + s * C::ABYTES + kItem);
+                    for (int ks = 0; ks < 2; ks++) { // two 32-row K steps per unit
+                        const uint64_t bd = umma_desc(bsb + j * C::BB + ks * C::KSTEP_B, 128, 256, 0);
 #pragma unroll
-                    for (int q = t; q < kItem / 16; q += 64) {
-                        const uint4 w = P[q];
-                        Alo[q] = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
-                        Ahi[q] = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu,
-                                            (w.z >> 4) & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
+                        for (int h = 0; h < H; h++)
+                            umma_i8(d0 + j * C::ACC + h * N,
+                                    umma_desc(asb + (j * H + h) * kItem + ks * 4096, kItem, 1024, 2), bd, idesc, ks);
                     }
                 }
-                fence_proxy_async(); // generic-proxy writes of A become visible to the tensor cores
-                named_sync(2, 64);
-                if (t == 0) mbar_arrive(&afull[s]);
+                umma_commit(&done[k % DR]);
+            }
+        }
+    } else if (warp < kEpiWarp0) {
+        // ---------------- int4: nibbles -> bytes (position for position) ----------------
+        if (BITS == 4) {
+            const int t = threadIdx.x - 64;
+            constexpr int NT = kExpWarps * 32;
+            BatchWalk w = walk0;
+            for (int k = 0; k < nbatches; k++) {
+                const int n = w.next(NU);
+                w.advance(n);
+                bool ok = wait_fast(&cfull[k % CS], (k / CS) & 1, abort, p.status);
+                if (k >= OS) ok = wait_fast(&done[(k - OS) % DR], ((k - OS) / DR) & 1, abort, p.status) && ok;
+                if (ok) {
+                    const uint4 *P = reinterpret_cast<const uint4 *>(cstage(k));
+                    uint4 *A = reinterpret_cast<uint4 *>(ostage(k));
+                    for (int j = 0; j < n; j++) {
+#pragma unroll
+                        for (int q = t; q < kItem / 16; q += NT) {
+                            const uint4 v = P[j * (kItem / 16) + q];
+                            A[(2 * j) * (kItem / 16) + q] =
+                                make_uint4(v.x & 0x0F0F0F0Fu, v.y & 0x0F0F0F0Fu, v.z & 0x0F0F0F0Fu, v.w & 0x0F0F0F0Fu);
+                            A[(2 * j + 1) * (kItem / 16) + q] =
+                                make_uint4((v.x >> 4) & 0x0F0F0F0Fu, (v.y >> 4) & 0x0F0F0F0Fu, (v.z >> 4) & 0x0F0F0F0Fu,
+                                           (v.w >> 4) & 0x0F0F0F0Fu);
+                        }
+                    }
+                }
+                fence_proxy_async(); // generic-proxy writes become visible to the tensor cores
+                named_sync(1, NT);
+                if (t == 0) mbar_arrive(&ofull[k % (OS ? OS : 1)]);
             }
         }
     } else {
-        // ---------------- epilogue (TMEM lanes 32*(warp%4) .. +31) ----------------
-        pdl_wait(); // scratch and the output may still be in use by the previous kernel
+        // ---------------- epilogue: two warpgroups take alternate batches ----------------
+        // Warp w reads TMEM lanes 32*(w%4)..+31, i.e. tile columns of that range.
+        pdl_wait(); // planes, scratch and the output belong to the previous kernel until here
+        const int g = (warp - kEpiWarp0) >> 2;
         const int q4 = warp & 3;
         const int col = q4 * 32 + lane; // tile column of this thread (int4: pair index in each run)
+        const int et = threadIdx.x - kEpiWarp0 * 32 - g * kEpiThreads; // 0..127 within the warpgroup
         const uint32_t lane_base = tbase + ((uint32_t)(q4 * 32) << 16);
-        float acc[2][M];
-#pragma unroll
-        for (int h = 0; h < 2; h++)
-#pragma unroll
-            for (int m = 0; m < M; m++) acc[h][m] = 0.f;
-        for (int k = 0; k < nitems; k++) {
-            const long long it = i0 + k;
-            const int tile = (int)(it / p.units);
-            const int s = k % S, b = k & 1;
-            float wlo = 1.f, whi = 1.f;
-            if (BITS == 4) {
-                wlo = __ldg(p.scale + it * (2 * kCols) + col);
-                whi = __ldg(p.scale + it * (2 * kCols) + kCols + col);
+        float *red = reinterpret_cast<float *>(smem + C::RED_OFF); // [H][M][128] from warpgroup 1
+        uint8_t *mring = smem + C::META_OFF + g * C::MSLOTS * NU * PL::MB;
+        const uint8_t *meta_g = p.planes + (size_t)p.units * PL::BBYTES;
+        // Meta prefetch: this warpgroup's j-th batch is batch 2j + g; cp.async
+        // one group per batch, MSLOTS - 2 batches ahead.
+        constexpr int PD = C::MSLOTS - 2;
+        BatchWalk pw = walk0; // prefetch walker: positioned at batch index pk
+        int pk = 0;
+        auto skip_to_mine = [&]() {
+            while (pk < nbatches && (pk & 1) != g) {
+                pw.advance(pw.next(NU));
+                pk++;
             }
-            bool ok = wait_bar(&accfull[b], (k >> 1) & 1, abort, p.status);
-            // The stage's meta arrived with full[s]; the stage cannot be refilled
-            // before this warpgroup releases it below.
-            ok = wait_bar(&full[s], (k / S) & 1, abort, p.status) && ok;
-            ok = __all_sync(0xffffffffu, ok);
-            tc_fence_after();
-            const float *meta = reinterpret_cast<const float *>(smem + C::B_OFF + s * C::UB + Planes<M>::BBYTES);
-            float scl[M];
-            int bsum[M][4];
-#pragma unroll
-            for (int m = 0; m < M; m++) {
-                scl[m] = meta[m];
-#pragma unroll
-                for (int q = 0; q < 4; q++) bsum[m][q] = reinterpret_cast<const int *>(meta)[8 + m * 4 + q];
+        };
+        auto prefetch = [&]() {
+            skip_to_mine();
+            if (pk < nbatches) {
+                const int n = pw.next(NU);
+                const int slot = (pk >> 1) % C::MSLOTS;
+                for (int q = et; q < n * PL::MB / 16; q += kEpiThreads)
+                    cp_async16(mring + slot * NU * PL::MB + q * 16, meta_g + (size_t)pw.unit * PL::MB + q * 16);
+                pw.advance(n);
+                pk++;
             }
-            int dlo[N], dhi[N];
-            if (ok) {
+            cp_async_commit();
+        };
+        for (int i = 0; i < PD; i++) prefetch();
+
+        BatchWalk w = walk0;
+        int k = 0;
+        while (k < nbatches) {
+            const int tile = w.tile;
+            float acc[H][M];
 #pragma unroll
-                for (int c0 = 0; c0 < N; c0 += 16)
-                    tmem_ld16(lane_base + (uint32_t)(b * C::ACC + c0), *reinterpret_cast<int(*)[16]>(&dlo[c0]));
-                if (BITS == 4) {
+            for (int h = 0; h < H; h++)
 #pragma unroll
-                    for (int c0 = 0; c0 < N; c0 += 16)
-                        tmem_ld16(lane_base + (uint32_t)(b * C::ACC + N + c0), *reinterpret_cast<int(*)[16]>(&dhi[c0]));
-                }
-                tmem_wait_ld();
-            } else {
+                for (int m = 0; m < M; m++) acc[h][m] = 0.f;
+            bool seg_end = false;
+            while (!seg_end) {
+                const int n = w.next(NU);
+                const long long it0 = (long long)w.tile * p.units + w.unit;
+                seg_end = w.advance(n);
+                if ((k & 1) == g) {
+                    const int buf = k % NB;
+                    float wsc[NU][H];
+                    if (BITS == 4) {
 #pragma unroll
-                for (int n = 0; n < N; n++) dlo[n] = dhi[n] = 0;
-            }
-            tc_fence_before();
-            named_sync(1, 128);
-            if (threadIdx.x == 128) {
-                mbar_arrive(&accempty[b]);
-                mbar_arrive(&empty[s]);
-            }
+                        for (int j = 0; j < NU; j++)
 #pragma unroll
-            for (int m = 0; m < M; m++) {
-                float vlo, vhi;
-                if (BITS == 8) {
-                    vlo = (float)dlo[m * 4 + 3];
-                    vlo = fmaf(vlo, 0.0078125f, (float)dlo[m * 4 + 2]);
-                    vlo = fmaf(vlo, 0.0078125f, (float)dlo[m * 4 + 1]);
-                    vlo = fmaf(vlo, 0.0078125f, (float)dlo[m * 4 + 0]);
-                    acc[0][m] = fmaf(vlo, scl[m], acc[0][m]);
-                } else {
-                    vlo = (float)(dlo[m * 4 + 3] - 8 * bsum[m][3]);
-                    vhi = (float)(dhi[m * 4 + 3] - 8 * bsum[m][3]);
-#pragma unroll
-                    for (int q = 2; q >= 0; q--) {
-                        vlo = fmaf(vlo, 0.0078125f, (float)(dlo[m * 4 + q] - 8 * bsum[m][q]));
-                        vhi = fmaf(vhi, 0.0078125f, (float)(dhi[m * 4 + q] - 8 * bsum[m][q]));
+                            for (int h = 0; h < H; h++)
+                                wsc[j][h] = j < n ? __ldg(p.scale + (it0 + j) * (2 * kCols) + h * kCols + col) : 0.f;
                     }
-                    acc[0][m] = fmaf(vlo * scl[m], wlo, acc[0][m]);
-                    acc[1][m] = fmaf(vhi * scl[m], whi, acc[1][m]);
+                    prefetch(); // batch (k >> 1) + PD of this warpgroup
+                    cp_async_wait<C::MSLOTS - 2>(); // this thread's part of batch k's meta has landed
+                    bool ok = wait_fast(&done[k % DR], (k / DR) & 1, abort, p.status);
+                    ok = __all_sync(0xffffffffu, ok);
+                    named_sync(2 + g, kEpiThreads); // publishes batch k's meta to the warpgroup
+                    tc_fence_after();
+                    const uint8_t *mb = mring + ((k >> 1) % C::MSLOTS) * NU * PL::MB;
+                    for (int j = 0; j < n; j++) {
+                        int d[H][N];
+                        if (ok) {
+#pragma unroll
+                            for (int h = 0; h < H; h++)
+#pragma unroll
+                                for (int c0 = 0; c0 < N; c0 += 16)
+                                    tmem_ld16(lane_base + (uint32_t)(buf * C::BACC + j * C::ACC + h * N + c0),
+                                              *reinterpret_cast<int(*)[16]>(&d[h][c0]));
+                            tmem_wait_ld();
+                        } else {
+#pragma unroll
+                            for (int h = 0; h < H; h++)
+#pragma unroll
+                                for (int q = 0; q < N; q++) d[h][q] = 0;
+                        }
+                        const float *meta = reinterpret_cast<const float *>(mb + j * PL::MB);
+#pragma unroll
+                        for (int h = 0; h < H; h++)
+#pragma unroll
+                            for (int m = 0; m < M; m++) {
+                                const int o = BITS == 4 ? 8 : 0; // int4 codes carry +8: subtract 8 * digit sum
+                                const int *bsum = reinterpret_cast<const int *>(meta) + M + m * 4;
+                                float v = (float)(d[h][m * 4 + 3] - o * bsum[3]);
+#pragma unroll
+                                for (int q = 2; q >= 0; q--)
+                                    v = fmaf(v, 0.0078125f, (float)(d[h][m * 4 + q] - o * bsum[q]));
+                                if (BITS == 4) {
+                                    float ws = 0.f;
+#pragma unroll
+                                    for (int jj = 0; jj < NU; jj++)
+                                        if (jj == j) ws = wsc[jj][h];
+                                    acc[h][m] = fmaf(v * meta[m], ws, acc[h][m]);
+                                } else {
+                                    acc[h][m] = fmaf(v, meta[m], acc[h][m]);
+                                }
+                            }
+                    }
+                    tc_fence_before();
+                    named_sync(2 + g, kEpiThreads);
+                    if (et == 0) mbar_arrive(&accempty[buf]);
                 }
+                k++;
             }
-            // ---- tile segment end: write or reduce ----
-            const bool seg_end = (k + 1 == nitems) || ((it + 1) % p.units == 0);
-            if (seg_end) {
+            // ---- tile segment end: warpgroup 1 hands its sums to warpgroup 0 ----
+            if (g == 1) {
+#pragma unroll
+                for (int h = 0; h < H; h++)
+#pragma unroll
+                    for (int m = 0; m < M; m++) red[(h * M + m) * kCols + col] = acc[h][m];
+            }
+            named_sync(4, 2 * kEpiThreads);
+            if (g == 0) {
+#pragma unroll
+                for (int h = 0; h < H; h++)
+#pragma unroll
+                    for (int m = 0; m < M; m++) acc[h][m] += red[(h * M + m) * kCols + col];
                 const long long t0 = (long long)tile * p.units, t1 = t0 + p.units;
                 int cf = (int)(t0 * G / p.items);
                 while (cf + 1 < G && item_start(p.items, cf + 1, G) <= t0) cf++;
@@ -453,40 +583,39 @@ __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
                 int cl = (int)((t1 - 1) * G / p.items);
                 while (cl + 1 < G && item_start(p.items, cl + 1, G) <= t1 - 1) cl++;
                 while (cl > 0 && item_start(p.items, cl, G) > t1 - 1) cl--;
-                constexpr int SL = (BITS == 8 ? 1 : 2) * M * kCols; // partial entries per tile
+                constexpr int SL = H * M * kCols; // partial entries per tile
                 bool write = true;
                 if (cf != cl) {
                     const int slot = 2 * c + (i0 >= t0 ? 0 : 1);
                     float *dst = p.partial + (size_t)slot * SL;
 #pragma unroll
-                    for (int h = 0; h < (BITS == 8 ? 1 : 2); h++)
+                    for (int h = 0; h < H; h++)
 #pragma unroll
                         for (int m = 0; m < M; m++) dst[(h * M + m) * kCols + col] = acc[h][m];
                     __threadfence();
-                    named_sync(1, 128);
-                    if (threadIdx.x == 128) {
+                    named_sync(2, kEpiThreads);
+                    if (et == 0) {
                         const unsigned prev = atomicAdd(&p.counters[tile], 1u);
                         *lastflag = prev == (unsigned)(cl - cf);
                         if (*lastflag) p.counters[tile] = 0;
                     }
-                    named_sync(1, 128);
+                    named_sync(2, kEpiThreads);
                     write = *lastflag != 0;
                     if (write) {
                         __threadfence();
 #pragma unroll
-                        for (int h = 0; h < (BITS == 8 ? 1 : 2); h++)
+                        for (int h = 0; h < H; h++)
 #pragma unroll
                             for (int m = 0; m < M; m++) acc[h][m] = 0.f;
                         for (int cc = cf; cc <= cl; cc++) {
                             const int sl = 2 * cc + (item_start(p.items, cc, G) >= t0 ? 0 : 1);
                             const float *src = p.partial + (size_t)sl * SL;
 #pragma unroll
-                            for (int h = 0; h < (BITS == 8 ? 1 : 2); h++)
+                            for (int h = 0; h < H; h++)
 #pragma unroll
                                 for (int m = 0; m < M; m++) acc[h][m] += __ldcg(src + (h * M + m) * kCols + col);
                         }
                     }
-                    named_sync(1, 128); // lastflag is rewritten by the next shared tile
                 }
                 if (write) {
                     const int base = tile * kCols + col; // byte index in the reference row
@@ -500,16 +629,14 @@ __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
 #pragma unroll
                         for (int m = 0; m < M; m++) {
                             p.out[(size_t)m * p.cols + base] = acc[0][m];
-                            p.out[(size_t)m * p.cols + p.half + base] = acc[1][m];
+                            p.out[(size_t)m * p.cols + p.half + base] = acc[H - 1][m];
                         }
                     }
                 }
-#pragma unroll
-                for (int h = 0; h < 2; h++)
-#pragma unroll
-                    for (int m = 0; m < M; m++) acc[h][m] = 0.f;
             }
+            named_sync(4, 2 * kEpiThreads); // red and lastflag are reused by the next segment
         }
+        cp_async_wait<0>();
     }
 
     tc_fence_before();
@@ -553,8 +680,8 @@ cudaError_t launch_ig(const TqMatrixDev &mat, const float *x, float *out, const 
     prm.items = (long long)mat.tiles * mat.units;
     const int sms = sm_count[dev];
     if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS) return cudaErrorInvalidValue;
+    if ((size_t)mat.units * (Planes<M>::BBYTES + Planes<M>::MB) > TQ_SCRATCH_PLANES_BYTES) return cudaErrorInvalidValue;
     const int ctas = (int)(prm.items < sms ? prm.items : sms);
-    if ((size_t)mat.units * C::UB > TQ_SCRATCH_PLANES_BYTES) return cudaErrorInvalidValue;
     // Both launches may begin before their predecessor on the stream ends
     // (programmatic dependent launch); each waits on griddepcontrol.wait
     // before touching data the predecessor produces.
@@ -567,7 +694,7 @@ cudaError_t launch_ig(const TqMatrixDev &mat, const float *x, float *out, const 
     cfg.numAttrs = 1;
     cfg.gridDim = dim3(mat.units);
     cfg.blockDim = dim3(64);
-    e = cudaLaunchKernelEx(&cfg, planes_kernel<M>, x, mat.rows, scr.planes);
+    e = cudaLaunchKernelEx(&cfg, planes_kernel<M>, x, mat.rows, mat.units, scr.planes);
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(ctas);
     cfg.blockDim = dim3(kThreads);
