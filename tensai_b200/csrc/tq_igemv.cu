@@ -592,9 +592,11 @@ __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
                     for (int h = 0; h < H; h++)
 #pragma unroll
                         for (int m = 0; m < M; m++) dst[(h * M + m) * kCols + col] = acc[h][m];
-                    __threadfence();
                     named_sync(2, kEpiThreads);
                     if (et == 0) {
+                        // The barrier orders the warpgroup's partial stores before this
+                        // thread's fence (cumulativity); the fence publishes them at gpu scope.
+                        __threadfence();
                         const unsigned prev = atomicAdd(&p.counters[tile], 1u);
                         *lastflag = prev == (unsigned)(cl - cf);
                         if (*lastflag) p.counters[tile] = 0;
@@ -607,13 +609,26 @@ __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
                         for (int h = 0; h < H; h++)
 #pragma unroll
                             for (int m = 0; m < M; m++) acc[h][m] = 0.f;
-                        for (int cc = cf; cc <= cl; cc++) {
-                            const int sl = 2 * cc + (item_start(p.items, cc, G) >= t0 ? 0 : 1);
-                            const float *src = p.partial + (size_t)sl * SL;
+                        // contributors in CTA order, up to four loads in flight per entry
+                        for (int cc = cf; cc <= cl; cc += 4) {
+                            float pv[4][H][M];
 #pragma unroll
-                            for (int h = 0; h < H; h++)
+                            for (int u = 0; u < 4; u++) {
+                                const int c2 = cc + u;
+                                const int sl = 2 * c2 + (c2 <= cl && item_start(p.items, c2, G) >= t0 ? 0 : 1);
+                                const float *src = p.partial + (size_t)sl * SL;
 #pragma unroll
-                                for (int m = 0; m < M; m++) acc[h][m] += __ldcg(src + (h * M + m) * kCols + col);
+                                for (int h = 0; h < H; h++)
+#pragma unroll
+                                    for (int m = 0; m < M; m++)
+                                        pv[u][h][m] = c2 <= cl ? __ldcg(src + (h * M + m) * kCols + col) : 0.f;
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+#pragma unroll
+                                for (int h = 0; h < H; h++)
+#pragma unroll
+                                    for (int m = 0; m < M; m++) acc[h][m] += pv[u][h][m];
                         }
                     }
                 }

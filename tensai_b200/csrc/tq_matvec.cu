@@ -46,7 +46,6 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTile = TQ_TILE_BYTES;  // bytes of a code row per item
 constexpr int kUnit = TQ_GROUP;       // rows per item
-constexpr int kStages = 2;            // buffers per warp
 constexpr int kBuf = kTile * kUnit;   // 8 KB
 constexpr unsigned long long kWaitNs = 2000000000ull; // mbarrier wait limit: 2 s
 
@@ -169,17 +168,19 @@ __device__ __forceinline__ void qmv_row(uint32_t w, const float (&xv)[M], float2
 }
 
 // Shared-memory layout (bytes):
-//   bufs [kWarps][kStages][kBuf]           code boxes (TMA destination)
+//   bufs [kWarps][ST][kBuf]                code boxes (TMA destination); ST = 3
+//                                          buffers per warp for M <= 2, else 2
 //   xs   [kWarps][2][M][kUnit] floats      activations of the current/next item
 //   red  [kWarps][M][2NP][32] floats       warp partials of a tile segment
-//   flag [4] ints, mbar [kWarps][kStages] u64
+//   flag [4] ints, mbar [kWarps][ST] u64
 template <int BITS, int M> struct Smem {
     static constexpr int NP = kPairs<BITS>();
-    static constexpr size_t bufs = (size_t)kWarps * kStages * kBuf;
+    static constexpr int ST = M <= 2 ? 3 : 2;
+    static constexpr size_t bufs = (size_t)kWarps * ST * kBuf;
     static constexpr size_t xs = (size_t)kWarps * 2 * M * kUnit * sizeof(float);
     static constexpr size_t red = (size_t)kWarps * M * 2 * NP * 32 * sizeof(float);
     static constexpr size_t flag = 16;
-    static constexpr size_t mbar = (size_t)kWarps * kStages * sizeof(uint64_t);
+    static constexpr size_t mbar = (size_t)kWarps * ST * sizeof(uint64_t);
     static constexpr size_t total = bufs + xs + red + flag + mbar;
 };
 
@@ -189,6 +190,7 @@ template <int BITS, int M>
 __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(QmvParams p) {
     using S = Smem<BITS, M>;
     constexpr int NP = S::NP;
+    constexpr int kStages = S::ST;
     constexpr int SLOTS = M * 2 * NP * 32; // partial entries per tile segment (M x tile columns)
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *bufs = smem;
@@ -346,9 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(QmvParams p) {
             float *dst = p.partial + (size_t)slot * SLOTS;
             __syncthreads();
             for (int idx = threadIdx.x; idx < SLOTS; idx += kThreads) dst[idx] = red[idx];
-            __threadfence();
             __syncthreads();
             if (threadIdx.x == 0) {
+                // The barrier orders the CTA's partial stores before this thread's
+                // fence (cumulativity); the fence publishes them at gpu scope.
+                __threadfence();
                 const unsigned prev = atomicAdd(&p.counters[tile], 1u);
                 flag[0] = prev == (unsigned)(cl - cf);
                 if (flag[0]) p.counters[tile] = 0; // every contributor has arrived: re-arm
@@ -364,10 +368,18 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(QmvParams p) {
             for (int idx = threadIdx.x; idx < SLOTS; idx += kThreads) {
                 float s;
                 if (shared_tile) {
+                    // contributors in CTA order, four loads in flight
                     s = 0.f;
-                    for (int cc = cf; cc <= cl; cc++) {
-                        const int slot = 2 * cc + (item_start(p.items, cc, G) >= t0 ? 0 : 1);
-                        s += __ldcg(p.partial + (size_t)slot * SLOTS + idx);
+                    for (int cc = cf; cc <= cl; cc += 4) {
+                        float pv[4];
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const int c2 = cc + u;
+                            const int slot = 2 * c2 + (c2 <= cl && item_start(p.items, c2, G) >= t0 ? 0 : 1);
+                            pv[u] = c2 <= cl ? __ldcg(p.partial + (size_t)slot * SLOTS + idx) : 0.f;
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; u++) s += pv[u];
                     }
                 } else {
                     s = src[idx];
