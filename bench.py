@@ -11,8 +11,11 @@ Each step is one CUDA-graph replay of the 64 launches.
            ranks), bytes per matvec = codes + scales + x + out (each once)
   e2e      the same bytes through the C-ABI MatVec entry point (tq_matvec) with
            host buffers: every call copies x host->device and out device->host
-  roofline the matvec kernel's achieved GB/s (per-launch CUDA events inside the
-           timed graph) against the measured HBM copy bandwidth
+  roofline the matvec's achieved GB/s: algorithmic bytes of one call over the
+           mean device time of a call inside the timed graph (CUDA events on
+           the launching stream around K replays of 64 calls; one call = the
+           digit-plane kernel plus the tcgen05 matvec kernel it chains to),
+           against the measured HBM copy bandwidth
   cpu_baseline  the CPU oracle (AVX2 restatement of quant4_simd.go with the
            reference's worker split) on the host cores, bounded sample
 
@@ -41,6 +44,7 @@ METRIC = "int8/int4 dequant-matvec HBM GB/s (% of peak); decode tokens/s at 1/2/
 K_UP, N_UP = 4096, 11008
 LAYERS = 32
 FALLBACK_HBM_GBS = 6650.0
+LAUNCHES_PER_CALL = 2  # planes_kernel + igemv_kernel per int4 M=1 matvec
 WORKLOAD = ("int4 g64 MLP pair (up 4096x11008 + down 11008x4096), M=1, fp32 accumulate; "
             "32 resident layer copies streamed per step")
 
@@ -66,13 +70,16 @@ def load_peak():
 
 
 def load_traffic():
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "traffic.json")
+    """Per-launch DRAM bytes (read + write) of the matvec kernel from the
+    committed ncu summary (its `traffic_bytes_per_launch:` line), or None."""
+    import re
+    path = os.path.join(ROOT, "profiles", "igemv_int4_m1_mlp_pair.md")
     try:
         with open(path) as f:
-            return json.load(f)
-    except Exception:
-        return {}
+            m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", f.read())
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
 
 
 class ClockSampler:
@@ -263,10 +270,6 @@ def run_gpu(args, rank: int, world: int):
     with torch.cuda.graph(graph, stream=stream):
         step()
     torch.cuda.synchronize()
-    # The last timed step runs the same 64 launches eagerly with an event pair
-    # around each one: per-launch kernel durations (events recorded inside a
-    # graph cannot be timed).
-    kev = [torch.cuda.Event(enable_timing=True) for _ in range(4 * LAYERS)]
 
     for _ in range(max(args.warmup, 3)):
         graph.replay()
@@ -279,15 +282,13 @@ def run_gpu(args, rank: int, world: int):
     with ClockSampler(dev) as clocks:
         with torch.cuda.stream(stream):
             start.record(stream)
-            for _ in range(args.steps - 1):
+            for _ in range(args.steps):
                 graph.replay()
-            step(kev)
             end.record(stream)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end)
-    kernel_ms = [kev[2 * i].elapsed_time(kev[2 * i + 1]) for i in range(2 * LAYERS)]
 
     ms_t = torch.tensor([ms], device="cuda", dtype=torch.float64)
     if world > 1:
@@ -297,7 +298,6 @@ def run_gpu(args, rank: int, world: int):
     value = bytes_step * world * args.steps / (ms_max * 1e-3) / 1e9
 
     # End to end through the C-ABI MatVec (host buffers, synchronous calls).
-    from oracle import oracle as O  # noqa: F401  (seeded host inputs only)
     hx_up = x_up.cpu().numpy().reshape(-1).copy()
     hx_dn = x_dn.cpu().numpy().reshape(-1).copy()
     ho_up = np.empty(N_UP, np.float32)
@@ -325,9 +325,9 @@ def run_gpu(args, rank: int, world: int):
     if rank == 0:
         peak, peak_src = load_peak()
         per_launch = pair_bytes() / 2  # up and down carry the same algorithmic bytes
-        kavg = statistics.mean(kernel_ms)
+        kavg = ms / (args.steps * 2 * LAYERS)  # ms per call on this rank
         achieved = per_launch / (kavg * 1e-3) / 1e9
-        traffic = load_traffic().get("qmv_int4_m1_mlp_pair")
+        traffic = load_traffic()
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
@@ -337,14 +337,16 @@ def run_gpu(args, rank: int, world: int):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "frac_of_8tbs": round(achieved / 8000.0, 4),
-                         "traffic": traffic, "kernel": "qmv_kernel<4,1,*> (int4 dequant-matvec, M=1)",
-                         "kernel_us_mean": round(kavg * 1e3, 3),
+                         "traffic": traffic,
+                         "kernel": "igemv_kernel<4,1> (int4 dequant-matvec on tcgen05 kind::i8, M=1) "
+                                   "with its planes_kernel<1>",
+                         "call_us_mean": round(kavg * 1e3, 3),
                          "algorithmic_bytes_per_launch": per_launch},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": LAYERS * 4 * (K_UP + N_UP),
                     "d2h_bytes_per_step": LAYERS * 4 * (N_UP + K_UP),
                     "api": "tq_matvec (host x/out, synchronous), the MatVec drop-in", "steps": e2e_steps},
-            "gpu_launches": args.steps * 2 * LAYERS,
+            "gpu_launches": args.steps * 2 * LAYERS * LAUNCHES_PER_CALL,
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -359,7 +361,7 @@ def main():
     global LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)  # >= 2: the last step carries the per-launch events
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
@@ -367,7 +369,7 @@ def main():
                     help="resident MLP pairs per step (default 32 = 1.63 GB; small values for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    args.steps = max(args.steps, 2)
+    args.steps = max(args.steps, 1)
     LAYERS = max(1, args.layers)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
