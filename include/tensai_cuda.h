@@ -124,6 +124,27 @@ TQ_EXPORT int tq_matmul(uint64_t handle, const float *x, float *out, int m);
  * these launches must not be replayed concurrently with each other. */
 TQ_EXPORT int tq_matmul_dev(uint64_t handle, const float *x, float *out, int m, void *stream);
 
+/* As tq_matmul_dev, but allocates nothing: no device or pinned memory, on
+ * any call. No counterpart in the reference (its Go MatVec allocates no GPU
+ * memory at all); it exists for callers that must not have the library
+ * allocate at run time, e.g. a serving process that has handed all free HBM
+ * to its own weight and KV-cache pool, where a library cudaMalloc could fail
+ * mid-decode or stall the device.
+ * Runs the CUDA-core kernel (tq_set_matvec_kernel does not apply) with its
+ * cross-CTA scratch in fixed device arrays inside the library: 1.25 MiB of
+ * partial sums plus 4096 tile counters, zero at load and left at zero by
+ * every call. Limits: matrices of at most 4096 column tiles (524,288 int8 /
+ * 1,048,576 int4 columns) and GPUs of at most 160 SMs, else
+ * TQ_ERR_UNSUPPORTED with a message naming the limit; activation rows run 4
+ * per launch, any m. The first call on each device does the set-up (looks up
+ * the fixed arrays' device addresses) and should come before any stream
+ * capture. All callers on one device share the fixed scratch: calls that may
+ * overlap on the device (other streams, other threads) race and corrupt each
+ * other's results, so issue them in order on one stream. A bounded-wait
+ * timeout inside the kernel is recorded in the fixed status word only and is
+ * not reported by tq_device_status. */
+TQ_EXPORT int tq_matmul_dev_fixed(uint64_t handle, const float *x, float *out, int m, void *stream);
+
 /* Selects the GPU kernel behind tq_matvec / tq_matmul / tq_matmul_dev for
  * m <= 8 (process-wide): 0 = tensor-core integer MMA (default: weights used as
  * stored, activations split into exact int8 digit planes); 1 = CUDA-core

@@ -49,6 +49,7 @@ SIGNATURES = {
     "tq_matvec": (I, [U64, P, SZ, P, SZ]),
     "tq_matmul": (I, [U64, P, P, I]),
     "tq_matmul_dev": (I, [U64, P, P, I, P]),
+    "tq_matmul_dev_fixed": (I, [U64, P, P, I, P]),
     "tq_synth_dev": (I, [P, SZ, U64, U64, F, P]),
     "tq_device_status": (I, [ctypes.POINTER(ctypes.c_uint)]),
     "tq_set_matvec_kernel": (I, [I]),

@@ -430,6 +430,30 @@ int tq_matmul_dev(uint64_t handle, const float *x, float *out, int m, void *stre
     return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "matmul launch");
 }
 
+int tq_matmul_dev_fixed(uint64_t handle, const float *x, float *out, int m, void *stream) {
+    int rc;
+    auto p = tq_lookup_checked(handle, &rc);
+    if (!p) return rc;
+    if (m < 0) return tq_fail(TQ_ERR_ARG, "tensai: negative row count %d", m);
+    if (m && ((!x && p->m.rows) || (!out && p->m.cols))) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    cudaError_t e = cudaSetDevice(p->device);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "set device");
+    switch (tq_launch_matvec_fixed(p->m, x, out, m, (cudaStream_t)stream, &e)) {
+    case TQ_FIXED_OK: return TQ_OK;
+    case TQ_FIXED_DEVICE: return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: fixed-scratch matvec serves devices 0-63 only");
+    case TQ_FIXED_SMS:
+        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: fixed-scratch matvec serves GPUs with at most %d SMs",
+                       TQ_FIXED_MAX_SMS);
+    case TQ_FIXED_TILES:
+        return tq_fail(TQ_ERR_UNSUPPORTED,
+                       "tensai: matrix of %d columns exceeds the fixed-scratch limit of %d column tiles "
+                       "(%d int8 / %d int4 columns); use tq_matmul_dev",
+                       p->m.cols, TQ_FIXED_MAX_TILES, TQ_FIXED_MAX_TILES * TQ_TILE_BYTES,
+                       2 * TQ_FIXED_MAX_TILES * TQ_TILE_BYTES);
+    default: return tq_cuda_fail(e, "fixed-scratch matmul launch");
+    }
+}
+
 int tq_matmul(uint64_t handle, const float *x, float *out, int m) {
     int rc;
     auto p = tq_lookup_checked(handle, &rc);

@@ -96,3 +96,10 @@ cudaError_t tq_launch_matvec(const TqMatrixDev &m, const float *x, float *out, i
                              cudaStream_t st);
 cudaError_t tq_launch_igemv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                             cudaStream_t st);
+// Allocation-free CUDA-core matvec (fixed device scratch in tq_matvec.cu).
+enum { TQ_FIXED_OK = 0, TQ_FIXED_CUDA, TQ_FIXED_DEVICE, TQ_FIXED_SMS, TQ_FIXED_TILES };
+#define TQ_FIXED_MAX_TILES 4096
+#define TQ_FIXED_MAX_SMS 160
+#define TQ_FIXED_ROWS_PER_LAUNCH 4
+int tq_launch_matvec_fixed(const TqMatrixDev &m, const float *x, float *out, int M, cudaStream_t st,
+                           cudaError_t *err);

@@ -37,6 +37,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
 
 #include "tq_common.cuh"
 
@@ -472,3 +473,79 @@ cudaError_t tq_launch_matvec(const TqMatrixDev &mat, const float *x, float *out,
     return cudaSuccess;
 }
 
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant (tq_matmul_dev_fixed in the C ABI): the same kernel
+// with its cross-CTA scratch in fixed device arrays of this file instead of
+// the per-stream scratch the library allocates on first use.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kFixedRows = TQ_FIXED_ROWS_PER_LAUNCH; // activation rows per launch (more: consecutive launches)
+constexpr int kFixedCtas = TQ_FIXED_MAX_SMS;          // largest grid served (one CTA per SM; a B200 has 148)
+constexpr int kFixedTiles = TQ_FIXED_MAX_TILES;       // column tiles: 524,288 int8 / 1,048,576 int4 columns
+// Partial sums: two slots per CTA of up to kFixedRows x 256 floats (int4, the
+// larger case): 1.25 MiB.
+constexpr size_t kFixedPartialFloats = (size_t)2 * kFixedCtas * kFixedRows * 2 * kPairs<4>() * 32;
+
+// Must be zero before the first launch: the tile arrival counters and the
+// status word. Static device memory is zero when the module loads, and every
+// launch leaves each counter it used at zero again (the last CTA to arrive at
+// a tile re-arms it). The partial sums need no initial value.
+static __device__ __align__(256) float g_fixed_partial[kFixedPartialFloats];
+static __device__ __align__(256) unsigned g_fixed_words[kFixedTiles + 32]; // counters, then status
+
+struct FixedScratch {
+    bool ready;
+    int sms;
+    TqScratch scr;
+};
+FixedScratch g_fixed[64];
+std::mutex g_fixed_mu;
+
+} // namespace
+
+// Launches out = x @ W for M rows with the fixed scratch. Set-up runs once per
+// device, with that device current: the symbol addresses of the fixed arrays
+// (cudaGetSymbolAddress) and the SM count. Returns TQ_FIXED_OK or the limit
+// that was exceeded; *err holds a CUDA error for TQ_FIXED_CUDA.
+int tq_launch_matvec_fixed(const TqMatrixDev &mat, const float *x, float *out, int M, cudaStream_t st,
+                           cudaError_t *err) {
+    *err = cudaSuccess;
+    int dev = 0;
+    if ((*err = cudaGetDevice(&dev)) != cudaSuccess) return TQ_FIXED_CUDA;
+    if (dev < 0 || dev >= 64) return TQ_FIXED_DEVICE;
+    TqScratch scr;
+    {
+        std::lock_guard<std::mutex> lk(g_fixed_mu);
+        FixedScratch &f = g_fixed[dev];
+        if (!f.ready) {
+            void *partial = nullptr, *words = nullptr;
+            if ((*err = cudaGetSymbolAddress(&partial, g_fixed_partial)) != cudaSuccess) return TQ_FIXED_CUDA;
+            if ((*err = cudaGetSymbolAddress(&words, g_fixed_words)) != cudaSuccess) return TQ_FIXED_CUDA;
+            if ((*err = cudaDeviceGetAttribute(&f.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+                return TQ_FIXED_CUDA;
+            f.scr.partial = static_cast<float *>(partial);
+            f.scr.counters = static_cast<unsigned *>(words);
+            f.scr.status = static_cast<unsigned *>(words) + kFixedTiles;
+            f.scr.planes = nullptr;
+            f.ready = true;
+        }
+        if (f.sms > kFixedCtas) return TQ_FIXED_SMS;
+        scr = f.scr;
+    }
+    if (mat.tiles > kFixedTiles) return TQ_FIXED_TILES;
+    if (M <= 0 || mat.cols == 0) return TQ_FIXED_OK;
+    if (mat.rows == 0) {
+        *err = cudaMemsetAsync(out, 0, sizeof(float) * (size_t)M * mat.cols, st);
+        return *err == cudaSuccess ? TQ_FIXED_OK : TQ_FIXED_CUDA;
+    }
+    for (int m0 = 0; m0 < M; m0 += kFixedRows) {
+        const int mm = M - m0 < kFixedRows ? M - m0 : kFixedRows;
+        const float *xm = x + (size_t)m0 * mat.rows;
+        float *om = out + (size_t)m0 * mat.cols;
+        *err = mat.bits == 8 ? dispatch_m<8>(mat, xm, om, mm, scr, st) : dispatch_m<4>(mat, xm, om, mm, scr, st);
+        if (*err != cudaSuccess) return TQ_FIXED_CUDA;
+    }
+    return TQ_FIXED_OK;
+}
