@@ -74,17 +74,35 @@ cudaError_t tq_dev_malloc(void **p, size_t bytes) {
 
 static ThreadCtx *ctx_for(int device) { return &t_ctx[device]; }
 
-// The scratch of (device, stream), created and cleared on first use; the first
-// matvec on a stream must therefore not be inside a CUDA-graph capture.
-static int scratch_for(int device, cudaStream_t st, TqScratch *out) {
+// The partial-sum buffer of the M >= 16 matmul, added to a stream's scratch
+// on the first such call.
+static int add_mm_partial(int device, TqScratch *s) {
+    int sms = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = tq_dev_malloc((void **)&s->mm_partial, tq_mm_partial_floats(sms) * sizeof(float));
+    if (e != cudaSuccess) {
+        s->mm_partial = nullptr;
+        return tq_cuda_fail(e, "matmul scratch allocation");
+    }
+    return TQ_OK;
+}
+
+// The scratch of (device, stream), created and cleared on first use (and
+// widened on the first call with m >= TQ_MM_MIN_ROWS); those first calls on a
+// stream must therefore not be inside a CUDA-graph capture.
+static int scratch_for(int device, cudaStream_t st, TqScratch *out, int m = 1) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     auto key = std::make_pair(device, st);
     auto it = g_scratch.find(key);
     if (it != g_scratch.end()) {
+        if (m >= TQ_MM_MIN_ROWS && !it->second.mm_partial) {
+            int rc = add_mm_partial(device, &it->second);
+            if (rc) return rc;
+        }
         *out = it->second;
         return TQ_OK;
     }
-    TqScratch s{nullptr, nullptr, nullptr, nullptr};
+    TqScratch s{nullptr, nullptr, nullptr, nullptr, nullptr};
     const size_t words = TQ_MAX_TILES + 32; // arrival counters, then the status word
     cudaError_t e = tq_dev_malloc((void **)&s.partial, TQ_SCRATCH_PARTIAL_FLOATS * sizeof(float));
     if (e == cudaSuccess) e = tq_dev_malloc((void **)&s.counters, words * sizeof(unsigned));
@@ -96,6 +114,15 @@ static int scratch_for(int device, cudaStream_t st, TqScratch *out) {
         if (s.counters) cudaFree(s.counters);
         if (s.planes) cudaFree(s.planes);
         return tq_cuda_fail(e, "matvec scratch allocation");
+    }
+    if (m >= TQ_MM_MIN_ROWS) {
+        int rc = add_mm_partial(device, &s);
+        if (rc) {
+            cudaFree(s.partial);
+            cudaFree(s.counters);
+            cudaFree(s.planes);
+            return rc;
+        }
     }
     g_scratch[key] = s;
     *out = s;
@@ -116,8 +143,11 @@ static cudaError_t read_status(const TqScratch &scr, cudaStream_t st, unsigned *
 // 0: tensor-core matvec (tq_igemv.cu, default); 1: CUDA-core matvec (tq_matvec.cu).
 std::atomic<int> g_matvec_kernel{0};
 
+// M >= TQ_MM_MIN_ROWS: the tf32 tensor-core matmul; fewer rows: the matvec
+// kernel chosen by tq_set_matvec_kernel (8 rows per launch).
 static cudaError_t launch_matvec(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                                  cudaStream_t st) {
+    if (M >= TQ_MM_MIN_ROWS) return tq_launch_mm(m, x, out, M, scr, st);
     return g_matvec_kernel.load() == 1 ? tq_launch_matvec(m, x, out, M, scr, st)
                                        : tq_launch_igemv(m, x, out, M, scr, st);
 }
@@ -425,7 +455,7 @@ int tq_matmul_dev(uint64_t handle, const float *x, float *out, int m, void *stre
     cudaError_t e = cudaSetDevice(p->device);
     if (e != cudaSuccess) return tq_cuda_fail(e, "set device");
     TqScratch scr;
-    if ((rc = scratch_for(p->device, (cudaStream_t)stream, &scr))) return rc;
+    if ((rc = scratch_for(p->device, (cudaStream_t)stream, &scr, m))) return rc;
     e = launch_matvec(p->m, x, out, m, scr, (cudaStream_t)stream);
     return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "matmul launch");
 }
@@ -470,7 +500,7 @@ int tq_matmul(uint64_t handle, const float *x, float *out, int m) {
         (rc = grow_host(&c->h_x, &c->h_x_cap, nx)) || (rc = grow_host(&c->h_out, &c->h_out_cap, no)))
         return rc;
     TqScratch scr;
-    if ((rc = scratch_for(p->device, c->stream, &scr))) return rc;
+    if ((rc = scratch_for(p->device, c->stream, &scr, m))) return rc;
     std::memcpy(c->h_x, x, nx * sizeof(float));
     e = cudaMemcpyAsync(c->d_x, c->h_x, nx * sizeof(float), cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess) e = launch_matvec(p->m, c->d_x, c->d_out, m, scr, c->stream);

@@ -41,9 +41,14 @@ struct TqScratch {
     unsigned *counters; // TQ_MAX_TILES
     unsigned *status;   // TQ_STATUS_* bits set by kernels on this stream
     uint8_t *planes;    // TQ_SCRATCH_PLANES_BYTES: activation digit planes of a matvec
+    float *mm_partial;  // tq_mm_partial_floats(SMs): tile partials of the M >= 16 matmul (or null)
 };
 #define TQ_SCRATCH_PARTIAL_FLOATS ((size_t)2 * TQ_MAX_CTAS * 8 * 8 * 32)
 #define TQ_SCRATCH_PLANES_BYTES ((size_t)8 << 20) // 2304 B per 64 rows: K <= 233,000
+#define TQ_MM_MIN_ROWS 16  // activation rows from which tq_matmul* use the tf32 tensor-core matmul
+#define TQ_MM_MAX_ROWS 128 // activation rows per matmul launch
+// Two partial slots per CTA of up to 2 runs x 128 rows x 128 columns.
+static inline size_t tq_mm_partial_floats(int sms) { return (size_t)2 * sms * 2 * TQ_MM_MAX_ROWS * TQ_TILE_BYTES; }
 
 struct TqMatrixDev {
     int bits;       // 8 or 4
@@ -96,6 +101,9 @@ cudaError_t tq_launch_matvec(const TqMatrixDev &m, const float *x, float *out, i
                              cudaStream_t st);
 cudaError_t tq_launch_igemv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                             cudaStream_t st);
+// Matmul for M >= 16 rows on tcgen05 kind::tf32 (needs scr.mm_partial).
+cudaError_t tq_launch_mm(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
+                         cudaStream_t st);
 // Allocation-free CUDA-core matvec (fixed device scratch in tq_matvec.cu).
 enum { TQ_FIXED_OK = 0, TQ_FIXED_CUDA, TQ_FIXED_DEVICE, TQ_FIXED_SMS, TQ_FIXED_TILES };
 #define TQ_FIXED_MAX_TILES 4096

@@ -529,6 +529,7 @@ int tq_launch_matvec_fixed(const TqMatrixDev &mat, const float *x, float *out, i
             f.scr.counters = static_cast<unsigned *>(words);
             f.scr.status = static_cast<unsigned *>(words) + kFixedTiles;
             f.scr.planes = nullptr;
+            f.scr.mm_partial = nullptr;
             f.ready = true;
         }
         if (f.sms > kFixedCtas) return TQ_FIXED_SMS;

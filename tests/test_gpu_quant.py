@@ -1,4 +1,4 @@
-"""GPU parity tests of the quantizers and the M<=8 dequant-matvec, through the
+"""GPU parity tests of the quantizers and the M<=15 dequant-matvec, through the
 C ABI (libtensai_cuda.so), against the CPU oracle.
 
 Bars (from the task's contract):
@@ -223,8 +223,9 @@ def test_ragged_shapes(bits, rows, cols, kernel):
 
 
 def test_more_than_8_rows_runs_in_chunks(kernel):
+    # 9..15 rows stay on the matvec kernels, 8 rows per launch
     _check_matmul(8, 512, 640, 11)
-    _check_matmul(4, 512, 640, 19)
+    _check_matmul(4, 512, 640, 15)
 
 
 def test_results_are_bit_reproducible(kernel):
