@@ -205,6 +205,71 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+# Side measurements of the other kernel configs (device time per call, CUDA
+# graph of back-to-back calls over enough distinct weight copies to exceed L2).
+SIDE_CONFIGS = [
+    # name, bits, rows, cols, m
+    ("C1 int8 4096x4096 M=1", 8, 4096, 4096, 1),
+    ("C2 int4 up 4096x11008 M=4", 4, 4096, 11008, 4),
+    ("C2 int4 up 4096x11008 M=8", 4, 4096, 11008, 8),
+    ("C3 int4 4096x4096 M=64 (tf32)", 4, 4096, 4096, 64),
+]
+
+
+def measure_side_configs(L, Q, torch, stream, peak):
+    out = {}
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    for name, bits, rows, cols, m in SIDE_CONFIGS:
+        per = algo_bytes(bits, rows, cols, m)
+        copies = max(2, int(160e6 // (rows * cols // (1 if bits == 8 else 2))) + 1)  # > L2 in total
+        w = torch.empty(rows, cols, device="cuda")
+        hs = []
+        for i in range(copies):
+            Q.synth_dev(w, 7, 100 + i, 0.02)
+            hs.append(Q.quantize_dev(w, bits))
+        del w
+        x = torch.empty(m, rows, device="cuda")
+        Q.synth_dev(x, 7, 99, 1.0)
+        o = torch.empty(m, cols, device="cuda")
+        xp, op = ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(o.data_ptr())
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for h in hs:
+                _check_rc(L, L.tq_matmul_dev(h, xp, op, m, sp))
+        torch.cuda.synchronize()
+        reps = 4
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(reps):
+                for h in hs:
+                    L.tq_matmul_dev(h, xp, op, m, sp)
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * len(hs))
+        rec = {"us_per_call": round(us, 3), "GB/s": round(per / us / 1e3, 1),
+               "frac_hbm": round(per / us / 1e3 / peak, 4), "algorithmic_bytes": per,
+               "weight_copies": len(hs)}
+        if m >= 16:
+            rec["TFLOP/s"] = round(2.0 * m * rows * cols / us / 1e6, 2)
+        out[name] = rec
+        del g
+        for h in hs:
+            Q.free(h)
+    return out
+
+
+def _check_rc(L, rc):
+    if rc:
+        raise RuntimeError(L.tq_last_error().decode())
+
+
 def bench_config():
     return {"workload": WORKLOAD.replace("32 resident", f"{LAYERS} resident"), "weights": "int4 group-64 (QuantizeMatrix4 layout)", "m": 1,
             "layers_per_step": LAYERS, "bytes_per_step": pair_bytes() * LAYERS,
@@ -322,6 +387,9 @@ def run_gpu(args, rank: int, world: int):
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_value = bytes_step * world * e2e_steps / float(e2e_t.item()) / 1e9
 
+    side = None
+    if rank == 0 and not args.no_side_configs:
+        side = measure_side_configs(L, Q, torch, stream, load_peak()[0])
     if rank == 0:
         peak, peak_src = load_peak()
         per_launch = pair_bytes() / 2  # up and down carry the same algorithmic bytes
@@ -349,6 +417,8 @@ def run_gpu(args, rank: int, world: int):
             "gpu_launches": args.steps * 2 * LAYERS * LAUNCHES_PER_CALL,
             "clocks": clocks.summary(),
         }
+        if side:
+            line["side_configs"] = side
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -368,6 +438,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="resident MLP pairs per step (default 32 = 1.63 GB; small values for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-side-configs", action="store_true")
     args = ap.parse_args()
     args.steps = max(args.steps, 1)
     LAYERS = max(1, args.layers)

@@ -46,7 +46,7 @@ struct TqScratch {
 #define TQ_SCRATCH_PARTIAL_FLOATS ((size_t)2 * TQ_MAX_CTAS * 8 * 8 * 32)
 #define TQ_SCRATCH_PLANES_BYTES ((size_t)8 << 20) // 2304 B per 64 rows: K <= 233,000
 #define TQ_MM_MIN_ROWS 16  // activation rows from which tq_matmul* use the tf32 tensor-core matmul
-#define TQ_MM_MAX_ROWS 128 // activation rows per matmul launch
+#define TQ_MM_MAX_ROWS 64  // activation rows per matmul launch
 // Two partial slots per CTA of up to 2 runs x 128 rows x 128 columns.
 static inline size_t tq_mm_partial_floats(int sms) { return (size_t)2 * sms * 2 * TQ_MM_MAX_ROWS * TQ_TILE_BYTES; }
 

@@ -8,12 +8,14 @@
 // exact in tf32; the dequantized weight code*scale (fp32, one rounding) and
 // x are rounded to tf32 (round to nearest, ties away) before the MMA, so
 // every product carries at most 2 x 2^-11 relative error and the sum is
-// accumulated in fp32: well inside a 2e-3 relative-L2 budget.
+// accumulated in fp32: well inside a 2e-3 relative-L2 budget. int8 codes go
+// into the MMA as they are and the column scale multiplies the finished sum,
+// as the reference does (quant.go:120).
 //
 // Mapping: the UMMA M dimension is 128 weight columns (one run of a column
 // tile: int8 tiles have one run, int4 tiles two, the low-nibble columns
 // j and the high-nibble columns j+N/2), N is the activation rows padded to
-// NP in {16, 32, 64, 128}, K is 8 rows of W per MMA. One 8 KB item (64 rows
+// NP in {16, 32, 64}, K is 8 rows of W per MMA. One 8 KB item (64 rows
 // x 128 code bytes, tq_common.cuh) feeds 8 K-steps per run.
 //
 // Operands in shared memory, both K-major in the canonical UMMA layout with
@@ -32,10 +34,14 @@
 // tile-major item list (stream-K). Warp roles (14 warps):
 //   warp 0       producer: one bulk copy per item (codes) plus its scales
 //   warp 1       owns tensor memory; lane 0 issues 8 x runs MMAs per item
-//   warps 2-9    dequantize the item into A, convert x into B (tf32)
-//   warps 10-13  epilogue: tcgen05.ld of a finished tile segment, output or
-//                scratch partials; tiles shared by several CTAs are summed
-//                by the last CTA to arrive, in CTA order (bit-reproducible)
+//   warps 2-9    dequantize the item into A, convert x into B (tf32); two
+//                groups of four warps, alternate items
+//   warps 10-13  epilogue: tcgen05.ld of a finished tile segment, written to
+//                the output (tile wholly inside the CTA) or to the CTA's
+//                partial slot in scratch (tile shared with other CTAs)
+// mm_reduce_kernel then sums the partials of every shared tile over its CTAs
+// in CTA order (a fixed order: results are bit-reproducible), all SMs at
+// once, so the split-K reduction runs at L2 bandwidth.
 // Accumulators are double-buffered in tensor memory, so the epilogue of one
 // tile segment overlaps the MMAs of the next. All waits are bounded (2 s);
 // a timeout sets TQ_STATUS_TIMEOUT and the CTA drains.
@@ -58,7 +64,7 @@ template <int BITS, int NP> struct MmCfg {
     static constexpr int B_BYTES = NP * kRows * 4;         // NP rows x 64 K x 4 B
     static constexpr int OSTRIDE = A_BYTES + B_BYTES;      // multiple of 1024
     static constexpr int OS = 2;                           // operand stages
-    static constexpr int SC_BYTES = H * kCols * 4;         // scales per item: 512 / 1024 B
+    static constexpr int SC_BYTES = BITS == 8 ? 0 : H * kCols * 4; // int4 group scales per item (1 KB)
     static constexpr int CSTRIDE = kItem + SC_BYTES;       // code stage: codes, then scales
     static constexpr int ACC = H * NP;                     // tensor-memory columns per accumulator
     static constexpr int NB = 2;                           // accumulator buffers
@@ -84,10 +90,10 @@ struct MmParams {
     const float *x; // [m][rows]
     float *out;     // [m][cols]
     float *partial; // [2 * ctas][H][NP][128]
-    unsigned *counters;
     unsigned *status;
     long long items;
     int rows, cols, half, units, tiles, m;
+    int xvec; // x rows are 16-byte aligned (rows % 4 == 0, aligned base): 128-bit loads
 };
 
 // Instruction descriptor of tcgen05.mma.kind::tf32: D f32, A and B tf32
@@ -128,7 +134,6 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmParams p) {
              *accempty = accfull + NB;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accempty + NB);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    volatile int *lastflag = reinterpret_cast<volatile int *>(tmem_slot + 2);
     auto ostage = [&](int j) { return smem + C::O_OFF + (j % OS) * C::OSTRIDE; };
     auto cstage = [&](int j) { return smem + C::C_OFF + (j % CS) * C::CSTRIDE; };
 
@@ -173,8 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmParams p) {
                 uint8_t *dst = cstage(j);
                 mbar_arrive_expect_tx(&cfull[j % CS], C::CSTRIDE);
                 bulk_load(dst, p.codes + it * kItem, kItem, &cfull[j % CS]);
-                const float *sc = BITS == 8 ? p.scale + (it / p.units) * kCols : p.scale + it * (2 * kCols);
-                bulk_load(dst + kItem, sc, C::SC_BYTES, &cfull[j % CS]);
+                if (BITS == 4) bulk_load(dst + kItem, p.scale + it * (2 * kCols), C::SC_BYTES, &cfull[j % CS]);
             }
         }
     } else if (warp == 1) {
@@ -212,44 +216,58 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmParams p) {
         }
     } else if (warp < kEpiWarp0) {
         // ---------------- dequantize A, convert B ----------------
-        // Thread t owns the block of rows 4kq..4kq+3 x code bytes 8co..8co+7 of
-        // each item: kq = 8*(warp%2) + lane%8, co = 4*(warp/2) + lane/8, so the
-        // 16-byte stores of a warp (eight K-chunks x four column groups) hit
-        // every bank position once per wavefront.
-        const int t = threadIdx.x - kDqWarp0 * 32;
+        // Two groups of four warps take alternate items (group g: items g, g+2,
+        // ...; operand stage g), so two items are being expanded at once. In a
+        // group, thread t owns two blocks of rows 4kq..4kq+3 x code bytes
+        // 8co..8co+7 of its items: kq = 8*(warp%2) + lane%8, co = 4*(warp/2 + 2*pass)
+        // + lane/8, so the 16-byte stores of a warp (eight K-chunks x four column
+        // groups) hit every bank position once per wavefront.
+        static_assert(OS == 2, "one operand stage per dequantizing group");
+        constexpr int GT = kDqThreads / 2; // threads per group
+        const int g = (threadIdx.x - kDqWarp0 * 32) / GT;
+        const int t = (threadIdx.x - kDqWarp0 * 32) % GT;
         const int dw = t >> 5, dl = t & 31;
-        const int kq = 8 * (dw & 1) + (dl & 7), co = 4 * (dw >> 1) + (dl >> 3);
-        const int k0 = 4 * kq;                        // first W row of the block
+        const int kq = 8 * (dw & 1) + (dl & 7);
+        const int k0 = 4 * kq;                        // first W row of the blocks
         const int kch = (k0 & 31) >> 2;               // its 16-byte K-chunk within the 32-row atom
         const int kofs = (k0 >> 5) * 16384;           // its K atom
-        for (int j = 0; j < n; j++) {
-            const long long it = i0 + j;
-            const int unit = (int)(it % p.units);
-            bool ok = wait_bar(&cfull[j % CS], (j / CS) & 1, abort, p.status);
-            if (j >= OS) ok = wait_bar(&oempty[j % OS], ((j / OS) - 1) & 1, abort, p.status) && ok;
-            // B first: its global loads are in flight while A is built.
-            constexpr int BCH = NP * 16 / kDqThreads > 0 ? NP * 16 / kDqThreads : 1; // 16-byte chunks per thread
-            float xv[BCH][4];
+        // x of the group's next item is loaded one item ahead, into registers.
+        constexpr int BCH = NP * 16 / GT > 0 ? NP * 16 / GT : 1; // 16-byte chunks per thread
+        float xv[BCH][4];
+        auto load_x = [&](int unit) {
 #pragma unroll
             for (int i = 0; i < BCH; i++) {
-                const int idx = i * kDqThreads + t, m = idx >> 4, kc = idx & 15;
+                const int idx = i * GT + t, m = idx >> 4, kc = idx & 15;
+                const int row = unit * kRows + kc * 4;
+                const bool mv = idx < NP * 16 && m < p.m;
+                if (p.xvec && mv && row + 3 < p.rows) {
+                    const float4 v = __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)m * p.rows + row));
+                    xv[i][0] = v.x, xv[i][1] = v.y, xv[i][2] = v.z, xv[i][3] = v.w;
+                } else {
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int row = unit * kRows + kc * 4 + e;
-                    xv[i][e] = (idx < NP * 16 && m < p.m && row < p.rows) ? __ldg(p.x + (size_t)m * p.rows + row) : 0.f;
+                    for (int e = 0; e < 4; e++)
+                        xv[i][e] = (mv && row + e < p.rows) ? __ldg(p.x + (size_t)m * p.rows + row + e) : 0.f;
                 }
             }
+        };
+        if (g < n) load_x((int)((i0 + g) % p.units));
+        for (int j = g; j < n; j += 2) {
+            bool ok = wait_bar(&cfull[j % CS], (j / CS) & 1, abort, p.status);
+            if (j >= OS) ok = wait_bar(&oempty[j % OS], ((j / OS) - 1) & 1, abort, p.status) && ok;
             uint8_t *A = ostage(j);
             uint8_t *B = A + C::A_BYTES;
             if (ok) {
                 const uint8_t *cs = cstage(j);
                 const float *sc = reinterpret_cast<const float *>(cs + kItem);
+#pragma unroll 1
+                for (int pass = 0; pass < 2; pass++) {
+                const int co = 4 * ((dw >> 1) + 2 * pass) + (dl >> 3);
                 float s_lo[8], s_hi[8];
+                if (BITS == 4) {
 #pragma unroll
-                for (int q = 0; q < 2; q++) {
-                    const float4 a = reinterpret_cast<const float4 *>(sc + co * 8)[q];
-                    s_lo[4 * q] = a.x, s_lo[4 * q + 1] = a.y, s_lo[4 * q + 2] = a.z, s_lo[4 * q + 3] = a.w;
-                    if (BITS == 4) {
+                    for (int q = 0; q < 2; q++) {
+                        const float4 a = reinterpret_cast<const float4 *>(sc + co * 8)[q];
+                        s_lo[4 * q] = a.x, s_lo[4 * q + 1] = a.y, s_lo[4 * q + 2] = a.z, s_lo[4 * q + 3] = a.w;
                         const float4 b = reinterpret_cast<const float4 *>(sc + kCols + co * 8)[q];
                         s_hi[4 * q] = b.x, s_hi[4 * q + 1] = b.y, s_hi[4 * q + 2] = b.z, s_hi[4 * q + 3] = b.w;
                     }
@@ -271,43 +289,48 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmParams p) {
                     const int adr = kofs + (nn >> 3) * 1024 + (nn & 7) * 128 + ((kch ^ (nn & 7)) << 4);
                     uint4 o;
                     if (BITS == 8) {
+                        // the code itself (exact in tf32); the column scale is applied to the sum
                         const uint32_t tt = g ^ 0x80808080u; // signed byte b -> b + 128
-                        o.x = to_tf32((magic_byte(tt, 0) - 8388736.0f) * s_lo[jc]);
-                        o.y = to_tf32((magic_byte(tt, 1) - 8388736.0f) * s_lo[jc]);
-                        o.z = to_tf32((magic_byte(tt, 2) - 8388736.0f) * s_lo[jc]);
-                        o.w = to_tf32((magic_byte(tt, 3) - 8388736.0f) * s_lo[jc]);
+                        const float2 off = make_float2(-8388736.0f, -8388736.0f); // 2^23 + 128
+                        const float2 c01 = __fadd2_rn(make_float2(magic_byte(tt, 0), magic_byte(tt, 1)), off);
+                        const float2 c23 = __fadd2_rn(make_float2(magic_byte(tt, 2), magic_byte(tt, 3)), off);
+                        o = make_uint4(__float_as_uint(c01.x), __float_as_uint(c01.y), __float_as_uint(c23.x),
+                                       __float_as_uint(c23.y));
                         *reinterpret_cast<uint4 *>(A + adr) = o;
                     } else {
+                        // (nibble - 8) * group scale, rounded to tf32
                         const uint32_t lo = g & 0x0F0F0F0Fu, hi = (g >> 4) & 0x0F0F0F0Fu;
-                        o.x = to_tf32((magic_byte(lo, 0) - 8388616.0f) * s_lo[jc]);
-                        o.y = to_tf32((magic_byte(lo, 1) - 8388616.0f) * s_lo[jc]);
-                        o.z = to_tf32((magic_byte(lo, 2) - 8388616.0f) * s_lo[jc]);
-                        o.w = to_tf32((magic_byte(lo, 3) - 8388616.0f) * s_lo[jc]);
+                        const float2 off = make_float2(-8388616.0f, -8388616.0f); // 2^23 + 8
+                        const float2 sl = make_float2(s_lo[jc], s_lo[jc]), sh = make_float2(s_hi[jc], s_hi[jc]);
+                        float2 a = __fmul2_rn(__fadd2_rn(make_float2(magic_byte(lo, 0), magic_byte(lo, 1)), off), sl);
+                        float2 b = __fmul2_rn(__fadd2_rn(make_float2(magic_byte(lo, 2), magic_byte(lo, 3)), off), sl);
+                        o = make_uint4(tf32_rna_bits(a.x), tf32_rna_bits(a.y), tf32_rna_bits(b.x), tf32_rna_bits(b.y));
                         *reinterpret_cast<uint4 *>(A + adr) = o;
-                        o.x = to_tf32((magic_byte(hi, 0) - 8388616.0f) * s_hi[jc]);
-                        o.y = to_tf32((magic_byte(hi, 1) - 8388616.0f) * s_hi[jc]);
-                        o.z = to_tf32((magic_byte(hi, 2) - 8388616.0f) * s_hi[jc]);
-                        o.w = to_tf32((magic_byte(hi, 3) - 8388616.0f) * s_hi[jc]);
+                        a = __fmul2_rn(__fadd2_rn(make_float2(magic_byte(hi, 0), magic_byte(hi, 1)), off), sh);
+                        b = __fmul2_rn(__fadd2_rn(make_float2(magic_byte(hi, 2), magic_byte(hi, 3)), off), sh);
+                        o = make_uint4(tf32_rna_bits(a.x), tf32_rna_bits(a.y), tf32_rna_bits(b.x), tf32_rna_bits(b.y));
                         *reinterpret_cast<uint4 *>(A + C::RUN + adr) = o;
                     }
                 }
+                } // pass
 #pragma unroll
                 for (int i = 0; i < BCH; i++) {
-                    const int idx = i * kDqThreads + t, m = idx >> 4, kc = idx & 15;
+                    const int idx = i * GT + t, m = idx >> 4, kc = idx & 15;
                     if (idx < NP * 16) {
                         const int r = m & 7;
                         uint4 o;
-                        o.x = to_tf32(xv[i][0]);
-                        o.y = to_tf32(xv[i][1]);
-                        o.z = to_tf32(xv[i][2]);
-                        o.w = to_tf32(xv[i][3]);
+                        o.x = tf32_rna_bits(xv[i][0]);
+                        o.y = tf32_rna_bits(xv[i][1]);
+                        o.z = tf32_rna_bits(xv[i][2]);
+                        o.w = tf32_rna_bits(xv[i][3]);
                         *reinterpret_cast<uint4 *>(B + (kc >> 3) * (NP * 128) + (m >> 3) * 1024 + r * 128 +
                                                    (((kc & 7) ^ r) << 4)) = o;
                     }
                 }
             }
+            if (j + 2 < n) load_x((int)((i0 + j + 2) % p.units)); // in flight across the next item's waits
             fence_proxy_async(); // generic-proxy writes of A and B become visible to the tensor cores
-            named_sync(1, kDqThreads);
+            named_sync(1 + 2 * g, GT); // barriers 1 and 3 (2 is the epilogue's)
             if (t == 0) {
                 mbar_arrive(&ofull[j % OS]);
                 mbar_arrive(&cempty[j % CS]);
@@ -333,6 +356,9 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmParams p) {
             tc_fence_after();
             float *dst = p.partial + (size_t)(2 * c + (i0 >= t0 ? 0 : 1)) * SL;
             const int base = tile * kCols + col; // byte column of this thread in the reference row
+            // int8: sum x*code, then times the column scale (quant.go:120); shared
+            // tiles are scaled after their cross-CTA sum.
+            const float cscale = BITS == 8 && base < p.cols ? __ldg(p.scale + base) : 1.f;
 #pragma unroll
             for (int h = 0; h < H; h++) {
                 const int gcol = BITS == 8 ? base : (h == 0 ? base : p.half + base);
@@ -349,50 +375,13 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmParams p) {
                         if (shared)
                             dst[(h * NP + m) * kCols + col] = f;
                         else if (cvalid && m < p.m)
-                            p.out[(size_t)m * p.cols + gcol] = f;
+                            p.out[(size_t)m * p.cols + gcol] = BITS == 8 ? f * cscale : f;
                     }
                 }
             }
             tc_fence_before();
             named_sync(2, 128);
             if (et == 0) mbar_arrive(&accempty[b]); // accumulator buffer b is free again
-            if (shared) {
-                if (et == 0) {
-                    // The barrier orders the partial stores of all 128 threads before
-                    // this thread's fence (cumulativity); the fence publishes them.
-                    __threadfence();
-                    const unsigned prev = atomicAdd(&p.counters[tile], 1u);
-                    *lastflag = prev == (unsigned)(cl - cf);
-                    if (*lastflag) p.counters[tile] = 0; // every contributor arrived: re-arm
-                }
-                named_sync(2, 128);
-                if (*lastflag) {
-                    __threadfence();
-#pragma unroll
-                    for (int h = 0; h < H; h++) {
-                        const int gcol = BITS == 8 ? base : (h == 0 ? base : p.half + base);
-                        const bool cvalid = BITS == 8 ? base < p.cols : base < p.half;
-#pragma unroll 1
-                        for (int m = 0; m < p.m && m < NP; m++) {
-                            float sum = 0.f;
-                            for (int c2 = cf; c2 <= cl; c2 += 4) { // contributors in CTA order, 4 loads in flight
-                                float pv[4];
-#pragma unroll
-                                for (int u = 0; u < 4; u++) {
-                                    const int cu = c2 + u;
-                                    const int sl = 2 * cu + (cu <= cl && item_start(p.items, cu, G) >= t0 ? 0 : 1);
-                                    pv[u] = cu <= cl ? __ldcg(p.partial + (size_t)sl * SL + (h * NP + m) * kCols + col)
-                                                     : 0.f;
-                                }
-#pragma unroll
-                                for (int u = 0; u < 4; u++) sum += pv[u];
-                            }
-                            if (cvalid) p.out[(size_t)m * p.cols + gcol] = sum;
-                        }
-                    }
-                }
-                named_sync(2, 128); // lastflag is rewritten by the next segment
-            }
             s0 = s1;
         }
     }
@@ -404,6 +393,46 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmParams p) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(C::TCOLS) : "memory");
     }
+}
+
+// Sums the partial slots of every tile shared by several CTAs of mm_kernel,
+// contributors in CTA order, and writes those output columns (int8: times the
+// column scale). Block (tile, run h, rows 4z..4z+3), thread = tile column.
+template <int BITS, int NP>
+__global__ void __launch_bounds__(128) mm_reduce_kernel(MmParams p, int ctas) {
+    constexpr int H = BITS == 8 ? 1 : 2;
+    constexpr int SL = H * NP * kCols;
+    constexpr int RB = 4; // rows per block
+    const int tile = blockIdx.x, h = blockIdx.y, m0 = blockIdx.z * RB, col = threadIdx.x;
+    const long long t0 = (long long)tile * p.units, t1 = t0 + p.units;
+    int cf, cl;
+    tile_ctas(p.items, ctas, t0, t1, cf, cl);
+    if (cf == cl) return; // written by the tile's only CTA
+    const int b = tile * kCols + col;
+    if (!(BITS == 8 ? b < p.cols : b < p.half)) return;
+    const float cscale = BITS == 8 ? __ldg(p.scale + b) : 1.f;
+    float sum[RB];
+#pragma unroll
+    for (int r = 0; r < RB; r++) sum[r] = 0.f;
+    for (int c2 = cf; c2 <= cl; c2 += 8) { // contributors in CTA order, 8 x RB loads in flight
+        float pv[8][RB];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int cu = c2 + u;
+            const int sl = 2 * cu + (cu <= cl && item_start(p.items, cu, ctas) >= t0 ? 0 : 1);
+            const float *src = p.partial + (size_t)sl * SL + (size_t)(h * NP + m0) * kCols + col;
+#pragma unroll
+            for (int r = 0; r < RB; r++) pv[u][r] = cu <= cl && m0 + r < p.m ? __ldcg(src + r * kCols) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+#pragma unroll
+            for (int r = 0; r < RB; r++) sum[r] += pv[u][r];
+    }
+    const int gcol = BITS == 8 || h == 0 ? b : p.half + b;
+#pragma unroll
+    for (int r = 0; r < RB; r++)
+        if (m0 + r < p.m) p.out[(size_t)(m0 + r) * p.cols + gcol] = BITS == 8 ? sum[r] * cscale : sum[r];
 }
 
 template <int BITS, int NP>
@@ -429,7 +458,6 @@ cudaError_t launch_mm(const TqMatrixDev &mat, const float *x, float *out, int M,
     prm.x = x;
     prm.out = out;
     prm.partial = scr.mm_partial;
-    prm.counters = scr.counters;
     prm.status = scr.status;
     prm.rows = mat.rows;
     prm.cols = mat.cols;
@@ -437,11 +465,15 @@ cudaError_t launch_mm(const TqMatrixDev &mat, const float *x, float *out, int M,
     prm.units = mat.units;
     prm.tiles = mat.tiles;
     prm.m = M;
+    prm.xvec = (mat.rows % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     prm.items = (long long)mat.tiles * mat.units;
     const int sms = sm_count[dev];
     if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS || !scr.mm_partial) return cudaErrorInvalidValue;
     const int ctas = (int)(prm.items < sms ? prm.items : sms);
     mm_kernel<BITS, NP><<<ctas, kThreads, C::SMEM, st>>>(prm);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || ctas == 1) return e;
+    mm_reduce_kernel<BITS, NP><<<dim3(mat.tiles, C::H, (M + 3) / 4), 128, 0, st>>>(prm, ctas);
     return cudaGetLastError();
 }
 
@@ -450,13 +482,12 @@ cudaError_t mm_dispatch(const TqMatrixDev &mat, const float *x, float *out, int 
                         cudaStream_t st) {
     if (M <= 16) return launch_mm<BITS, 16>(mat, x, out, M, scr, st);
     if (M <= 32) return launch_mm<BITS, 32>(mat, x, out, M, scr, st);
-    if (M <= 64) return launch_mm<BITS, 64>(mat, x, out, M, scr, st);
-    return launch_mm<BITS, 128>(mat, x, out, M, scr, st);
+    return launch_mm<BITS, 64>(mat, x, out, M, scr, st);
 }
 
 } // namespace
 
-// out[M][cols] = x[M][rows] @ W on the tf32 tensor-core path, 128 activation
+// out[M][cols] = x[M][rows] @ W on the tf32 tensor-core path, 64 activation
 // rows per launch.
 cudaError_t tq_launch_mm(const TqMatrixDev &mat, const float *x, float *out, int M, const TqScratch &scr,
                          cudaStream_t st) {
