@@ -167,6 +167,42 @@ TQ_EXPORT int tq_synth_dev(float *out, size_t n, uint64_t seed, uint64_t stream_
  * pointer calls check this themselves and return TQ_ERR_TIMEOUT. */
 TQ_EXPORT int tq_device_status(unsigned *bits);
 
+/* ---- whole-model decode: GPT-2 (int8 decode weights) ----------------------- */
+
+/* Shape of a GPT-2 model (_example/gpt2/model.go:17-24): layers, heads,
+ * embedding width d (head size d/n_head must be 64: the example divides the
+ * scores by 8), MLP width, vocabulary, context length. */
+typedef struct {
+    int n_layer, n_head, d, ffn, vocab, ctx;
+} tq_gpt2_config;
+
+/* Builds a random-init GPT-2 on the current device: every matrix and
+ * embedding drawn from the tq_synth_dev generator with standard deviation
+ * sigma (streams: wte 1, wpe 2, layer l: c_attn 16+8l, attn c_proj 17+8l,
+ * mlp c_fc 18+8l, mlp c_proj 19+8l), layer-norm weights 1, biases 0. Keeps
+ * the fp32 weights for the prefill and their QuantizeMatrix int8 twins for
+ * decode (gpt2.quantize, model.go:51-60), plus a fp32 KV cache of ctx
+ * positions, all resident. Replaces loadModel + quantize (model.go:79-133)
+ * for synthetic weights. */
+TQ_EXPORT int tq_gpt2_create(const tq_gpt2_config *cfg, uint64_t seed, float sigma, uint64_t *model);
+
+/* Greedy generation (main.go:163-170 at temperature 0): prefill of the
+ * n_prompt ids with the fp32 weights (model.go:361-401), then n_gen - 1 int8
+ * decode steps (model.go:179-245); tokens[0..n_gen) receives the generated
+ * ids (argmax, ties to the lowest id, main.go:69-77). times_ms (optional,
+ * 2 floats): device time of the prefill and of the decode steps. Starts a
+ * fresh sequence every call. n_prompt + n_gen - 1 must not exceed ctx. */
+TQ_EXPORT int tq_gpt2_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen, int *tokens,
+                               float *times_ms);
+
+/* Releases a model (a second call is a no-op). */
+TQ_EXPORT int tq_gpt2_free(uint64_t model);
+
+/* Seeded uniform token ids in [0, vocab) on the host: id i =
+ * mix64(key + (i+1)*0x9E3779B97F4A7C15) % vocab with the generator key of
+ * (seed, stream 3). A stand-in for a tokenized prompt. */
+TQ_EXPORT int tq_synth_tokens(int *out, int n, int vocab, uint64_t seed);
+
 /* ---- host-side fault injection (tests) ------------------------------------ */
 
 /* Makes the next n device allocations made by this library fail with

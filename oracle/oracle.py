@@ -9,6 +9,7 @@ The functions restate mattn/tensai's Go code (file:line in tq_oracle.c):
   quantize4   -> QuantizeMatrix4           quant4.go:28-89
   q8_matmul   -> (*QMatrix).MatVec         quant.go:77-103 (+ :108-122 / quant_simd.go:12-48)
   q4_matmul   -> (*Q4Matrix).MatVec        quant4.go:93-119 (+ :126-154 / quant4_simd.go:17-57)
+  gpt2_generate -> GPT-2 -q8 greedy loop   _example/gpt2/model.go:179-401, main.go:69-77,163-170
 """
 from __future__ import annotations
 
@@ -54,6 +55,10 @@ def lib():
         L.tqo_q8_matmul.restype = None
         L.tqo_q4_matmul.argtypes = [P, P, I, I, P, P, I, I]
         L.tqo_q4_matmul.restype = None
+        L.tqo_gpt2_generate.argtypes = [P, U64, F, P, I, I, P, P, P]
+        L.tqo_gpt2_generate.restype = I
+        L.tqo_synth_tokens.argtypes = [P, I, I, U64]
+        L.tqo_synth_tokens.restype = None
         _lib = L
     return _lib
 
@@ -149,3 +154,33 @@ def unpack4(q, rows, cols) -> np.ndarray:
     half = cols // 2
     B = q[: rows * half].reshape(rows, half)
     return np.concatenate([(B & 0x0F).astype(np.int8) - 8, (B >> 4).astype(np.int8) - 8], axis=1)
+
+
+class Gpt2Cfg(ctypes.Structure):
+    _fields_ = [("n_layer", ctypes.c_int), ("n_head", ctypes.c_int), ("d", ctypes.c_int), ("ffn", ctypes.c_int),
+                ("vocab", ctypes.c_int), ("ctx", ctypes.c_int)]
+
+
+GPT2_SMALL = dict(n_layer=12, n_head=12, d=768, ffn=3072, vocab=50257, ctx=1024)
+
+
+def synth_tokens(n: int, vocab: int, seed: int) -> np.ndarray:
+    """Seeded uniform token ids in [0, vocab) (a stand-in for a tokenized prompt)."""
+    out = np.empty(n, np.int32)
+    lib().tqo_synth_tokens(_p(out), n, vocab, seed)
+    return out
+
+
+def gpt2_generate(cfg: dict, seed: int, sigma: float, prompt, n_gen: int):
+    """Greedy GPT-2 generation with int8 decode weights on the CPU: returns
+    (token ids [n_gen], top-1 margins [n_gen], prefill logits [vocab])."""
+    c = Gpt2Cfg(**cfg)
+    prompt = np.ascontiguousarray(prompt, np.int32)
+    toks = np.empty(n_gen, np.int32)
+    margins = np.empty(n_gen, np.float32)
+    first = np.empty(cfg["vocab"], np.float32)
+    rc = lib().tqo_gpt2_generate(ctypes.byref(c), seed, sigma, _p(prompt), len(prompt), n_gen, _p(toks),
+                                 _p(margins), _p(first))
+    if rc != 0:
+        raise ValueError("tqo_gpt2_generate: bad configuration")
+    return toks, margins, first

@@ -148,6 +148,9 @@ static void pool_run(tqo_task_fn fn, void *arg, int ntasks) {
     pthread_mutex_unlock(&g_pool.mu);
 }
 
+/* The pool for the model restatements (tq_model.c). */
+TQO_EXPORT void tqo_pool_run(void (*fn)(void *arg, int idx), void *arg, int ntasks) { pool_run(fn, arg, ntasks); }
+
 /* Fills out[0..n) from (seed, stream) with standard deviation sigma. The   */
 /* value of element i depends only on (seed, stream, i), never on threads.  */
 struct synth_job { float *out; size_t n; uint64_t key; float c; size_t per; };

@@ -52,6 +52,10 @@ SIGNATURES = {
     "tq_matmul_dev_fixed": (I, [U64, P, P, I, P]),
     "tq_synth_dev": (I, [P, SZ, U64, U64, F, P]),
     "tq_device_status": (I, [ctypes.POINTER(ctypes.c_uint)]),
+    "tq_gpt2_create": (I, [P, U64, F, PU64]),
+    "tq_gpt2_generate": (I, [U64, P, I, I, P, P]),
+    "tq_gpt2_free": (I, [U64]),
+    "tq_synth_tokens": (I, [P, I, I, U64]),
     "tq_set_matvec_kernel": (I, [I]),
     "tq_debug_fail_allocs": (I, [I]),
 }

@@ -130,6 +130,7 @@ static int scratch_for(int device, cudaStream_t st, TqScratch *out, int m = 1) {
 }
 
 // Reads and clears a scratch's status word (synchronous on st).
+cudaError_t tq_read_status(const TqScratch &scr, cudaStream_t st, unsigned *out);
 static cudaError_t read_status(const TqScratch &scr, cudaStream_t st, unsigned *out) {
     unsigned v = 0;
     cudaError_t e = cudaMemcpyAsync(&v, scr.status, sizeof v, cudaMemcpyDeviceToHost, st);
@@ -150,6 +151,15 @@ static cudaError_t launch_matvec(const TqMatrixDev &m, const float *x, float *ou
     if (M >= TQ_MM_MIN_ROWS) return tq_launch_mm(m, x, out, M, scr, st);
     return g_matvec_kernel.load() == 1 ? tq_launch_matvec(m, x, out, M, scr, st)
                                        : tq_launch_igemv(m, x, out, M, scr, st);
+}
+
+int tq_scratch_for(int device, cudaStream_t st, TqScratch *out, int m) { return scratch_for(device, st, out, m); }
+
+cudaError_t tq_read_status(const TqScratch &scr, cudaStream_t st, unsigned *out) { return read_status(scr, st, out); }
+
+cudaError_t tq_launch_matmul(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
+                             cudaStream_t st) {
+    return launch_matvec(m, x, out, M, scr, st);
 }
 
 static int ensure_stream(ThreadCtx *c) {
@@ -240,6 +250,12 @@ static void release_matrix(TqMatrixDev *m) {
     m->codes = nullptr;
     m->scale = nullptr;
 }
+
+int tq_alloc_matrix(int bits, int rows, int cols, TqMatrixDev *m, cudaStream_t st) {
+    int rc = check_dims(bits, rows, cols);
+    return rc ? rc : alloc_matrix(bits, rows, cols, m, st);
+}
+void tq_release_matrix(TqMatrixDev *m) { release_matrix(m); }
 
 static uint64_t register_handle(int device, const TqMatrixDev &m) {
     auto h = std::make_shared<Handle>();
@@ -529,6 +545,12 @@ int tq_synth_dev(float *out, size_t n, uint64_t seed, uint64_t stream_id, float 
     if (!out && n) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
     cudaError_t e = tq_launch_synth(out, n, seed, stream_id, sigma, (cudaStream_t)cuda_stream);
     return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "synth launch");
+}
+
+int tq_synth_tokens(int *out, int n, int vocab, uint64_t seed) {
+    if (n < 0 || vocab < 1 || (n && !out)) return tq_fail(TQ_ERR_ARG, "tensai: bad token synthesis arguments");
+    tq_host_synth_tokens(out, n, vocab, seed);
+    return TQ_OK;
 }
 
 int tq_device_status(unsigned *bits) {

@@ -22,3 +22,16 @@ int tq_cuda_fail(cudaError_t e, const char *what);
 cudaError_t tq_dev_malloc(void **p, size_t bytes);
 // Looks a handle up; on failure *rc holds TQ_ERR_HANDLE and the message is set.
 std::shared_ptr<Handle> tq_lookup_checked(uint64_t h, int *rc);
+// The matvec scratch of (device, stream), created on first use (with the
+// M >= 16 matmul partials when m >= TQ_MM_MIN_ROWS). Not inside a capture.
+int tq_scratch_for(int device, cudaStream_t st, TqScratch *out, int m);
+// out[M][cols] = x @ W with the kernel the library would pick for M rows.
+cudaError_t tq_launch_matmul(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
+                             cudaStream_t st);
+// A zeroed device matrix (shape checked) on the current device / its release.
+int tq_alloc_matrix(int bits, int rows, int cols, TqMatrixDev *m, cudaStream_t st);
+void tq_release_matrix(TqMatrixDev *m);
+// Reads and clears a scratch's status word, ORing it into *out (synchronous on st).
+cudaError_t tq_read_status(const TqScratch &scr, cudaStream_t st, unsigned *out);
+// Seeded uniform token ids on the host (tq_quantize.cu).
+void tq_host_synth_tokens(int *out, int n, int vocab, uint64_t seed);

@@ -41,6 +41,12 @@ __global__ void tq_synth_kernel(float *__restrict__ out, size_t n, uint64_t key,
     }
 }
 
+// Seeded uniform token ids (host): id i = mix64(key + (i+1)*gamma) % vocab.
+void tq_host_synth_tokens(int *out, int n, int vocab, uint64_t seed) {
+    const uint64_t key = tq_synth_key(seed, 3);
+    for (int i = 0; i < n; i++) out[i] = (int)(tq_mix64(key + (uint64_t)(i + 1) * TQ_GAMMA) % (uint64_t)vocab);
+}
+
 cudaError_t tq_launch_synth(float *out, size_t n, uint64_t seed, uint64_t stream, float sigma, cudaStream_t st) {
     if (n == 0) return cudaSuccess;
     size_t blocks = (n + 255) / 256;
