@@ -265,6 +265,34 @@ def measure_side_configs(L, Q, torch, stream, peak):
     return out
 
 
+GPT2_PROMPT, GPT2_GEN = 128, 256
+
+
+def measure_gpt2(cpu: bool):
+    """GPT-2-small int8 greedy decode (128-token prompt, 256 tokens): device
+    time of the fp32 prefill and of the 255 decode steps (one CUDA graph per
+    token). With cpu=True also the oracle's decode rate on the host cores over
+    a bounded 32-token sample."""
+    from tensai_b200.decode import GPT2_SMALL, Gpt2, synth_tokens
+    prompt = synth_tokens(GPT2_PROMPT, GPT2_SMALL["vocab"], 1)
+    with Gpt2(GPT2_SMALL, 1) as m:
+        m.generate(prompt, 16)  # warm-up: kernel set-up and the step graph
+        m.generate(prompt, GPT2_GEN)
+        pre_ms, dec_ms = m.last_times_ms
+    rec = {"decode_tok_s": round((GPT2_GEN - 1) / (dec_ms * 1e-3), 1), "ms_per_token": round(dec_ms / (GPT2_GEN - 1), 4),
+           "prefill_ms": round(pre_ms, 3), "prompt": GPT2_PROMPT, "generated": GPT2_GEN,
+           "algorithmic_bytes_per_token": "124,064,836 + 73,728 x cached positions",
+           "weights": "random-init N(0, 0.02), int8 QuantizeMatrix decode weights, fp32 prefill"}
+    if cpu:
+        from oracle import oracle as O
+        secs = [0.0, 0.0]
+        O.gpt2_generate(O.GPT2_SMALL, 1, 0.02, prompt, 33, seconds=secs)
+        rec["cpu_baseline"] = {"decode_tok_s": round(32 / secs[1], 2), "cores": O.set_threads(0), "kind": "port",
+                               "sample": "32 decode steps after the 128-token prompt, oracle restatement of the "
+                                         "-q8 loop (AVX2 int8 MatVec, float64 attention)"}
+    return rec
+
+
 def _check_rc(L, rc):
     if rc:
         raise RuntimeError(L.tq_last_error().decode())
@@ -390,6 +418,7 @@ def run_gpu(args, rank: int, world: int):
     side = None
     if rank == 0 and not args.no_side_configs:
         side = measure_side_configs(L, Q, torch, stream, load_peak()[0])
+        side["C4 GPT-2-small int8 greedy decode"] = measure_gpt2(world == 1 and not args.no_cpu_baseline)
     if rank == 0:
         peak, peak_src = load_peak()
         per_launch = pair_bytes() / 2  # up and down carry the same algorithmic bytes

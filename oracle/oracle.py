@@ -55,7 +55,7 @@ def lib():
         L.tqo_q8_matmul.restype = None
         L.tqo_q4_matmul.argtypes = [P, P, I, I, P, P, I, I]
         L.tqo_q4_matmul.restype = None
-        L.tqo_gpt2_generate.argtypes = [P, U64, F, P, I, I, P, P, P]
+        L.tqo_gpt2_generate.argtypes = [P, U64, F, P, I, I, P, P, P, P]
         L.tqo_gpt2_generate.restype = I
         L.tqo_synth_tokens.argtypes = [P, I, I, U64]
         L.tqo_synth_tokens.restype = None
@@ -171,16 +171,20 @@ def synth_tokens(n: int, vocab: int, seed: int) -> np.ndarray:
     return out
 
 
-def gpt2_generate(cfg: dict, seed: int, sigma: float, prompt, n_gen: int):
+def gpt2_generate(cfg: dict, seed: int, sigma: float, prompt, n_gen: int, seconds=None):
     """Greedy GPT-2 generation with int8 decode weights on the CPU: returns
-    (token ids [n_gen], top-1 margins [n_gen], prefill logits [vocab])."""
+    (token ids [n_gen], top-1 margins [n_gen], prefill logits [vocab]); if
+    `seconds` is a list it receives the prefill and decode wall times."""
     c = Gpt2Cfg(**cfg)
     prompt = np.ascontiguousarray(prompt, np.int32)
     toks = np.empty(n_gen, np.int32)
     margins = np.empty(n_gen, np.float32)
     first = np.empty(cfg["vocab"], np.float32)
+    secs = np.zeros(2, np.float64)
     rc = lib().tqo_gpt2_generate(ctypes.byref(c), seed, sigma, _p(prompt), len(prompt), n_gen, _p(toks),
-                                 _p(margins), _p(first))
+                                 _p(margins), _p(first), _p(secs))
     if rc != 0:
         raise ValueError("tqo_gpt2_generate: bad configuration")
+    if seconds is not None:
+        seconds[:] = [float(secs[0]), float(secs[1])]
     return toks, margins, first

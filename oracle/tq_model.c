@@ -23,6 +23,7 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include "tq_oracle.h"
 
@@ -309,16 +310,25 @@ static void gpt2_free(gpt2 *m) {
  * The generation loop of main.go:163-170 at temperature 0: prefill the
  * prompt, then n_gen times pick the argmax and feed it back. tokens[i] is
  * the i-th generated id; margins[i] its logit lead over the runner-up;
- * first_logits (optional, vocab floats) the prefill logits. Returns 0, or -1
- * on bad arguments.
+ * first_logits (optional, vocab floats) the prefill logits; seconds
+ * (optional, 2 doubles) the wall time of the prefill and of the n_gen - 1
+ * decode steps. Returns 0, or -1 on bad arguments.
  */
+static double now_s(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
 TQO_EXPORT int tqo_gpt2_generate(const tqo_gpt2_cfg *c, uint64_t seed, float sigma, const int *prompt, int n_prompt,
-                                 int n_gen, int *tokens, float *margins, float *first_logits) {
+                                 int n_gen, int *tokens, float *margins, float *first_logits, double *seconds) {
     /* the attention scale is the reference's literal 1/8 = 1/sqrt(64) */
     if (!c || n_prompt < 1 || n_prompt + n_gen > c->ctx + 1 || c->d % c->n_head || c->d / c->n_head != 64) return -1;
     gpt2 *m = gpt2_new(c, seed, sigma);
     float *logits = malloc(sizeof(float) * (size_t)c->vocab);
+    const double t0 = now_s();
     gpt2_prefill(m, prompt, n_prompt, logits);
+    const double t1 = now_s();
     if (first_logits) memcpy(first_logits, logits, sizeof(float) * (size_t)c->vocab);
     int pos = n_prompt;
     for (int i = 0; i < n_gen; i++) {
@@ -326,6 +336,7 @@ TQO_EXPORT int tqo_gpt2_generate(const tqo_gpt2_cfg *c, uint64_t seed, float sig
         tokens[i] = next;
         if (i + 1 < n_gen) gpt2_step(m, next, pos++, logits);
     }
+    if (seconds) seconds[0] = t1 - t0, seconds[1] = now_s() - t1; /* prefill, decode steps */
     free(logits);
     gpt2_free(m);
     return 0;
