@@ -198,6 +198,48 @@ TQ_EXPORT int tq_gpt2_generate(uint64_t model, const int *prompt, int n_prompt, 
 /* Releases a model (a second call is a no-op). */
 TQ_EXPORT int tq_gpt2_free(uint64_t model);
 
+/* ---- whole-model decode: Qwen2 (int4 weights), tensor parallel ------------- */
+
+/* Shape of a Qwen2 model (_example/qwen/model.go:20-32): layers, query and
+ * KV heads (grouped-query attention; head size d/n_head, even), hidden
+ * width d, MLP width, vocabulary, context length, RMSNorm epsilon, RoPE
+ * theta. The lm head is untied. */
+typedef struct {
+    int n_layer, n_head, n_kv, d, ffn, vocab, ctx;
+    double eps, theta;
+} tq_qwen_config;
+
+#define TQ_NCCL_ID_BYTES 128
+
+/* Writes a fresh NCCL unique id (TQ_NCCL_ID_BYTES bytes) for
+ * tq_qwen_create: rank 0 makes it and every rank receives a copy. */
+TQ_EXPORT int tq_nccl_unique_id(void *id);
+
+/* Builds this rank's shard of a random-init Qwen2 on the current device
+ * (one process per GPU; all ranks call it together when world > 1): every
+ * matrix in the reference's [in, out] orientation drawn from the
+ * tq_synth_dev generator with standard deviation sigma (streams: embedding
+ * 1, lm head 2, layer l: q 32+16l, k +1, v +2, o +3, gate +4, up +5,
+ * down +6), norm weights 1, biases 0, quantized with QuantizeMatrix4 per
+ * shard (quantizeMat, model.go:40-52). q/k/v and gate/up are column-sharded,
+ * o_proj and down row-sharded on 64-row groups, the lm head column-sharded;
+ * world must divide or be a multiple of n_kv, and d/world, ffn/world be
+ * multiples of 64. nccl_id: from tq_nccl_unique_id (NULL when world == 1).
+ * Replaces loadQwen (model.go:95-177) for synthetic weights. */
+TQ_EXPORT int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sigma, int rank, int world,
+                             const void *nccl_id, uint64_t *model);
+
+/* Greedy generation (main.go:225-240 at temperature 0, no end-of-turn
+ * stop): the prompt through the decode step one token at a time, then n_gen
+ * greedy tokens into tokens[0..n_gen). Collective over the ranks of a
+ * tensor-parallel model. times_ms (optional, 2 floats): device time of the
+ * prompt steps and of the n_gen - 1 later steps. */
+TQ_EXPORT int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen, int *tokens,
+                               float *times_ms);
+
+/* Releases a model and its NCCL communicator (a second call is a no-op). */
+TQ_EXPORT int tq_qwen_free(uint64_t model);
+
 /* Seeded uniform token ids in [0, vocab) on the host: id i =
  * mix64(key + (i+1)*0x9E3779B97F4A7C15) % vocab with the generator key of
  * (seed, stream 3). A stand-in for a tokenized prompt. */

@@ -10,6 +10,7 @@ The functions restate mattn/tensai's Go code (file:line in tq_oracle.c):
   q8_matmul   -> (*QMatrix).MatVec         quant.go:77-103 (+ :108-122 / quant_simd.go:12-48)
   q4_matmul   -> (*Q4Matrix).MatVec        quant4.go:93-119 (+ :126-154 / quant4_simd.go:17-57)
   gpt2_generate -> GPT-2 -q8 greedy loop   _example/gpt2/model.go:179-401, main.go:69-77,163-170
+  qwen_generate -> Qwen2 -q4 greedy loop   _example/qwen/model.go:182-307, main.go:225-240
 """
 from __future__ import annotations
 
@@ -57,6 +58,8 @@ def lib():
         L.tqo_q4_matmul.restype = None
         L.tqo_gpt2_generate.argtypes = [P, U64, F, P, I, I, P, P, P, P]
         L.tqo_gpt2_generate.restype = I
+        L.tqo_qwen_generate.argtypes = [P, U64, F, P, I, I, P, P, P, P]
+        L.tqo_qwen_generate.restype = I
         L.tqo_synth_tokens.argtypes = [P, I, I, U64]
         L.tqo_synth_tokens.restype = None
         _lib = L
@@ -188,3 +191,31 @@ def gpt2_generate(cfg: dict, seed: int, sigma: float, prompt, n_gen: int, second
     if seconds is not None:
         seconds[:] = [float(secs[0]), float(secs[1])]
     return toks, margins, first
+
+
+class QwenCfg(ctypes.Structure):
+    _fields_ = [("n_layer", ctypes.c_int), ("n_head", ctypes.c_int), ("n_kv", ctypes.c_int), ("d", ctypes.c_int),
+                ("ffn", ctypes.c_int), ("vocab", ctypes.c_int), ("ctx", ctypes.c_int), ("eps", ctypes.c_double),
+                ("theta", ctypes.c_double)]
+
+
+QWEN_7B = dict(n_layer=28, n_head=28, n_kv=4, d=3584, ffn=18944, vocab=152064, ctx=2560, eps=1e-6, theta=1e6)
+
+
+def qwen_generate(cfg: dict, seed: int, sigma: float, prompt, n_gen: int, seconds=None, prompt_logits=False):
+    """Greedy Qwen2 generation with int4 weights on the CPU, the prompt fed
+    token by token: returns (token ids [n_gen], top-1 margins [n_gen]) and,
+    with prompt_logits=True, also the logits after the last prompt token."""
+    c = QwenCfg(**cfg)
+    prompt = np.ascontiguousarray(prompt, np.int32)
+    toks = np.empty(n_gen, np.int32)
+    margins = np.empty(n_gen, np.float32)
+    secs = np.zeros(2, np.float64)
+    logits = np.empty(cfg["vocab"], np.float32)
+    rc = lib().tqo_qwen_generate(ctypes.byref(c), seed, sigma, _p(prompt), len(prompt), n_gen, _p(toks),
+                                 _p(margins), _p(secs), _p(logits))
+    if rc != 0:
+        raise ValueError("tqo_qwen_generate: bad configuration")
+    if seconds is not None:
+        seconds[:] = [float(secs[0]), float(secs[1])]
+    return (toks, margins, logits) if prompt_logits else (toks, margins)

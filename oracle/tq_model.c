@@ -355,3 +355,215 @@ TQO_EXPORT void tqo_synth_tokens(int *out, int n, int vocab, uint64_t seed) {
         out[i] = (int)(z % (uint64_t)vocab);
     }
 }
+
+/* ======================================================================== */
+/* Qwen2 (_example/qwen/model.go:182-307, main.go:225-240) with int4        */
+/* (QuantizeMatrix4) weights: RMSNorm, half-split RoPE, grouped-query       */
+/* attention, SwiGLU, untied lm head; the prompt is fed token by token      */
+/* through step, as main.go:229-231 does. Random init: matrices in the     */
+/* reference's [in, out] orientation from the shared generator (embed 1,    */
+/* lm head 2, layer l: q 32+16l, k +1, v +2, o +3, gate +4, up +5, down +6),  */
+/* norm weights 1, biases 0.                                                */
+/* ======================================================================== */
+
+typedef struct {
+    int n_layer, n_head, n_kv, d, ffn, vocab, ctx;
+    double eps, theta;
+} tqo_qwen_cfg;
+
+typedef struct {
+    uint8_t *q; /* QuantizeMatrix4 codes (+16 pad) */
+    float *scale;
+    int rows, cols;
+} q4mat;
+
+typedef struct {
+    q4mat wq, wk, wv, wo, gate, up, down;
+    float *ln1, *ln2, *bq, *bk, *bv;
+    float *kc, *vc; /* [ctx][n_kv * hd] */
+} qwblock;
+
+typedef struct {
+    tqo_qwen_cfg c;
+    int hd, kvd;
+    float *embed, *normw;
+    q4mat lm;
+    qwblock *b;
+} qwen;
+
+static void q4_init(q4mat *m, uint64_t seed, uint64_t stream, float sigma, int rows, int cols) {
+    float *w = synth((size_t)rows * cols, seed, stream, sigma);
+    m->rows = rows, m->cols = cols;
+    m->q = calloc((size_t)rows * (cols / 2) + 16, 1);
+    m->scale = zeros((size_t)((rows + 63) / 64) * cols);
+    tqo_quantize4(w, rows, cols, m->q, m->scale); /* quantizeMat(.., 4), model.go:40-52 */
+    free(w);
+}
+
+static void q4_mv(const q4mat *m, const float *x, float *out) {
+    tqo_q4_matmul(m->q, m->scale, m->rows, m->cols, x, out, 1, TQO_AVX2_VARIANT);
+}
+
+/* rmsnorm, model.go:182-193. */
+static void rmsnorm(const float *x, const float *w, int n, double eps, float *out) {
+    double ss = 0;
+    for (int i = 0; i < n; i++) ss += (double)x[i] * (double)x[i];
+    double inv = 1 / sqrt(ss / (double)n + eps);
+    for (int i = 0; i < n; i++) out[i] = (float)((double)x[i] * inv) * w[i];
+}
+
+/* rope, model.go:219-229: rotate pairs (i, i + hd/2) of one head. */
+static void rope(float *h, int hd, int pos, double theta) {
+    const int half = hd / 2;
+    for (int i = 0; i < half; i++) {
+        double freq = pow(theta, -2 * (double)i / (double)hd);
+        double s = sin((double)pos * freq), c = cos((double)pos * freq);
+        double a = h[i], b = h[i + half];
+        h[i] = (float)(a * c - b * s);
+        h[i + half] = (float)(b * c + a * s);
+    }
+}
+
+struct gqa_job {
+    const float *q, *kc, *vc;
+    float *out;
+    int steps, hd, kvd, group;
+    double scale;
+};
+static void gqa_head_task(void *arg, int h) {
+    struct gqa_job *j = arg;
+    const int qoff = h * j->hd, kvoff = (h / j->group) * j->hd;
+    double *scores = malloc(sizeof(double) * (size_t)(j->steps > 0 ? j->steps : 1));
+    double maxs = -INFINITY;
+    for (int t = 0; t < j->steps; t++) {
+        double s = 0;
+        const float *kt = j->kc + (size_t)t * j->kvd;
+        for (int i = 0; i < j->hd; i++) s += (double)j->q[qoff + i] * (double)kt[kvoff + i];
+        s *= j->scale;
+        scores[t] = s;
+        if (s > maxs) maxs = s;
+    }
+    double sum = 0;
+    for (int t = 0; t < j->steps; t++) {
+        scores[t] = exp(scores[t] - maxs);
+        sum += scores[t];
+    }
+    for (int t = 0; t < j->steps; t++) {
+        const float p = (float)(scores[t] / sum);
+        const float *vt = j->vc + (size_t)t * j->kvd;
+        for (int i = 0; i < j->hd; i++) j->out[qoff + i] += p * vt[kvoff + i];
+    }
+    free(scores);
+}
+
+/* step, model.go:232-307. */
+static void qwen_step(qwen *m, int token, int pos, float *logits) {
+    const tqo_qwen_cfg *c = &m->c;
+    const int d = c->d, hd = m->hd, kvd = m->kvd, ffn = c->ffn;
+    float *x = malloc(sizeof(float) * d), *a = malloc(sizeof(float) * d), *q = malloc(sizeof(float) * d);
+    float *k = malloc(sizeof(float) * kvd), *v = malloc(sizeof(float) * kvd), *attn = malloc(sizeof(float) * d);
+    float *proj = malloc(sizeof(float) * d), *gate = malloc(sizeof(float) * ffn), *up = malloc(sizeof(float) * ffn);
+    memcpy(x, m->embed + (size_t)token * d, sizeof(float) * d);
+    for (int l = 0; l < c->n_layer; l++) {
+        qwblock *b = &m->b[l];
+        rmsnorm(x, b->ln1, d, c->eps, a);
+        q4_mv(&b->wq, a, q), add_bias(q, b->bq, d);
+        q4_mv(&b->wk, a, k), add_bias(k, b->bk, kvd);
+        q4_mv(&b->wv, a, v), add_bias(v, b->bv, kvd);
+        for (int h = 0; h < c->n_head; h++) rope(q + h * hd, hd, pos, c->theta);
+        for (int h = 0; h < c->n_kv; h++) rope(k + h * hd, hd, pos, c->theta);
+        memcpy(b->kc + (size_t)pos * kvd, k, sizeof(float) * kvd);
+        memcpy(b->vc + (size_t)pos * kvd, v, sizeof(float) * kvd);
+        memset(attn, 0, sizeof(float) * d);
+        struct gqa_job j = {q, b->kc, b->vc, attn, pos + 1, hd, kvd, c->n_head / c->n_kv, 1 / sqrt((double)hd)};
+        tqo_pool_run(gqa_head_task, &j, c->n_head);
+        q4_mv(&b->wo, attn, proj);
+        for (int i = 0; i < d; i++) x[i] += proj[i];
+        rmsnorm(x, b->ln2, d, c->eps, a);
+        q4_mv(&b->gate, a, gate);
+        q4_mv(&b->up, a, up);
+        for (int i = 0; i < ffn; i++) {
+            double g = gate[i];
+            gate[i] = (float)(g / (1 + exp(-g))) * up[i]; /* silu(gate) * up */
+        }
+        q4_mv(&b->down, gate, proj);
+        for (int i = 0; i < d; i++) x[i] += proj[i];
+    }
+    rmsnorm(x, m->normw, d, c->eps, a);
+    q4_mv(&m->lm, a, logits);
+    free(x), free(a), free(q), free(k), free(v), free(attn), free(proj), free(gate), free(up);
+}
+
+static qwen *qwen_new(const tqo_qwen_cfg *c, uint64_t seed, float sigma) {
+    qwen *m = calloc(1, sizeof(qwen));
+    m->c = *c;
+    m->hd = c->d / c->n_head;
+    m->kvd = c->n_kv * m->hd;
+    const int d = c->d, kvd = m->kvd, ffn = c->ffn;
+    m->embed = synth((size_t)c->vocab * d, seed, 1, sigma);
+    m->normw = ones(d);
+    q4_init(&m->lm, seed, 2, sigma, d, c->vocab);
+    m->b = calloc((size_t)c->n_layer, sizeof(qwblock));
+    for (int l = 0; l < c->n_layer; l++) {
+        qwblock *b = &m->b[l];
+        const uint64_t s0 = 32 + 16 * (uint64_t)l;
+        q4_init(&b->wq, seed, s0, sigma, d, d);
+        q4_init(&b->wk, seed, s0 + 1, sigma, d, kvd);
+        q4_init(&b->wv, seed, s0 + 2, sigma, d, kvd);
+        q4_init(&b->wo, seed, s0 + 3, sigma, d, d);
+        q4_init(&b->gate, seed, s0 + 4, sigma, d, ffn);
+        q4_init(&b->up, seed, s0 + 5, sigma, d, ffn);
+        q4_init(&b->down, seed, s0 + 6, sigma, ffn, d);
+        b->ln1 = ones(d), b->ln2 = ones(d);
+        b->bq = zeros(d), b->bk = zeros(kvd), b->bv = zeros(kvd);
+        b->kc = zeros((size_t)c->ctx * kvd);
+        b->vc = zeros((size_t)c->ctx * kvd);
+    }
+    return m;
+}
+
+static void q4_free(q4mat *m) { free(m->q), free(m->scale); }
+
+static void qwen_free(qwen *m) {
+    free(m->embed), free(m->normw);
+    q4_free(&m->lm);
+    for (int l = 0; l < m->c.n_layer; l++) {
+        qwblock *b = &m->b[l];
+        q4_free(&b->wq), q4_free(&b->wk), q4_free(&b->wv), q4_free(&b->wo);
+        q4_free(&b->gate), q4_free(&b->up), q4_free(&b->down);
+        free(b->ln1), free(b->ln2), free(b->bq), free(b->bk), free(b->bv), free(b->kc), free(b->vc);
+    }
+    free(m->b);
+    free(m);
+}
+
+/*
+ * main.go:225-240 at temperature 0 without the end-of-turn stop: the
+ * prompt through step one token at a time, then n_gen greedy picks, each fed
+ * back. tokens/margins as tqo_gpt2_generate; seconds (optional): wall time of
+ * the prompt steps and of the n_gen - 1 decode steps; prompt_logits
+ * (optional, vocab floats): the logits after the last prompt token.
+ * Returns 0 or -1.
+ */
+TQO_EXPORT int tqo_qwen_generate(const tqo_qwen_cfg *c, uint64_t seed, float sigma, const int *prompt, int n_prompt,
+                                 int n_gen, int *tokens, float *margins, double *seconds, float *prompt_logits) {
+    if (!c || n_prompt < 1 || n_prompt + n_gen > c->ctx + 1 || c->n_head % c->n_kv || c->d % c->n_head ||
+        (c->d / c->n_head) % 2 || c->ffn % 2 || c->vocab % 2 || c->d % 2)
+        return -1;
+    qwen *m = qwen_new(c, seed, sigma);
+    float *logits = malloc(sizeof(float) * (size_t)c->vocab);
+    const double t0 = now_s();
+    for (int p = 0; p < n_prompt; p++) qwen_step(m, prompt[p], p, logits);
+    const double t1 = now_s();
+    if (prompt_logits) memcpy(prompt_logits, logits, sizeof(float) * (size_t)c->vocab);
+    int pos = n_prompt;
+    for (int i = 0; i < n_gen; i++) {
+        const int next = argmax(logits, c->vocab, margins ? &margins[i] : NULL);
+        tokens[i] = next;
+        if (i + 1 < n_gen) qwen_step(m, next, pos++, logits);
+    }
+    if (seconds) seconds[0] = t1 - t0, seconds[1] = now_s() - t1;
+    free(logits);
+    qwen_free(m);
+    return 0;
+}

@@ -56,6 +56,10 @@ SIGNATURES = {
     "tq_gpt2_generate": (I, [U64, P, I, I, P, P]),
     "tq_gpt2_free": (I, [U64]),
     "tq_synth_tokens": (I, [P, I, I, U64]),
+    "tq_nccl_unique_id": (I, [P]),
+    "tq_qwen_create": (I, [P, U64, F, I, I, P, PU64]),
+    "tq_qwen_generate": (I, [U64, P, I, I, P, P]),
+    "tq_qwen_free": (I, [U64]),
     "tq_set_matvec_kernel": (I, [I]),
     "tq_debug_fail_allocs": (I, [I]),
 }

@@ -24,39 +24,13 @@
 #include <vector>
 
 #include "../../include/tensai_cuda.h"
+#define TQD_NS tqd_gpt2
+#include "tq_decode.cuh"
 #include "tq_internal.h"
 
 namespace {
 
-constexpr int kThreads = 256;
-
-// ---- reductions -------------------------------------------------------------
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-__device__ __forceinline__ double warp_max_d(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-// Block-wide sum (kind 0) or max (kind 1) of one double per thread; all
-// threads get the result. sh: 32 doubles of shared memory.
-__device__ double block_reduce_d(double v, double *sh, int kind) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-    v = kind ? warp_max_d(v) : warp_sum_d(v);
-    __syncthreads();
-    if (lane == 0) sh[w] = v;
-    __syncthreads();
-    if (w == 0) {
-        double u = lane < nw ? sh[lane] : (kind ? -INFINITY : 0.0);
-        u = kind ? warp_max_d(u) : warp_sum_d(u);
-        if (lane == 0) sh[0] = u;
-    }
-    __syncthreads();
-    return sh[0];
-}
+using namespace tqd_gpt2;
 
 // ---- elementwise / normalisation kernels -------------------------------------
 // x = wte[token] + wpe[pos] (model.go:181-184); decode: token and position
@@ -89,13 +63,6 @@ __global__ void layernorm_kernel(const float *x, const float *w, const float *b,
         o[i] = __fadd_rn(__fmul_rn((float)__dmul_rn(__dsub_rn((double)xr[i], mean), inv), w[i]), b[i]);
 }
 
-// x += y + b, row by row (model.go:229-231 / 242-244: bias into the matvec
-// output, then the residual add).
-__global__ void residual_kernel(float *x, const float *y, const float *b, int n, size_t total) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
-        x[i] = __fadd_rn(x[i], __fadd_rn(y[i], b[i % n]));
-}
-
 // h = geluNew(h + b) (model.go:170-175, 239-240).
 __global__ void bias_gelu_kernel(float *h, const float *b, int n, size_t total) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -121,46 +88,6 @@ __global__ void qkv_post_kernel(float *qkv, const float *bias, float *kc, float 
             kc[(size_t)pos * d + (i - d)] = v;
         else
             vc[(size_t)pos * d + (i - 2 * d)] = v;
-    }
-}
-
-// Attention of one query row over cached positions 0..pos for head
-// blockIdx.x (model.go:195-227; the rows of cpuCausalMHA, model.go:289-322):
-// scores in float64 divided by 8, softmax in float64, p = float32(score /
-// sum), out += p * v in float32 over positions in order. Query row
-// blockIdx.y of q (row stride qstride); decode: pos from the state.
-__global__ void attention_kernel(const float *q, int qstride, const float *kc, const float *vc, float *out,
-                                 const int *state, int d, int hd, int prefill, int ctx) {
-    extern __shared__ double sc[]; // [ctx] scores, then [ctx] probabilities as float
-    __shared__ double sh[32];
-
-    const int h = blockIdx.x, r = blockIdx.y;
-    const int pos = prefill ? r : state[1];
-    const float *qr = q + (size_t)r * qstride + h * hd;
-    double mx = -INFINITY;
-    for (int t = threadIdx.x; t <= pos; t += blockDim.x) {
-        const float *kt = kc + (size_t)t * d + h * hd;
-        double s = 0;
-        for (int i = 0; i < hd; i++) s = __dadd_rn(s, __dmul_rn((double)qr[i], (double)kt[i]));
-        s = __ddiv_rn(s, 8.0); // sqrt(headSz)
-        sc[t] = s;
-        mx = fmax(mx, s);
-    }
-    mx = block_reduce_d(mx, sh, 1);
-    double sum = 0;
-    for (int t = threadIdx.x; t <= pos; t += blockDim.x) {
-        const double e = exp(__dsub_rn(sc[t], mx));
-        sc[t] = e;
-        sum = __dadd_rn(sum, e);
-    }
-    sum = block_reduce_d(sum, sh, 0);
-    float *p = reinterpret_cast<float *>(sc + ctx);
-    for (int t = threadIdx.x; t <= pos; t += blockDim.x) p[t] = (float)__ddiv_rn(sc[t], sum);
-    __syncthreads();
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        float acc = 0.f;
-        for (int t = 0; t <= pos; t++) acc = __fadd_rn(acc, __fmul_rn(p[t], vc[(size_t)t * d + h * hd + i]));
-        out[(size_t)r * d + h * hd + i] = acc;
     }
 }
 
@@ -208,38 +135,6 @@ __global__ void __launch_bounds__(256) sgemm_chain_kernel(const float *__restric
         }
 }
 
-// Greedy pick (main.go:69-77): the first index of the largest logit. Writes
-// it as the next token and the generated-token record, and advances the
-// state: position = set_pos if >= 0, else position + 1.
-__global__ void argmax_kernel(const float *logits, int n, int *state, int *tokens, int set_pos) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    float best = -INFINITY;
-    int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = logits[i];
-        if (v > best) best = v, idx = i; // increasing i per thread: keeps the first maximum
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
-    }
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    if (lane == 0) bv[w] = best, bi[w] = idx;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int k = 1; k < (int)(blockDim.x >> 5); k++)
-            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) best = bv[k], idx = bi[k];
-        if (idx == 0x7fffffff) idx = 0;
-        tokens[state[2]] = idx;
-        state[0] = idx;
-        state[1] = set_pos >= 0 ? set_pos : state[1] + 1;
-        state[2] += 1;
-    }
-}
-
 __global__ void transpose_kernel(const float *in, float *out, int rows, int cols) {
     __shared__ float t[32][33];
     const int c = blockIdx.x * 32 + threadIdx.x, r0 = blockIdx.y * 32;
@@ -249,16 +144,6 @@ __global__ void transpose_kernel(const float *in, float *out, int rows, int cols
     const int r = r0 + threadIdx.x, cb = blockIdx.x * 32;
     for (int j = threadIdx.y; j < 32; j += blockDim.y)
         if (cb + j < cols && r < rows) out[(size_t)(cb + j) * rows + r] = t[threadIdx.x][j];
-}
-
-__global__ void fill_kernel(float *p, float v, size_t n) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
-}
-
-__global__ void set_state_kernel(int *state, int token, int pos, int generated) {
-    state[0] = token;
-    state[1] = pos;
-    state[2] = generated;
 }
 
 // ---- engine -------------------------------------------------------------------
@@ -288,7 +173,7 @@ struct Gpt2 {
     // prefill buffers (max_prompt rows)
     int max_prompt = 0;
     float *X = nullptr, *XN = nullptr, *QKV = nullptr, *ATT = nullptr, *Y = nullptr, *H = nullptr;
-    int *state = nullptr, *tokens = nullptr, *d_prompt = nullptr;
+    int *state = nullptr, *tokens = nullptr, *d_prompt = nullptr, *cand = nullptr;
     cudaGraphExec_t graph = nullptr;
     std::vector<void *> allocs;
 };
@@ -332,7 +217,7 @@ void destroy(Gpt2 &m) {
         if (e_ != cudaSuccess) return e_;                                                                              \
     } while (0)
 
-size_t attn_smem(const Gpt2 &m) { return (sizeof(double) + sizeof(float)) * (size_t)m.c.ctx; }
+size_t attn_smem(const Gpt2 &m) { return attention_smem(m.c.ctx); }
 
 // A random-init weight: fp32 from the shared generator, then its int8 twin.
 cudaError_t make_weight(Gpt2 &m, Weight &w, int rows, int cols, uint64_t seed, uint64_t stream, float sigma, int *rc) {
@@ -387,6 +272,7 @@ cudaError_t build(Gpt2 &m, uint64_t seed, float sigma, int *rc) {
     TRY(dalloc(m, (void **)&m.h, sizeof(float) * ffn));
     TRY(dalloc(m, (void **)&m.logits, sizeof(float) * c.vocab));
     TRY(dalloc(m, (void **)&m.state, sizeof(int) * 4));
+    TRY(dalloc(m, (void **)&m.cand, sizeof(int) * 2));
     TRY(dalloc(m, (void **)&m.tokens, sizeof(int) * (size_t)(c.ctx + 1)));
     if ((*rc = tq_scratch_for(m.device, m.st, &m.scr, 1)) != TQ_OK) return cudaErrorMemoryAllocation;
     const size_t smem = attn_smem(m);
@@ -426,8 +312,8 @@ cudaError_t prefill(Gpt2 &m, const int *prompt, int T) {
         layernorm_kernel<<<T, kThreads, 0, m.st>>>(m.X, bl.ln1w, bl.ln1b, m.XN, d);
         TRY(sgemm(m.XN, bl.attn.w, m.QKV, T, 3 * d, d, m.st));
         qkv_post_kernel<<<T, kThreads, 0, m.st>>>(m.QKV, bl.attnB, bl.kc, bl.vc, m.state, d, 1);
-        attention_kernel<<<dim3(m.c.n_head, T), kThreads, attn_smem(m), m.st>>>(m.QKV, 3 * d, bl.kc, bl.vc, m.ATT,
-                                                                               m.state, d, hd, 1, m.c.ctx);
+        attention_kernel<<<dim3(m.c.n_head, T), kThreads, attn_smem(m), m.st>>>(
+            m.QKV, 3 * d, bl.kc, bl.vc, d, m.ATT, d, m.state, hd, 1, 0.125 /* 1/sqrt(64) */, 1, m.c.ctx);
         TRY(cudaGetLastError());
         TRY(sgemm(m.ATT, bl.proj.w, m.Y, T, d, d, m.st));
         residual_kernel<<<grid_for((size_t)T * d), kThreads, 0, m.st>>>(m.X, m.Y, bl.projB, d, (size_t)T * d);
@@ -440,7 +326,7 @@ cudaError_t prefill(Gpt2 &m, const int *prompt, int T) {
     }
     layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.X + (size_t)(T - 1) * d, m.lnfw, m.lnfb, m.xn, d);
     TRY(sgemm(m.xn, m.wteT.w, m.logits, 1, m.c.vocab, d, m.st));
-    argmax_kernel<<<1, 1024, 0, m.st>>>(m.logits, m.c.vocab, m.state, m.tokens, T);
+    argmax_kernel<<<1, 1024, 0, m.st>>>(m.logits, m.c.vocab, 0, m.cand, m.state, m.tokens, T, 1);
     return cudaGetLastError();
 }
 
@@ -453,8 +339,8 @@ cudaError_t decode_step(Gpt2 &m) {
         layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, bl.ln1w, bl.ln1b, m.xn, d);
         TRY(tq_launch_matmul(bl.attn.q, m.xn, m.qkv, 1, m.scr, m.st));
         qkv_post_kernel<<<1, kThreads, 0, m.st>>>(m.qkv, bl.attnB, bl.kc, bl.vc, m.state, d, 0);
-        attention_kernel<<<dim3(m.c.n_head, 1), kThreads, attn_smem(m), m.st>>>(m.qkv, 3 * d, bl.kc, bl.vc, m.att,
-                                                                               m.state, d, hd, 0, m.c.ctx);
+        attention_kernel<<<dim3(m.c.n_head, 1), kThreads, attn_smem(m), m.st>>>(
+            m.qkv, 3 * d, bl.kc, bl.vc, d, m.att, d, m.state, hd, 1, 0.125 /* 1/sqrt(64) */, 0, m.c.ctx);
         TRY(tq_launch_matmul(bl.proj.q, m.att, m.y, 1, m.scr, m.st));
         residual_kernel<<<grid_for(d), kThreads, 0, m.st>>>(m.x, m.y, bl.projB, d, d);
         layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, bl.ln2w, bl.ln2b, m.xn, d);
@@ -466,7 +352,7 @@ cudaError_t decode_step(Gpt2 &m) {
     }
     layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, m.lnfw, m.lnfb, m.xn, d);
     TRY(tq_launch_matmul(m.wteT.q, m.xn, m.logits, 1, m.scr, m.st));
-    argmax_kernel<<<1, 1024, 0, m.st>>>(m.logits, m.c.vocab, m.state, m.tokens, -1);
+    argmax_kernel<<<1, 1024, 0, m.st>>>(m.logits, m.c.vocab, 0, m.cand, m.state, m.tokens, -1, 1);
     return cudaGetLastError();
 }
 

@@ -1,9 +1,12 @@
-"""Host mirror of the whole-model greedy decode engines (C ABI tq_gpt2_*).
+"""Host mirror of the whole-model greedy decode engines (C ABI tq_gpt2_*,
+tq_qwen_*).
 
 Gpt2 stands for the GPT-2 example's model (_example/gpt2/model.go) with
 random-init weights: Gpt2(cfg, seed, sigma).generate(prompt, n) runs the
 fp32 prefill and the int8 decode steps on the GPU and returns the greedy
-token ids (main.go:163-170 at temperature 0).
+token ids (main.go:163-170 at temperature 0). Qwen does the same for the
+Qwen2 example (_example/qwen/model.go) with int4 weights, tensor-parallel
+over the ranks of a process group (one process per GPU).
 """
 from __future__ import annotations
 
@@ -53,6 +56,93 @@ class Gpt2:
     def free(self) -> None:
         if self.handle:
             _lib.load().tq_gpt2_free(self.handle)
+            self.handle = 0
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.free()
+
+
+# ---------------------------------------------------------------------------
+# Qwen2 (int4), tensor parallel
+# ---------------------------------------------------------------------------
+
+QWEN_7B = dict(n_layer=28, n_head=28, n_kv=4, d=3584, ffn=18944, vocab=152064, ctx=2560, eps=1e-6, theta=1e6)
+
+
+class QwenConfig(ctypes.Structure):
+    _fields_ = [("n_layer", ctypes.c_int), ("n_head", ctypes.c_int), ("n_kv", ctypes.c_int), ("d", ctypes.c_int),
+                ("ffn", ctypes.c_int), ("vocab", ctypes.c_int), ("ctx", ctypes.c_int), ("eps", ctypes.c_double),
+                ("theta", ctypes.c_double)]
+
+
+def qwen_shard_plan(cfg: dict, world: int, rank: int) -> dict:
+    """The slices of the model that rank `rank` of `world` holds (the rule
+    tq_qwen_create applies): attention heads, o_proj rows, MLP columns
+    (gate/up) = down rows, lm-head columns. Raises ValueError when the
+    configuration does not split over `world` GPUs."""
+    nh, nkv, d, ffn, V = cfg["n_head"], cfg["n_kv"], cfg["d"], cfg["ffn"], cfg["vocab"]
+    hd = d // nh
+    if nkv % world == 0:
+        wa = world
+    elif world % nkv == 0:
+        wa = nkv
+    else:
+        raise ValueError(f"{world} GPUs do not split {nkv} KV heads")
+    if d % world or (d // world) % 64 or ffn % world or (ffn // world) % 64 or V % world or (V // world) % 2:
+        raise ValueError("d/world and ffn/world must be whole 64-row groups and vocab/world even")
+    ashard = rank * wa // world
+    nq, nk = nh // wa, nkv // wa
+    orows = d // world
+    return dict(q_heads=(ashard * nq, (ashard + 1) * nq), kv_heads=(ashard * nk, (ashard + 1) * nk),
+                o_rows=(rank * orows, (rank + 1) * orows), att_dims=(ashard * nq * hd, (ashard + 1) * nq * hd),
+                ffn=(rank * (ffn // world), (rank + 1) * (ffn // world)),
+                vocab=(rank * (V // world), (rank + 1) * (V // world)))
+
+
+def nccl_unique_id() -> bytes:
+    buf = (ctypes.c_char * 128)()
+    _lib.check(_lib.load().tq_nccl_unique_id(buf))
+    return bytes(buf)
+
+
+def broadcast_nccl_id(dist) -> bytes:
+    """Rank 0 makes an NCCL unique id; every rank of the process group gets it."""
+    obj = [nccl_unique_id() if dist.get_rank() == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    return obj[0]
+
+
+class Qwen:
+    """This rank's shard of a resident random-init Qwen2 (int4) on the current
+    device. world > 1: every rank builds its shard at the same time with the
+    same nccl_id (see broadcast_nccl_id) and calls generate together."""
+
+    def __init__(self, cfg: dict, seed: int, sigma: float = 0.02, rank: int = 0, world: int = 1,
+                 nccl_id: bytes | None = None):
+        self.cfg = dict(cfg)
+        c = QwenConfig(**self.cfg)
+        h = ctypes.c_uint64()
+        idp = ctypes.create_string_buffer(nccl_id, 128) if nccl_id else None
+        _lib.check(_lib.load().tq_qwen_create(ctypes.byref(c), seed, ctypes.c_float(sigma), rank, world, idp,
+                                              ctypes.byref(h)))
+        self.handle = h.value
+        self.last_times_ms = (0.0, 0.0)
+
+    def generate(self, prompt, n: int) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.empty(n, np.int32)
+        t = (ctypes.c_float * 2)()
+        _lib.check(_lib.load().tq_qwen_generate(self.handle, p.ctypes.data_as(ctypes.c_void_p), len(p), n,
+                                                out.ctypes.data_as(ctypes.c_void_p), t))
+        self.last_times_ms = (t[0], t[1])
+        return out
+
+    def free(self) -> None:
+        if self.handle:
+            _lib.load().tq_qwen_free(self.handle)
             self.handle = 0
 
     def __enter__(self):

@@ -1,0 +1,115 @@
+"""GPU Qwen2 int4 decode (tensor parallel) against the CPU oracle, through the
+C ABI. Bar: identical greedy token ids (the -q4 loop of _example/qwen,
+restated in oracle/tq_model.c) on small models, on the Qwen2.5-7B-shaped
+config against committed golden ids, and over 2/4/8 GPUs when present."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tensai_b200 import _lib
+from tensai_b200.decode import QWEN_7B, Qwen, synth_tokens
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(n_layer=2, n_head=4, n_kv=2, d=256, ffn=512, vocab=1000, ctx=64, eps=1e-6, theta=1e6)
+TINY_TP = dict(n_layer=2, n_head=8, n_kv=2, d=512, ffn=1024, vocab=1008, ctx=96, eps=1e-6, theta=1e6)
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _ndev():
+    import torch
+    return torch.cuda.device_count()
+
+
+@pytest.fixture(scope="module", autouse=True)
+def device():
+    import torch
+    torch.cuda.init()
+    _lib.check(_lib.load().tq_set_device(0))
+
+
+def _diverge(got, want, margins):
+    bad = np.nonzero(np.asarray(got) != np.asarray(want))[0]
+    if len(bad) == 0:
+        return None
+    i = int(bad[0])
+    return f"token {i}: gpu {got[i]} oracle {want[i]}, oracle top-1 margin {float(margins[i]):.3g}"
+
+
+@pytest.mark.parametrize("seed", [1, 2])
+def test_tiny_qwen_matches_oracle(seed):
+    prompt = synth_tokens(20, TINY["vocab"], seed)
+    want, margins = O.qwen_generate(TINY, seed, 0.02, prompt, 30)
+    with Qwen(TINY, seed) as m:
+        got = m.generate(prompt, 30)
+        again = m.generate(prompt, 30)
+    assert np.array_equal(got, want), _diverge(got, want, margins)
+    assert np.array_equal(again, got)
+
+
+def test_single_token_prompt():
+    prompt = synth_tokens(1, TINY["vocab"], 4)
+    want, margins = O.qwen_generate(TINY, 4, 0.02, prompt, 8)
+    with Qwen(TINY, 4) as m:
+        got = m.generate(prompt, 8)
+    assert np.array_equal(got, want), _diverge(got, want, margins)
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "qwen7b_decode_golden_*.npz"))))
+def test_qwen7b_shape_matches_golden_tokens(path):
+    z = np.load(path)
+    n_prompt, n_gen = len(z["prompt"]), len(z["tokens"])
+    cfg = dict(QWEN_7B, ctx=n_prompt + n_gen)
+    prompt = synth_tokens(n_prompt, cfg["vocab"], int(z["seed"]))
+    assert np.array_equal(prompt, z["prompt"])
+    with Qwen(cfg, int(z["seed"]), float(z["sigma"])) as m:
+        got = m.generate(prompt, n_gen)
+    assert np.array_equal(got, z["tokens"]), _diverge(got, z["tokens"], z["margins"])
+
+
+def _tp_worker(rank, world, port, q, cfg, seed, prompt, n):
+    import torch
+    import torch.distributed as dist
+
+    from tensai_b200.decode import broadcast_nccl_id
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    _lib.check(_lib.load().tq_set_device(rank))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        nid = broadcast_nccl_id(dist)
+        with Qwen(cfg, seed, 0.02, rank, world, nid) as m:
+            q.put((rank, m.generate(prompt, n).tolist()))
+    except Exception as e:  # reported to the parent
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def run_tp(cfg, seed, prompt, n, world):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + os.getpid() % 500
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q, cfg, seed, prompt, n)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    return got
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_tiny_qwen_matches_oracle(world):
+    if _ndev() < world:
+        pytest.skip(f"needs {world} GPUs")
+    prompt = synth_tokens(24, TINY_TP["vocab"], 3)
+    want, margins = O.qwen_generate(TINY_TP, 3, 0.02, prompt, 40)
+    got = run_tp(TINY_TP, 3, prompt, 40, world)
+    for r in range(world):
+        assert isinstance(got[r], list), got[r]
+        assert np.array_equal(got[r], want), (r, _diverge(got[r], want, margins))
