@@ -293,6 +293,41 @@ def measure_gpt2(cpu: bool):
     return rec
 
 
+QWEN_PROMPT, QWEN_GEN = 2048, 512
+QWEN_BYTES_PER_TOKEN = 3_977_035_776  # int4 codes + scales streamed per token (all layers + lm head)
+
+
+def measure_qwen(rank: int, world: int, peak: float):
+    """Qwen2.5-7B-shaped int4 greedy decode, tensor parallel over the job's
+    GPUs (one rank per GPU): the 2048-token prompt through the decode step,
+    then 512 tokens. Decode tokens/s from the device time of the 511 later
+    steps, max over ranks. Every rank must call this (collective)."""
+    import torch
+    import torch.distributed as dist
+
+    from tensai_b200.decode import QWEN_7B, Qwen, broadcast_nccl_id, synth_tokens
+    prompt = synth_tokens(QWEN_PROMPT, QWEN_7B["vocab"], 1)
+    nid = broadcast_nccl_id(dist) if world > 1 else None
+    with Qwen(QWEN_7B, 1, 0.02, rank, world, nid) as m:
+        toks = m.generate(prompt, QWEN_GEN)
+        pre_ms, dec_ms = m.last_times_ms
+    t = torch.tensor([pre_ms, dec_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    pre_ms, dec_ms = float(t[0]), float(t[1])
+    tok_s = (QWEN_GEN - 1) / (dec_ms * 1e-3)
+    bound = world * peak * 1e9 / QWEN_BYTES_PER_TOKEN
+    return {"tp": world, "decode_tok_s": round(tok_s, 2), "ms_per_token": round(dec_ms / (QWEN_GEN - 1), 4),
+            "prompt_ms": round(pre_ms, 1), "prompt_tok_s": round(QWEN_PROMPT / (pre_ms * 1e-3), 1),
+            "roofline": {"bound": "aggregate hbm", "tok_s_bound": round(bound, 1), "frac": round(tok_s / bound, 4),
+                         "bytes_per_token": QWEN_BYTES_PER_TOKEN, "peak_gbs_per_gpu": peak},
+            "first_tokens": [int(x) for x in toks[:8]],
+            "cpu_baseline_recorded": {"decode_tok_s": 2.81, "cores": 8, "kind": "port",
+                                      "sample": "511 decode steps after the 2048-token prompt, oracle restatement "
+                                                "of the -q4 loop, timed once in the build container "
+                                                "(tests/golden/qwen7b_decode_golden_2048_512.npz)"}}
+
+
 def _check_rc(L, rc):
     if rc:
         raise RuntimeError(L.tq_last_error().decode())
@@ -419,6 +454,11 @@ def run_gpu(args, rank: int, world: int):
     if rank == 0 and not args.no_side_configs:
         side = measure_side_configs(L, Q, torch, stream, load_peak()[0])
         side["C4 GPT-2-small int8 greedy decode"] = measure_gpt2(world == 1 and not args.no_cpu_baseline)
+    qwen = None
+    if not args.no_side_configs:
+        qwen = measure_qwen(rank, world, load_peak()[0])  # collective over all ranks
+        if side is not None:
+            side[f"C5 Qwen2.5-7B int4 greedy decode TP={world}"] = qwen
     if rank == 0:
         peak, peak_src = load_peak()
         per_launch = pair_bytes() / 2  # up and down carry the same algorithmic bytes

@@ -108,6 +108,121 @@ __global__ void attention_kernel(const float *q, int qstride, const float *kc, c
 
 inline size_t attention_smem(int ctx) { return (sizeof(double) + sizeof(float)) * (size_t)ctx; }
 
+// ---- split-K decode attention -------------------------------------------------------
+// The same attention for the decode step's single query row, spread over
+// chunks of kAttChunk cached positions so that long contexts use every SM:
+//   scores:   per (head, chunk): s_t = (q . k_t in float64) * scale, and the
+//             chunk's max m_b and sum l_b = sum exp(s_t - m_b);
+//   weights:  per (head, chunk): the softmax's global max M and sum
+//             L = sum_b l_b exp(m_b - M) (chunks in order), p_t = float32(
+//             exp(s_t - M) / L) as the Go code forms it, and the chunk's
+//             float32 partial sum_t p_t * v_t (positions in order);
+//   combine:  per head: the chunk partials summed in chunk order.
+// Scratch (per engine): scores [heads][ctx] doubles, stats [heads][chunks][2]
+// doubles, partials [heads][chunks][hd] floats.
+constexpr int kAttChunk = 128;
+
+__global__ void __launch_bounds__(128) att_scores_kernel(const float *q, const float *kc, int kvstride, const int *state,
+                                                         int hd, int group, double scale, double *scores,
+                                                         double *stats, int ctx, int nchunks) {
+    __shared__ double ss[kAttChunk];
+    __shared__ double sh[32];
+    const int h = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttChunk;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, kvh = h / group;
+    if (t0 > pos) return;
+    const int t1 = min(t0 + kAttChunk, pos + 1);
+    const float *qh = q + h * hd;
+    for (int t = t0 + warp; t < t1; t += 4) {
+        const float *kt = kc + (size_t)t * kvstride + kvh * hd;
+        double s = 0;
+        for (int i = lane; i < hd; i += 32) s = __dadd_rn(s, __dmul_rn((double)qh[i], (double)kt[i]));
+        s = warp_sum_d(s);
+        if (lane == 0) ss[t - t0] = __dmul_rn(s, scale);
+    }
+    __syncthreads();
+    double mx = -INFINITY;
+    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) mx = fmax(mx, ss[t - t0]);
+    mx = block_reduce_d(mx, sh, 1);
+    double l = 0;
+    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
+        l = __dadd_rn(l, exp(__dsub_rn(ss[t - t0], mx)));
+        scores[(size_t)h * ctx + t] = ss[t - t0];
+    }
+    l = block_reduce_d(l, sh, 0);
+    if (threadIdx.x == 0) {
+        stats[((size_t)h * nchunks + b) * 2] = mx;
+        stats[((size_t)h * nchunks + b) * 2 + 1] = l;
+    }
+}
+
+__global__ void __launch_bounds__(128) att_weighted_kernel(const float *vc, int kvstride, const int *state, int hd,
+                                                           int group, const double *scores, const double *stats,
+                                                           float *partial, int ctx, int nchunks) {
+    __shared__ float ps[kAttChunk];
+    const int h = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttChunk, kvh = h / group;
+    if (t0 > pos) return;
+    const int t1 = min(t0 + kAttChunk, pos + 1), nb = pos / kAttChunk + 1;
+    const double *st = stats + (size_t)h * nchunks * 2;
+    double M = -INFINITY;
+    for (int c = 0; c < nb; c++) M = fmax(M, st[2 * c]);
+    double L = 0;
+    for (int c = 0; c < nb; c++) L = __dadd_rn(L, __dmul_rn(st[2 * c + 1], exp(__dsub_rn(st[2 * c], M))));
+    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x)
+        ps[t - t0] = (float)__ddiv_rn(exp(__dsub_rn(scores[(size_t)h * ctx + t], M)), L);
+    __syncthreads();
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        const float *v = vc + kvh * hd + i;
+        float acc = 0.f;
+#pragma unroll 8
+        for (int t = t0; t < t1; t++) acc = __fadd_rn(acc, __fmul_rn(ps[t - t0], v[(size_t)t * kvstride]));
+        partial[((size_t)h * nchunks + b) * hd + i] = acc;
+    }
+}
+
+__global__ void att_combine_kernel(const float *partial, const int *state, int hd, float *out, int nchunks) {
+    const int h = blockIdx.x, nb = state[1] / kAttChunk + 1;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        float acc = 0.f;
+        for (int c = 0; c < nb; c++) acc = __fadd_rn(acc, partial[((size_t)h * nchunks + c) * hd + i]);
+        out[h * hd + i] = acc;
+    }
+}
+
+struct AttScratch {
+    double *scores = nullptr, *stats = nullptr;
+    float *partial = nullptr;
+    int ctx = 0, nchunks = 0;
+};
+
+inline size_t att_scratch_bytes(int heads, int ctx, int hd) {
+    const int nc = (ctx + kAttChunk - 1) / kAttChunk;
+    return sizeof(double) * (size_t)heads * ctx + sizeof(double) * 2 * (size_t)heads * nc +
+           sizeof(float) * (size_t)heads * nc * hd;
+}
+
+// Carves the scratch out of one device buffer of att_scratch_bytes().
+inline AttScratch att_scratch(void *buf, int heads, int ctx, int hd) {
+    AttScratch a;
+    a.ctx = ctx;
+    a.nchunks = (ctx + kAttChunk - 1) / kAttChunk;
+    a.scores = static_cast<double *>(buf);
+    a.stats = a.scores + (size_t)heads * ctx;
+    a.partial = reinterpret_cast<float *>(a.stats + 2 * (size_t)heads * a.nchunks);
+    return a;
+}
+
+// The decode-step attention of q (heads x hd) over cached positions 0..state[1].
+inline cudaError_t decode_attention(const float *q, const float *kc, const float *vc, int kvstride, float *out,
+                                    const int *state, int heads, int hd, int group, double scale, const AttScratch &a,
+                                    cudaStream_t st) {
+    att_scores_kernel<<<dim3(heads, a.nchunks), 128, 0, st>>>(q, kc, kvstride, state, hd, group, scale, a.scores,
+                                                              a.stats, a.ctx, a.nchunks);
+    att_weighted_kernel<<<dim3(heads, a.nchunks), 128, 0, st>>>(vc, kvstride, state, hd, group, a.scores, a.stats,
+                                                                a.partial, a.ctx, a.nchunks);
+    att_combine_kernel<<<heads, 128, 0, st>>>(a.partial, state, hd, out, a.nchunks);
+    return cudaGetLastError();
+}
+
 // ---- greedy pick ------------------------------------------------------------------------
 // The first index of the largest of n logits (main.go:69-77: strict >), as
 // the candidate (value, offset + index) in cand[0..1] (value bits, index).

@@ -174,6 +174,7 @@ struct Gpt2 {
     int max_prompt = 0;
     float *X = nullptr, *XN = nullptr, *QKV = nullptr, *ATT = nullptr, *Y = nullptr, *H = nullptr;
     int *state = nullptr, *tokens = nullptr, *d_prompt = nullptr, *cand = nullptr;
+    AttScratch att_scr;
     cudaGraphExec_t graph = nullptr;
     std::vector<void *> allocs;
 };
@@ -273,6 +274,9 @@ cudaError_t build(Gpt2 &m, uint64_t seed, float sigma, int *rc) {
     TRY(dalloc(m, (void **)&m.logits, sizeof(float) * c.vocab));
     TRY(dalloc(m, (void **)&m.state, sizeof(int) * 4));
     TRY(dalloc(m, (void **)&m.cand, sizeof(int) * 2));
+    void *ab = nullptr;
+    TRY(dalloc(m, &ab, att_scratch_bytes(c.n_head, c.ctx, d / c.n_head)));
+    m.att_scr = att_scratch(ab, c.n_head, c.ctx, d / c.n_head);
     TRY(dalloc(m, (void **)&m.tokens, sizeof(int) * (size_t)(c.ctx + 1)));
     if ((*rc = tq_scratch_for(m.device, m.st, &m.scr, 1)) != TQ_OK) return cudaErrorMemoryAllocation;
     const size_t smem = attn_smem(m);
@@ -339,8 +343,8 @@ cudaError_t decode_step(Gpt2 &m) {
         layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, bl.ln1w, bl.ln1b, m.xn, d);
         TRY(tq_launch_matmul(bl.attn.q, m.xn, m.qkv, 1, m.scr, m.st));
         qkv_post_kernel<<<1, kThreads, 0, m.st>>>(m.qkv, bl.attnB, bl.kc, bl.vc, m.state, d, 0);
-        attention_kernel<<<dim3(m.c.n_head, 1), kThreads, attn_smem(m), m.st>>>(
-            m.qkv, 3 * d, bl.kc, bl.vc, d, m.att, d, m.state, hd, 1, 0.125 /* 1/sqrt(64) */, 0, m.c.ctx);
+        TRY(decode_attention(m.qkv, bl.kc, bl.vc, d, m.att, m.state, m.c.n_head, hd, 1, 0.125 /* 1/sqrt(64) */,
+                             m.att_scr, m.st));
         TRY(tq_launch_matmul(bl.proj.q, m.att, m.y, 1, m.scr, m.st));
         residual_kernel<<<grid_for(d), kThreads, 0, m.st>>>(m.x, m.y, bl.projB, d, d);
         layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, bl.ln2w, bl.ln2b, m.xn, d);

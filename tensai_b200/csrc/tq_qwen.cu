@@ -187,6 +187,7 @@ struct Qwen {
     TqMatrixDev lm{};
     float *x, *a, *qkv, *att, *y, *gu, *h, *logits;
     int *state = nullptr, *tokens = nullptr, *cand = nullptr, *cands = nullptr, *prompt = nullptr;
+    AttScratch att_scr;
     int prompt_cap = 0;
     cudaGraphExec_t graph = nullptr;
     int graph_prompt = -1; // the prompt length baked into the graph (advance_kernel)
@@ -318,10 +319,10 @@ cudaError_t build(Qwen &m, uint64_t seed, float sigma, int *rc) {
     TRY(dalloc(m, (void **)&m.tokens, sizeof(int) * (size_t)(c.ctx + 1)));
     TRY(dalloc(m, (void **)&m.cand, sizeof(int) * 2));
     TRY(dalloc(m, (void **)&m.cands, sizeof(int) * 2 * m.world));
+    void *ab = nullptr;
+    TRY(dalloc(m, &ab, att_scratch_bytes(m.nq, c.ctx, m.hd)));
+    m.att_scr = att_scratch(ab, m.nq, c.ctx, m.hd);
     if ((*rc = tq_scratch_for(m.device, m.st, &m.scr, 1)) != TQ_OK) return cudaErrorMemoryAllocation;
-    const size_t smem = attention_smem(c.ctx);
-    if (smem > 48 * 1024)
-        TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     return cudaSuccess;
 }
 
@@ -336,10 +337,8 @@ cudaError_t step(Qwen &m, int n_prompt) {
         TRY(tq_launch_matmul(ly.qkv, m.a, m.qkv, 1, m.scr, m.st));
         qkv_rope_kernel<<<grid_for((size_t)(m.nq + m.nkv) * m.hd / 2 + m.kvd), kThreads, 0, m.st>>>(
             m.qkv, m.zeros, ly.kc, ly.vc, m.state, m.nq, m.nkv, m.hd, m.c.theta);
-        attention_kernel<<<dim3(m.nq, 1), kThreads, attention_smem(m.c.ctx), m.st>>>(
-            m.qkv, m.qd, ly.kc, ly.vc, m.kvd, m.att, m.qd, m.state, m.hd, m.group, 1.0 / sqrt((double)m.hd), 0,
-            m.c.ctx);
-        TRY(cudaGetLastError());
+        TRY(decode_attention(m.qkv, ly.kc, ly.vc, m.kvd, m.att, m.state, m.nq, m.hd, m.group,
+                             1.0 / sqrt((double)m.hd), m.att_scr, m.st));
         TRY(tq_launch_matmul(ly.o, m.att + m.arow, m.y, 1, m.scr, m.st));
         if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
         residual_kernel<<<grid_for(d), kThreads, 0, m.st>>>(m.x, m.y, nullptr, d, d);
