@@ -263,6 +263,71 @@ __global__ void argmax_kernel(const float *logits, int n, int offset, int *cand,
     }
 }
 
+// Two-stage greedy pick for long logit vectors: block b finds the first
+// maximum of its contiguous slice (argmax_part_kernel), then one block takes
+// the best of the slices in order (argmax_final_kernel, same outputs as
+// argmax_kernel). Ties resolve to the lowest index either way.
+constexpr int kArgBlocks = 128;
+
+__global__ void argmax_part_kernel(const float *logits, int n, int *part) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const int per = (n + gridDim.x - 1) / gridDim.x;
+    const int lo = blockIdx.x * per, hi = min(n, lo + per);
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float v = logits[i];
+        if (v > best) best = v, idx = i;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
+    }
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) bv[w] = best, bi[w] = idx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); k++)
+            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) best = bv[k], idx = bi[k];
+        part[2 * blockIdx.x] = __float_as_int(best);
+        part[2 * blockIdx.x + 1] = idx;
+    }
+}
+
+__global__ void argmax_final_kernel(const int *part, int nparts, int offset, int *cand, int *state, int *tokens,
+                                    int set_pos, int final) {
+    if (threadIdx.x != 0) return;
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int k = 0; k < nparts; k++) {
+        const float v = __int_as_float(part[2 * k]);
+        const int i = part[2 * k + 1];
+        if (v > best || (v == best && i < idx)) best = v, idx = i;
+    }
+    if (idx == 0x7fffffff) idx = 0;
+    idx += offset;
+    cand[0] = __float_as_int(best);
+    cand[1] = idx;
+    if (final) {
+        tokens[state[2]] = idx;
+        state[0] = idx;
+        state[1] = set_pos >= 0 ? set_pos : state[1] + 1;
+        state[2] += 1;
+    }
+}
+
+// argmax over n logits into cand (and the state when final), part: 2 *
+// kArgBlocks ints of scratch.
+inline cudaError_t greedy_pick(const float *logits, int n, int offset, int *part, int *cand, int *state, int *tokens,
+                               int set_pos, int final, cudaStream_t st) {
+    argmax_part_kernel<<<kArgBlocks, 256, 0, st>>>(logits, n, part);
+    argmax_final_kernel<<<1, 32, 0, st>>>(part, kArgBlocks, offset, cand, state, tokens, set_pos, final);
+    return cudaGetLastError();
+}
+
 // The best of w candidates (value, global index) from the shards of a
 // column-split head: larger value, ties to the lower index. Advances the
 // state like argmax_kernel's final form.

@@ -44,11 +44,18 @@ __global__ void embed_kernel(const float *wte, const float *wpe, const int *stat
         x[(size_t)r * d + i] = __fadd_rn(wte[(size_t)tok * d + i], wpe[(size_t)pos * d + i]);
 }
 
-// layernorm (model.go:135-153) of row blockIdx.x.
-__global__ void layernorm_kernel(const float *x, const float *w, const float *b, float *out, int n) {
+// layernorm (model.go:135-153) of row blockIdx.x. With y (decode, one row):
+// first the residual add x += y + yb (model.go:229-231 / 242-244), then the
+// norm of the new x, in one launch.
+__global__ void layernorm_kernel(float *x, const float *w, const float *b, float *out, int n, const float *y = nullptr,
+                                 const float *yb = nullptr) {
     __shared__ double sh[32];
-    const float *xr = x + (size_t)blockIdx.x * n;
+    float *xr = x + (size_t)blockIdx.x * n;
     float *o = out + (size_t)blockIdx.x * n;
+    if (y) {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __fadd_rn(xr[i], __fadd_rn(y[i], yb[i]));
+        __syncthreads();
+    }
     double s = 0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) s = __dadd_rn(s, (double)xr[i]);
     const double mean = __ddiv_rn(block_reduce_d(s, sh, 0), (double)n);
@@ -173,7 +180,7 @@ struct Gpt2 {
     // prefill buffers (max_prompt rows)
     int max_prompt = 0;
     float *X = nullptr, *XN = nullptr, *QKV = nullptr, *ATT = nullptr, *Y = nullptr, *H = nullptr;
-    int *state = nullptr, *tokens = nullptr, *d_prompt = nullptr, *cand = nullptr;
+    int *state = nullptr, *tokens = nullptr, *d_prompt = nullptr, *cand = nullptr, *part = nullptr;
     AttScratch att_scr;
     cudaGraphExec_t graph = nullptr;
     std::vector<void *> allocs;
@@ -274,6 +281,7 @@ cudaError_t build(Gpt2 &m, uint64_t seed, float sigma, int *rc) {
     TRY(dalloc(m, (void **)&m.logits, sizeof(float) * c.vocab));
     TRY(dalloc(m, (void **)&m.state, sizeof(int) * 4));
     TRY(dalloc(m, (void **)&m.cand, sizeof(int) * 2));
+    TRY(dalloc(m, (void **)&m.part, sizeof(int) * 2 * kArgBlocks));
     void *ab = nullptr;
     TRY(dalloc(m, &ab, att_scratch_bytes(c.n_head, c.ctx, d / c.n_head)));
     m.att_scr = att_scratch(ab, c.n_head, c.ctx, d / c.n_head);
@@ -339,25 +347,24 @@ cudaError_t prefill(Gpt2 &m, const int *prompt, int T) {
 cudaError_t decode_step(Gpt2 &m) {
     const int d = m.c.d, ffn = m.c.ffn, hd = d / m.c.n_head;
     embed_kernel<<<1, kThreads, 0, m.st>>>(m.wte, m.wpe, m.state, nullptr, m.x, d);
+    const float *pend = nullptr, *pendb = nullptr; // residual still to be added to x
     for (Block &bl : m.b) {
-        layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, bl.ln1w, bl.ln1b, m.xn, d);
+        layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, bl.ln1w, bl.ln1b, m.xn, d, pend, pendb);
         TRY(tq_launch_matmul(bl.attn.q, m.xn, m.qkv, 1, m.scr, m.st));
         qkv_post_kernel<<<1, kThreads, 0, m.st>>>(m.qkv, bl.attnB, bl.kc, bl.vc, m.state, d, 0);
         TRY(decode_attention(m.qkv, bl.kc, bl.vc, d, m.att, m.state, m.c.n_head, hd, 1, 0.125 /* 1/sqrt(64) */,
                              m.att_scr, m.st));
         TRY(tq_launch_matmul(bl.proj.q, m.att, m.y, 1, m.scr, m.st));
-        residual_kernel<<<grid_for(d), kThreads, 0, m.st>>>(m.x, m.y, bl.projB, d, d);
-        layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, bl.ln2w, bl.ln2b, m.xn, d);
+        layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, bl.ln2w, bl.ln2b, m.xn, d, m.y, bl.projB);
         TRY(tq_launch_matmul(bl.fc.q, m.xn, m.h, 1, m.scr, m.st));
         bias_gelu_kernel<<<grid_for(ffn), kThreads, 0, m.st>>>(m.h, bl.fcB, ffn, ffn);
         TRY(tq_launch_matmul(bl.fc2.q, m.h, m.y, 1, m.scr, m.st));
-        residual_kernel<<<grid_for(d), kThreads, 0, m.st>>>(m.x, m.y, bl.fc2B, d, d);
+        pend = m.y, pendb = bl.fc2B;
         TRY(cudaGetLastError());
     }
-    layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, m.lnfw, m.lnfb, m.xn, d);
+    layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.x, m.lnfw, m.lnfb, m.xn, d, pend, pendb);
     TRY(tq_launch_matmul(m.wteT.q, m.xn, m.logits, 1, m.scr, m.st));
-    argmax_kernel<<<1, 1024, 0, m.st>>>(m.logits, m.c.vocab, 0, m.cand, m.state, m.tokens, -1, 1);
-    return cudaGetLastError();
+    return greedy_pick(m.logits, m.c.vocab, 0, m.part, m.cand, m.state, m.tokens, -1, 1, m.st);
 }
 
 cudaError_t capture_step(Gpt2 &m) {

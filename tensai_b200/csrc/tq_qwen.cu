@@ -84,11 +84,16 @@ __global__ void embed_row_kernel(const float *embed, const int *state, float *x,
 }
 
 // rmsnorm (model.go:182-193): sum of squares in float64, out = float32(v *
-// inv) * w.
-__global__ void rmsnorm_kernel(const float *x, const float *w, float *out, int n, double eps) {
+// inv) * w. With y: first the residual add x += y (model.go:276-278 /
+// 301-303), then the norm of the new x, in one launch.
+__global__ void rmsnorm_kernel(float *x, const float *y, const float *w, float *out, int n, double eps) {
     __shared__ double sh[32];
     double ss = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = __dadd_rn(ss, __dmul_rn((double)x[i], (double)x[i]));
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = y ? __fadd_rn(x[i], y[i]) : x[i];
+        if (y) x[i] = v;
+        ss = __dadd_rn(ss, __dmul_rn((double)v, (double)v));
+    }
     ss = block_reduce_d(ss, sh, 0);
     const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)n), eps)));
     for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn((float)__dmul_rn((double)x[i], inv), w[i]);
@@ -186,7 +191,7 @@ struct Qwen {
     std::vector<Layer> L;
     TqMatrixDev lm{};
     float *x, *a, *qkv, *att, *y, *gu, *h, *logits;
-    int *state = nullptr, *tokens = nullptr, *cand = nullptr, *cands = nullptr, *prompt = nullptr;
+    int *state = nullptr, *tokens = nullptr, *cand = nullptr, *cands = nullptr, *prompt = nullptr, *part = nullptr;
     AttScratch att_scr;
     int prompt_cap = 0;
     cudaGraphExec_t graph = nullptr;
@@ -319,6 +324,7 @@ cudaError_t build(Qwen &m, uint64_t seed, float sigma, int *rc) {
     TRY(dalloc(m, (void **)&m.tokens, sizeof(int) * (size_t)(c.ctx + 1)));
     TRY(dalloc(m, (void **)&m.cand, sizeof(int) * 2));
     TRY(dalloc(m, (void **)&m.cands, sizeof(int) * 2 * m.world));
+    TRY(dalloc(m, (void **)&m.part, sizeof(int) * 2 * kArgBlocks));
     void *ab = nullptr;
     TRY(dalloc(m, &ab, att_scratch_bytes(m.nq, c.ctx, m.hd)));
     m.att_scr = att_scratch(ab, m.nq, c.ctx, m.hd);
@@ -332,8 +338,9 @@ cudaError_t nccl_err(ncclResult_t r) { return r == ncclSuccess ? cudaSuccess : c
 cudaError_t step(Qwen &m, int n_prompt) {
     const int d = m.c.d;
     embed_row_kernel<<<1, kThreads, 0, m.st>>>(m.embed, m.state, m.x, d);
+    const float *pending = nullptr; // residual still to be added to x (the previous down_proj output)
     for (Layer &ly : m.L) {
-        rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.x, m.ones, m.a, d, m.c.eps);
+        rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.x, pending, m.ones, m.a, d, m.c.eps);
         TRY(tq_launch_matmul(ly.qkv, m.a, m.qkv, 1, m.scr, m.st));
         qkv_rope_kernel<<<grid_for((size_t)(m.nq + m.nkv) * m.hd / 2 + m.kvd), kThreads, 0, m.st>>>(
             m.qkv, m.zeros, ly.kc, ly.vc, m.state, m.nq, m.nkv, m.hd, m.c.theta);
@@ -341,19 +348,17 @@ cudaError_t step(Qwen &m, int n_prompt) {
                              1.0 / sqrt((double)m.hd), m.att_scr, m.st));
         TRY(tq_launch_matmul(ly.o, m.att + m.arow, m.y, 1, m.scr, m.st));
         if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
-        residual_kernel<<<grid_for(d), kThreads, 0, m.st>>>(m.x, m.y, nullptr, d, d);
-        rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.x, m.ones, m.a, d, m.c.eps);
+        rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.x, m.y, m.ones, m.a, d, m.c.eps); // x += o_proj, then norm
         TRY(tq_launch_matmul(ly.gu, m.a, m.gu, 1, m.scr, m.st));
         silu_mul_kernel<<<grid_for(m.fcols), kThreads, 0, m.st>>>(m.gu, m.h, m.fcols);
         TRY(tq_launch_matmul(ly.down, m.h, m.y, 1, m.scr, m.st));
         if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
-        residual_kernel<<<grid_for(d), kThreads, 0, m.st>>>(m.x, m.y, nullptr, d, d);
+        pending = m.y;
         TRY(cudaGetLastError());
     }
-    rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.x, m.ones, m.a, d, m.c.eps);
+    rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.x, pending, m.ones, m.a, d, m.c.eps);
     TRY(tq_launch_matmul(m.lm, m.a, m.logits, 1, m.scr, m.st));
-    argmax_kernel<<<1, 1024, 0, m.st>>>(m.logits, m.vcols, m.voff, m.cand, m.state, m.tokens, -1, 0);
-    TRY(cudaGetLastError());
+    TRY(greedy_pick(m.logits, m.vcols, m.voff, m.part, m.cand, m.state, m.tokens, -1, 0, m.st));
     if (m.world > 1)
         TRY(nccl_err(g_nccl.allGather(m.cand, m.cands, 2, ncclInt32, m.comm, m.st)));
     else
