@@ -78,6 +78,45 @@ TQ_HD size_t tq_scale4_offset(int units, int u, int hi, int p) {
     return ((size_t)(p / TQ_TILE_BYTES) * units + u) * (2 * TQ_TILE_BYTES) + hi * TQ_TILE_BYTES + (p % TQ_TILE_BYTES);
 }
 
+#ifdef __CUDACC__
+// Stream-K split of `items` work items (column tile, 64-row unit), tile-major,
+// over G <= items persistent CTAs: CTA c owns [start(c), start(c + 1)) with
+// start(c) = floor(items * c / G), so column tile t (items [t0, t1)) is shared
+// by CTAs owner(t0) .. owner(t1 - 1). 32-bit division whenever items * G < 2^32.
+struct TqSplit {
+    long long items;
+    int G;
+    bool narrow;
+    __device__ __forceinline__ TqSplit(long long n, int g)
+        : items(n), G(g), narrow((unsigned long long)n * (unsigned)g < (1ull << 32)) {}
+    __device__ __forceinline__ long long start(int c) const {
+        return narrow ? (long long)((unsigned)items * (unsigned)c / (unsigned)G) : items * c / G;
+    }
+    // The largest c with start(c) <= it: floor(((it + 1) * G - 1) / items).
+    __device__ __forceinline__ int owner(long long it) const {
+        return narrow ? (int)(((unsigned)(it + 1) * (unsigned)G - 1u) / (unsigned)items)
+                      : (int)(((it + 1) * G - 1) / items);
+    }
+    // Partial-sum slot of contributor c to the tile starting at item t0: 2c for
+    // a slice that starts inside the tile (its first segment), 2c + 1 for one
+    // that started before it (its last segment). Only owner(t0) can be the latter.
+    __device__ __forceinline__ int slot(int c, long long t0) const { return 2 * c + (start(c) >= t0 ? 0 : 1); }
+};
+
+// One CTA's arrival at a shared tile's counter, by one thread after a barrier
+// that orders the CTA's partial-sum stores before it. acq_rel at gpu scope
+// publishes those stores and, for the last of n arrivals, acquires every other
+// contributor's; a barrier after this call extends that to the whole CTA. The
+// last arrival re-arms the counter for the next launch on the stream.
+__device__ __forceinline__ bool tq_arrive_last(unsigned *counter, unsigned n) {
+    unsigned prev;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
+    const bool last = prev == n - 1;
+    if (last) asm volatile("st.relaxed.gpu.u32 [%0], %1;" ::"l"(counter), "r"(0u) : "memory");
+    return last;
+}
+#endif
+
 static inline int tq_row_bytes(int bits, int cols) { return bits == 8 ? cols : cols / 2; }
 static inline int tq_tiles(int bits, int cols) { return (tq_row_bytes(bits, cols) + TQ_TILE_BYTES - 1) / TQ_TILE_BYTES; }
 static inline int tq_units(int rows) { return (rows + TQ_GROUP - 1) / TQ_GROUP; }

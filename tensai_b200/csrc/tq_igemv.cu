@@ -217,7 +217,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ long long item_start(long long items, int c, int ctas) { return items * c / ctas; }
 
 // Instruction descriptor of tcgen05.mma.kind::i8: D s32, A = codes (s8 for
 // int8, u8 for int4; MN-major), B = digits (s8, K-major), M = 128, N.
@@ -330,7 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, c = blockIdx.x;
-    const long long i0 = item_start(p.items, c, G), i1 = item_start(p.items, c + 1, G);
+    const TqSplit split(p.items, G);
+    const long long i0 = split.start(c), i1 = split.start(c + 1);
     const BatchWalk walk0{(int)(i0 / p.units), (int)(i0 % p.units), (int)(i1 - i0), p.units};
     int nbatches = 0;
     {
@@ -577,34 +577,21 @@ __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
 #pragma unroll
                     for (int m = 0; m < M; m++) acc[h][m] += red[(h * M + m) * kCols + col];
                 const long long t0 = (long long)tile * p.units, t1 = t0 + p.units;
-                int cf = (int)(t0 * G / p.items);
-                while (cf + 1 < G && item_start(p.items, cf + 1, G) <= t0) cf++;
-                while (cf > 0 && item_start(p.items, cf, G) > t0) cf--;
-                int cl = (int)((t1 - 1) * G / p.items);
-                while (cl + 1 < G && item_start(p.items, cl + 1, G) <= t1 - 1) cl++;
-                while (cl > 0 && item_start(p.items, cl, G) > t1 - 1) cl--;
+                const int cf = split.owner(t0), cl = split.owner(t1 - 1);
                 constexpr int SL = H * M * kCols; // partial entries per tile
                 bool write = true;
                 if (cf != cl) {
-                    const int slot = 2 * c + (i0 >= t0 ? 0 : 1);
-                    float *dst = p.partial + (size_t)slot * SL;
+                    float *dst = p.partial + (size_t)split.slot(c, t0) * SL;
 #pragma unroll
                     for (int h = 0; h < H; h++)
 #pragma unroll
                         for (int m = 0; m < M; m++) dst[(h * M + m) * kCols + col] = acc[h][m];
                     named_sync(2, kEpiThreads);
-                    if (et == 0) {
-                        // The barrier orders the warpgroup's partial stores before this
-                        // thread's fence (cumulativity); the fence publishes them at gpu scope.
-                        __threadfence();
-                        const unsigned prev = atomicAdd(&p.counters[tile], 1u);
-                        *lastflag = prev == (unsigned)(cl - cf);
-                        if (*lastflag) p.counters[tile] = 0;
-                    }
+                    if (et == 0) *lastflag = tq_arrive_last(&p.counters[tile], (unsigned)(cl - cf + 1));
                     named_sync(2, kEpiThreads);
                     write = *lastflag != 0;
                     if (write) {
-                        __threadfence();
+                        const int slot_f = split.slot(cf, t0);
 #pragma unroll
                         for (int h = 0; h < H; h++)
 #pragma unroll
@@ -615,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1) igemv_kernel(IgParams p) {
 #pragma unroll
                             for (int u = 0; u < 4; u++) {
                                 const int c2 = cc + u;
-                                const int sl = 2 * c2 + (c2 <= cl && item_start(p.items, c2, G) >= t0 ? 0 : 1);
+                                const int sl = c2 == cf ? slot_f : 2 * c2;
                                 const float *src = p.partial + (size_t)sl * SL;
 #pragma unroll
                                 for (int h = 0; h < H; h++)

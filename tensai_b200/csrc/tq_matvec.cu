@@ -185,7 +185,6 @@ template <int BITS, int M> struct Smem {
     static constexpr size_t total = bufs + xs + red + flag + mbar;
 };
 
-__device__ __forceinline__ long long item_start(long long items, int c, int ctas) { return items * c / ctas; }
 
 template <int BITS, int M>
 __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(QmvParams p) {
@@ -202,7 +201,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(QmvParams p) {
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, c = blockIdx.x;
-    const long long i0 = item_start(p.items, c, G), i1 = item_start(p.items, c + 1, G);
+    const TqSplit split(p.items, G);
+    const long long i0 = split.start(c), i1 = split.start(c + 1);
     uint8_t *wbuf = bufs + (size_t)warp * kStages * kBuf;
     float *wx = xs_all + (size_t)warp * 2 * M * kUnit;
     uint64_t *wbar = mbar + warp * kStages;
@@ -336,31 +336,17 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(QmvParams p) {
 
         // Which CTAs contribute to this tile, and is this one the last to arrive?
         const long long t0 = (long long)tile * p.units, t1 = t0 + p.units;
-        int cf = (int)(t0 * G / p.items);
-        while (cf + 1 < G && item_start(p.items, cf + 1, G) <= t0) cf++;
-        while (cf > 0 && item_start(p.items, cf, G) > t0) cf--;
-        int cl = (int)((t1 - 1) * G / p.items);
-        while (cl + 1 < G && item_start(p.items, cl + 1, G) <= t1 - 1) cl++;
-        while (cl > 0 && item_start(p.items, cl, G) > t1 - 1) cl--;
+        const int cf = split.owner(t0), cl = split.owner(t1 - 1);
         const bool shared_tile = cf != cl;
         const float *src = red;
         if (shared_tile) {
-            const int slot = 2 * c + (i0 >= t0 ? 0 : 1);
-            float *dst = p.partial + (size_t)slot * SLOTS;
+            float *dst = p.partial + (size_t)split.slot(c, t0) * SLOTS;
             __syncthreads();
             for (int idx = threadIdx.x; idx < SLOTS; idx += kThreads) dst[idx] = red[idx];
             __syncthreads();
-            if (threadIdx.x == 0) {
-                // The barrier orders the CTA's partial stores before this thread's
-                // fence (cumulativity); the fence publishes them at gpu scope.
-                __threadfence();
-                const unsigned prev = atomicAdd(&p.counters[tile], 1u);
-                flag[0] = prev == (unsigned)(cl - cf);
-                if (flag[0]) p.counters[tile] = 0; // every contributor has arrived: re-arm
-            }
+            if (threadIdx.x == 0) flag[0] = tq_arrive_last(&p.counters[tile], (unsigned)(cl - cf + 1));
             __syncthreads();
             if (!flag[0]) src = nullptr;
-            else __threadfence();
         } else {
             __syncthreads();
         }
@@ -371,12 +357,13 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(QmvParams p) {
                 if (shared_tile) {
                     // contributors in CTA order, four loads in flight
                     s = 0.f;
+                    const int slot_f = split.slot(cf, t0);
                     for (int cc = cf; cc <= cl; cc += 4) {
                         float pv[4];
 #pragma unroll
                         for (int u = 0; u < 4; u++) {
                             const int c2 = cc + u;
-                            const int slot = 2 * c2 + (c2 <= cl && item_start(p.items, c2, G) >= t0 ? 0 : 1);
+                            const int slot = c2 == cf ? slot_f : 2 * c2;
                             pv[u] = c2 <= cl ? __ldcg(p.partial + (size_t)slot * SLOTS + idx) : 0.f;
                         }
 #pragma unroll

@@ -114,13 +114,9 @@ __device__ __forceinline__ float magic_byte(uint32_t t, int e) {
 }
 
 // The contributing CTAs [cf, cl] of the tile whose items are [t0, t1).
-__device__ __forceinline__ void tile_ctas(long long items, int G, long long t0, long long t1, int &cf, int &cl) {
-    cf = (int)(t0 * G / items);
-    while (cf + 1 < G && item_start(items, cf + 1, G) <= t0) cf++;
-    while (cf > 0 && item_start(items, cf, G) > t0) cf--;
-    cl = (int)((t1 - 1) * G / items);
-    while (cl + 1 < G && item_start(items, cl + 1, G) <= t1 - 1) cl++;
-    while (cl > 0 && item_start(items, cl, G) > t1 - 1) cl--;
+__device__ __forceinline__ void tile_ctas(const TqSplit &split, long long t0, long long t1, int &cf, int &cl) {
+    cf = split.owner(t0);
+    cl = split.owner(t1 - 1);
 }
 
 template <int BITS, int NP>
@@ -139,7 +135,8 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmParams p) {
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, c = blockIdx.x;
-    const long long i0 = item_start(p.items, c, G), i1 = item_start(p.items, c + 1, G);
+    const TqSplit split(p.items, G);
+    const long long i0 = split.start(c), i1 = split.start(c + 1);
     const int n = (int)(i1 - i0);
 
     if (threadIdx.x == 0) {
@@ -350,11 +347,11 @@ __global__ void __launch_bounds__(kThreads, 1) mm_kernel(MmParams p) {
             const long long s1 = t1 < i1 ? t1 : i1;
             const int b = seg % NB;
             int cf, cl;
-            tile_ctas(p.items, G, t0, t1, cf, cl);
+            tile_ctas(split, t0, t1, cf, cl);
             const bool shared = cf != cl;
             const bool ok = wait_bar(&accfull[b], (seg / NB) & 1, abort, p.status);
             tc_fence_after();
-            float *dst = p.partial + (size_t)(2 * c + (i0 >= t0 ? 0 : 1)) * SL;
+            float *dst = p.partial + (size_t)split.slot(c, t0) * SL;
             const int base = tile * kCols + col; // byte column of this thread in the reference row
             // int8: sum x*code, then times the column scale (quant.go:120); shared
             // tiles are scaled after their cross-CTA sum.
@@ -406,7 +403,8 @@ __global__ void __launch_bounds__(128) mm_reduce_kernel(MmParams p, int ctas) {
     const int tile = blockIdx.x, h = blockIdx.y, m0 = blockIdx.z * RB, col = threadIdx.x;
     const long long t0 = (long long)tile * p.units, t1 = t0 + p.units;
     int cf, cl;
-    tile_ctas(p.items, ctas, t0, t1, cf, cl);
+    const TqSplit split(p.items, ctas);
+    tile_ctas(split, t0, t1, cf, cl);
     if (cf == cl) return; // written by the tile's only CTA
     const int b = tile * kCols + col;
     if (!(BITS == 8 ? b < p.cols : b < p.half)) return;
@@ -414,12 +412,13 @@ __global__ void __launch_bounds__(128) mm_reduce_kernel(MmParams p, int ctas) {
     float sum[RB];
 #pragma unroll
     for (int r = 0; r < RB; r++) sum[r] = 0.f;
+    const int slot_f = split.slot(cf, t0);
     for (int c2 = cf; c2 <= cl; c2 += 8) { // contributors in CTA order, 8 x RB loads in flight
         float pv[8][RB];
 #pragma unroll
         for (int u = 0; u < 8; u++) {
             const int cu = c2 + u;
-            const int sl = 2 * cu + (cu <= cl && item_start(p.items, cu, ctas) >= t0 ? 0 : 1);
+            const int sl = cu == cf ? slot_f : 2 * cu;
             const float *src = p.partial + (size_t)sl * SL + (size_t)(h * NP + m0) * kCols + col;
 #pragma unroll
             for (int r = 0; r < RB; r++) pv[u][r] = cu <= cl && m0 + r < p.m ? __ldcg(src + r * kCols) : 0.f;

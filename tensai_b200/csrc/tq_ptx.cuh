@@ -117,7 +117,4 @@ __device__ __forceinline__ uint32_t to_tf32(float f) {
 // overflow): add half a tf32 unit in the last place, clear the 13 low bits.
 __device__ __forceinline__ uint32_t tf32_rna_bits(float f) { return (__float_as_uint(f) + 0x1000u) & 0xFFFFE000u; }
 
-// First item of CTA c in an even split of `items` over `ctas`.
-__device__ __forceinline__ long long item_start(long long items, int c, int ctas) { return items * c / ctas; }
-
 } // namespace tqp
