@@ -355,6 +355,8 @@ def run_gpu(args, rank: int, world: int):
     torch.cuda.set_device(dev)
     L = _lib.load()
     _lib.check(L.tq_set_device(dev))
+    if args.kernel is not None:
+        _lib.check(L.tq_set_matvec_kernel(args.kernel))
 
     # Resident weights: generated and quantized on the device.
     handles = []
@@ -508,6 +510,8 @@ def main():
                     help="resident MLP pairs per step (default 32 = 1.63 GB; small values for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-side-configs", action="store_true")
+    ap.add_argument("--kernel", type=int, default=None,
+                    help="matvec kernel for M <= 15 (tq_set_matvec_kernel); default: the library's")
     args = ap.parse_args()
     args.steps = max(args.steps, 1)
     LAYERS = max(1, args.layers)

@@ -141,19 +141,42 @@ static cudaError_t read_status(const TqScratch &scr, cudaStream_t st, unsigned *
     return e;
 }
 
-// 0: tensor-core matvec (tq_igemv.cu, default); 1: CUDA-core matvec (tq_matvec.cu).
+// Matvec kernel for M <= 15 rows (tq_set_matvec_kernel):
+//   0 (default): single-launch CUDA-core matvec (tq_cmv.cu) for M <= 2, the
+//                tensor-core matvec (tq_igemv.cu) for 3 <= M <= 15;
+//   1: CUDA-core matvec with per-warp copies (tq_matvec.cu);
+//   2: single-launch tensor-core matvec (tq_gemv.cu);
+//   3: single-launch CUDA-core matvec (tq_cmv.cu), 2 rows per launch;
+//   4: tensor-core matvec with a digit-plane launch (tq_igemv.cu).
 std::atomic<int> g_matvec_kernel{0};
 
 // M >= TQ_MM_MIN_ROWS: the tf32 tensor-core matmul; fewer rows: the matvec
-// kernel chosen by tq_set_matvec_kernel (8 rows per launch).
+// kernel chosen by tq_set_matvec_kernel.
 static cudaError_t launch_matvec(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                                  cudaStream_t st) {
     if (M >= TQ_MM_MIN_ROWS) return tq_launch_mm(m, x, out, M, scr, st);
-    return g_matvec_kernel.load() == 1 ? tq_launch_matvec(m, x, out, M, scr, st)
-                                       : tq_launch_igemv(m, x, out, M, scr, st);
+    switch (g_matvec_kernel.load()) {
+    case 1: return tq_launch_matvec(m, x, out, M, scr, st);
+    case 2: return tq_launch_gemv(m, x, out, M, scr, st);
+    case 3: return tq_launch_cmv(m, x, out, M, scr, st);
+    case 4: return tq_launch_igemv(m, x, out, M, scr, st);
+    default: return M <= 2 ? tq_launch_cmv(m, x, out, M, scr, st) : tq_launch_igemv(m, x, out, M, scr, st);
+    }
 }
 
 int tq_scratch_for(int device, cudaStream_t st, TqScratch *out, int m) { return scratch_for(device, st, out, m); }
+
+// Frees the scratch of (device, stream) and forgets it; for owners of a
+// stream (the decode engines) before they destroy it, with its work finished.
+void tq_scratch_release(int device, cudaStream_t st) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    auto it = g_scratch.find(std::make_pair(device, st));
+    if (it == g_scratch.end()) return;
+    TqScratch &s = it->second;
+    for (void *p : {(void *)s.partial, (void *)s.counters, (void *)s.planes, (void *)s.mm_partial})
+        if (p) cudaFree(p);
+    g_scratch.erase(it);
+}
 
 cudaError_t tq_read_status(const TqScratch &scr, cudaStream_t st, unsigned *out) { return read_status(scr, st, out); }
 
@@ -562,13 +585,19 @@ int tq_device_status(unsigned *bits) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     for (auto &kv : g_scratch) {
         if (kv.first.first != t_device) continue;
-        if ((e = read_status(kv.second, kv.first.second, bits)) != cudaSuccess) return tq_cuda_fail(e, "status read");
+        // after the device synchronize: plain synchronous copies, so no
+        // registered stream handle is used (a caller's stream may be gone)
+        unsigned v = 0;
+        e = cudaMemcpy(&v, kv.second.status, sizeof v, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && v) e = cudaMemset(kv.second.status, 0, sizeof v);
+        if (e != cudaSuccess) return tq_cuda_fail(e, "status read");
+        *bits |= v;
     }
     return TQ_OK;
 }
 
 int tq_set_matvec_kernel(int which) {
-    if (which != 0 && which != 1) return tq_fail(TQ_ERR_ARG, "tensai: matvec kernel must be 0 or 1, got %d", which);
+    if (which < 0 || which > 4) return tq_fail(TQ_ERR_ARG, "tensai: matvec kernel must be 0..4, got %d", which);
     g_matvec_kernel.store(which);
     return TQ_OK;
 }

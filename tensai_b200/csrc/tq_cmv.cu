@@ -1,0 +1,695 @@
+// tq_cmv.cu — weight-only int8 / int4 matvec for M <= 2 activation rows on the
+// CUDA cores, one launch per call, HBM-bound.
+//
+// Computes out[m][j] = sum_i x[m][i] * W[i][j], the product of qmatvecCols
+// (quant_simd.go:12-48) and q4matvecCols (quant4_simd.go:17-57):
+//   int8: acc_j = sum_i x_i * q_ij, out_j = acc_j * scale_j (quant.go:120);
+//   int4: per 64-row group g, tmp_j = sum_{i in g} x_i * (nib_ij - 8), then
+//         acc_j = fma(tmp_j, scale_gj, acc_j), the fold of quant4_simd.go:46-50.
+//
+// Why the CUDA cores: a tcgen05.mma of M = 128 rows costs about 170 cycles
+// whatever its N, so a matvec (N = one activation row) pays 170 cycles per
+// 4 KB of codes on the tensor cores, more than HBM needs to deliver them. Here
+// a code costs about 2.3 instructions:
+//   int4: each nibble becomes a float with one LOP3 by OR-ing it, in place,
+//         under the exponent of 2^23 (the float 2^23 + 16^k n for the nibble at
+//         bits 4k..4k+3, k < 5; the top three nibbles after one shift), one
+//         packed f32x2 add removes 2^23 + 16^k * 8 exactly, and packed f32x2
+//         FMAs accumulate 16^k (n - 8) x. The power of two 16^k is taken out
+//         exactly by folding 16^-k into the group scale: fma(16^k tmp,
+//         scale * 16^-k, acc) == fma(tmp, scale, acc) bit for bit.
+//   int8: byte_perm puts each signed byte (xor 0x80) under the exponent of
+//         2^23; a packed add removes 2^23 + 128.
+//
+// Schedule. One persistent CTA per SM takes an equal contiguous slice of the
+// tile-major item list (8 KB items: 64 rows x 128 code bytes; stream-K,
+// balanced to +-1 item). A producer warp streams the slice's items (int4:
+// with their 1 KB of scales) through a ring of up to 25 slots by bulk copies,
+// from kernel start: the weights do not depend on the previous kernel, so the
+// ring fills while it finishes (programmatic dependent launch). Sixteen
+// consumer warps take the slice's items round robin; lane l owns code bytes
+// 4l..4l+3 of every row (int4: 8 columns, int8: 4). Activations of an item
+// (64 rows x M) go through a per-warp shared slot, duplicated for the packed
+// FMAs, loaded one item ahead.
+//
+// Reductions, all in a fixed order (results are bit-reproducible run to run):
+//   * per tile segment (the slice's items of one column tile), each warp
+//     deposits its sums in a shared buffer; the last warp to deposit adds the
+//     deposits in warp order;
+//   * a tile wholly inside the slice is written at once; a tile shared with
+//     other CTAs goes through scratch partials and an acq_rel arrival counter,
+//     and the last CTA to arrive adds all partials in CTA order. The slice's
+//     first segment, when shared and not also its last, is published by a
+//     fixup warp so the consumers do not wait on global memory ordering.
+// Every wait is bounded (tqp::kWaitNs); a timeout sets TQ_STATUS_TIMEOUT and an
+// abort flag that turns later waits into no-ops.
+#include "tq_ptx.cuh"
+
+namespace {
+
+using namespace tqp;
+
+constexpr int kItem = TQ_ITEM_BYTES; // 8192
+constexpr int kRows = TQ_GROUP;      // 64
+constexpr int kCols = TQ_TILE_BYTES; // 128
+constexpr int W = 8;                 // consumer warps
+constexpr int WI = W / 2;            // item streams: warps 2i and 2i + 1 take the two 32-row halves of an item
+constexpr int kHalf = TQ_GROUP / 2;  // rows per half item
+constexpr int kThreads = (W + 2) * 32;
+// Shared memory per CTA, small enough for two CTAs per SM: the next kernel on
+// the stream (programmatic dependent launch) is resident while this one
+// computes and reduces, and fills its ring meanwhile.
+constexpr int kSmemCap = 113 * 1024; // 2 x (113 + 1 reserved) KB <= 228 KB per SM
+
+template <int BITS, int M> struct CCfg {
+    static constexpr int NP = BITS == 8 ? 4 : 8;       // columns per lane
+    static constexpr int E = M * NP * 32;              // sums of one tile segment
+    static constexpr int SLOT = BITS == 4 ? kItem + 1024 : kItem; // codes (+ int4 scales)
+    static constexpr int XD = 4;                      // per-warp activation ring (half items)
+    static constexpr int XSLOT = XD * kHalf * M * 4;  // [XD][M][32] floats per warp
+    static constexpr int RED = 2 * W * E * 4;          // two deposit buffers
+    static constexpr int HAND = E * 4;
+    static constexpr int FIXED = W * XSLOT + RED + HAND + 1024;
+    static constexpr int R0 = (kSmemCap - FIXED) / SLOT;
+    static constexpr int R = R0 < 16 ? R0 : 16;       // ring slots
+    static constexpr int RING_OFF = 0;
+    static constexpr int X_OFF = R * SLOT;
+    static constexpr int RED_OFF = X_OFF + W * XSLOT;
+    static constexpr int HAND_OFF = RED_OFF + RED;
+    static constexpr int BAR_OFF = HAND_OFF + HAND;
+    static constexpr int MISC_OFF = BAR_OFF + (2 * R + 1) * 8;
+    static constexpr int SMEM = MISC_OFF + 64;
+    static_assert(R >= 6, "ring too shallow");
+    static_assert(SMEM <= kSmemCap, "shared memory budget");
+};
+
+struct CmvParams {
+    const uint8_t *codes;
+    const float *scale;
+    const float *x;
+    float *out;
+    float *partial;
+    unsigned *counters;
+    unsigned *status;
+    long long items;
+    int rows, cols, half, units, tiles;
+    uint32_t magic; // 0x4B000000 (2^23), passed in so it sits in a register: one LOP3 per nibble
+};
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void named_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// 4-byte global -> shared async copy; src_size 0 writes a zero.
+__device__ __forceinline__ void cp_async_f32(float *dst, const float *src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// The float 2^23 + (w & mask), exact for a mask inside bits 0..22 (magic = 2^23's bits).
+__device__ __forceinline__ float mag(uint32_t w, uint32_t mask, uint32_t magic) { return __uint_as_float((w & mask) | magic); }
+// Byte e of t under the exponent of 2^23: the float 2^23 + byte, exact.
+__device__ __forceinline__ float mag_byte(uint32_t t, int e) { return __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7440 + e)); }
+
+// int4 column order of a lane's 8 sums: pairs (lo0, lo1), (lo2, lo3),
+// (hi0, hi1), (hi2, hi3); lo e = low nibble of byte e (column pair 4l + e),
+// hi e = its high nibble. The nibble at bits 4k..4k+3 carries 16^k:
+//   lo0 k=0, hi0 k=1, lo1 k=2, hi1 k=3, lo2 k=4 (bits 0..19 of w), then
+//   w >> 20: hi2 k=0, lo3 k=1, hi3 k=2.
+__device__ __forceinline__ float pos_scale(int j) { // 16^-k of sum j (j = 0..7 in the order above)
+    // lo0 lo1 lo2 lo3 hi0 hi1 hi2 hi3
+    constexpr float s[8] = {1.f, 1.f / 256.f, 1.f / 65536.f, 1.f / 16.f, 1.f / 16.f, 1.f / 4096.f, 1.f, 1.f / 256.f};
+    return s[j];
+}
+
+// Code rows r and r + 1 of a lane (words w0, w1) into its column sums:
+// t[m][j] = (sum over even rows, sum over odd rows) of column j, packed so
+// that one f32x2 FMA takes both rows against (x_r, x_r+1). int4: 8 columns in
+// the order lo0 lo1 lo2 lo3 hi0 hi1 hi2 hi3; int8: 4 columns (bytes 0..3).
+template <int BITS, int M>
+__device__ __forceinline__ void row_pair(uint32_t w0, uint32_t w1, const float2 (&xp)[M],
+                                         float2 (&t)[M][BITS == 8 ? 4 : 8], uint32_t mg) {
+    if (BITS == 4) {
+        const uint32_t v0 = w0 >> 20, v1 = w1 >> 20;
+        float2 c[8];
+        c[0] = __fadd2_rn(f2(mag(w0, 0xFu, mg), mag(w1, 0xFu, mg)), f2(-8388616.0f, -8388616.0f));          // 2^23 + n
+        c[1] = __fadd2_rn(f2(mag(w0, 0xF00u, mg), mag(w1, 0xF00u, mg)), f2(-8390656.0f, -8390656.0f));      // 2^23 + 256 n
+        c[2] = __fadd2_rn(f2(mag(w0, 0xF0000u, mg), mag(w1, 0xF0000u, mg)), f2(-8912896.0f, -8912896.0f));  // 2^23 + 65536 n
+        c[3] = __fadd2_rn(f2(mag(v0, 0xF0u, mg), mag(v1, 0xF0u, mg)), f2(-8388736.0f, -8388736.0f));        // 2^23 + 16 n
+        c[4] = __fadd2_rn(f2(mag(w0, 0xF0u, mg), mag(w1, 0xF0u, mg)), f2(-8388736.0f, -8388736.0f));        // 2^23 + 16 n
+        c[5] = __fadd2_rn(f2(mag(w0, 0xF000u, mg), mag(w1, 0xF000u, mg)), f2(-8421376.0f, -8421376.0f));    // 2^23 + 4096 n
+        c[6] = __fadd2_rn(f2(mag(v0, 0xFu, mg), mag(v1, 0xFu, mg)), f2(-8388616.0f, -8388616.0f));          // 2^23 + n
+        c[7] = __fadd2_rn(f2(mag(v0, 0xF00u, mg), mag(v1, 0xF00u, mg)), f2(-8390656.0f, -8390656.0f));      // 2^23 + 256 n
+#pragma unroll
+        for (int m = 0; m < M; m++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) t[m][j] = __ffma2_rn(c[j], xp[m], t[m][j]);
+    } else {
+        const uint32_t u0 = w0 ^ 0x80808080u, u1 = w1 ^ 0x80808080u; // signed byte b -> b + 128
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float2 c = __fadd2_rn(f2(mag_byte(u0, e), mag_byte(u1, e)), f2(-8388736.0f, -8388736.0f));
+#pragma unroll
+            for (int m = 0; m < M; m++) t[m][e] = __ffma2_rn(c, xp[m], t[m][e]);
+        }
+    }
+}
+
+// Output column of sum j of lane `lane` in tile `tile` (int4: -1 if beyond N/2 pairs).
+template <int BITS>
+__device__ __forceinline__ int out_col(const CmvParams &p, int tile, int lane, int j) {
+    if (BITS == 8) {
+        const int col = tile * kCols + 4 * lane + j;
+        return col < p.cols ? col : -1;
+    }
+    const int e = j & 3, hi = j >> 2;
+    const int pair = tile * kCols + 4 * lane + e;
+    if (pair >= p.half) return -1;
+    return hi ? p.half + pair : pair;
+}
+
+// Sums of a finished tile (entry (m, j, lane) in the order [m][j][lane]) to the output.
+template <int BITS, int M>
+__device__ __forceinline__ void write_out(const CmvParams &p, int tile, int lane, const float (&v)[M][BITS == 8 ? 4 : 8]) {
+    constexpr int NP = BITS == 8 ? 4 : 8;
+#pragma unroll
+    for (int j = 0; j < NP; j++) {
+        const int col = out_col<BITS>(p, tile, lane, j);
+        if (col < 0) continue;
+        const float sc = BITS == 8 ? __ldg(p.scale + col) : 1.f;
+#pragma unroll
+        for (int m = 0; m < M; m++) p.out[(size_t)m * p.cols + col] = BITS == 8 ? v[m][j] * sc : v[m][j];
+    }
+}
+
+// A shared tile, by one warp (lane holds entries [m][j][lane]): publish this
+// CTA's sums, count in, and if last add every contributor in CTA order.
+template <int BITS, int M>
+__device__ void publish_shared(const CmvParams &p, const TqSplit &split, int c, int tile, int lane,
+                               const float (&v)[M][BITS == 8 ? 4 : 8]) {
+    constexpr int NP = BITS == 8 ? 4 : 8;
+    constexpr int E = M * NP * 32;
+    const long long t0 = (long long)tile * p.units;
+    const int cf = split.owner(t0), cl = split.owner(t0 + p.units - 1);
+    float *dst = p.partial + (size_t)split.slot(c, t0) * E + lane;
+#pragma unroll
+    for (int m = 0; m < M; m++)
+#pragma unroll
+        for (int j = 0; j < NP; j++) dst[(m * NP + j) * 32] = v[m][j];
+    // __syncwarp orders the lanes' stores before lane 0's cumulative acq_rel
+    // arrival; for the last CTA its acquire, then __syncwarp, orders the other
+    // CTAs' partials before the lanes' loads.
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = tq_arrive_last(&p.counters[tile], (unsigned)(cl - cf + 1)) ? 1 : 0;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();
+    if (!last) return;
+    const int slot_f = split.slot(cf, t0);
+    float s[M][NP];
+#pragma unroll
+    for (int m = 0; m < M; m++)
+#pragma unroll
+        for (int j = 0; j < NP; j++) s[m][j] = 0.f;
+    constexpr int CH = 32 / (M * NP) > 0 ? 32 / (M * NP) : 1; // contributors per round of loads
+    for (int cc = cf; cc <= cl; cc += CH) {
+        float pv[CH][M][NP];
+#pragma unroll
+        for (int u = 0; u < CH; u++) {
+            const int c2 = cc + u;
+            const float *src = p.partial + (size_t)(c2 == cf ? slot_f : 2 * c2) * E + lane;
+#pragma unroll
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int j = 0; j < NP; j++) pv[u][m][j] = c2 <= cl ? __ldcg(src + (m * NP + j) * 32) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < CH; u++)
+#pragma unroll
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int j = 0; j < NP; j++) s[m][j] += pv[u][m][j];
+    }
+    write_out<BITS, M>(p, tile, lane, s);
+}
+
+template <int BITS, int M>
+__global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
+    using C = CCfg<BITS, M>;
+    constexpr int R = C::R, NP = C::NP, E = C::E;
+    // 16-byte alignment is all the bulk copies and vector loads need; indexing
+    // the array directly keeps every access in the shared state space.
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *empty = full + R;
+    uint64_t *hand_full = empty + R;
+    volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF);
+    int *cnt = reinterpret_cast<int *>(smem + C::MISC_OFF + 16);             // [2] deposits per buffer
+    volatile int *ready = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 32); // [2] next segment a buffer takes
+    // Items issued by the producer so far. Consumers take items out of ring
+    // order (warp cw takes items cw, cw + W, ...), so before the parity wait
+    // on full[j % R] for item j a consumer checks that item j was issued: the
+    // producer issues it only after item j - R was consumed, so the barrier's
+    // previous phase is complete and the parity test cannot pass on it.
+    volatile int *issued = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 48);
+    volatile int *lastflag = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 52);
+    volatile int *first_last = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 56);
+    float *red = reinterpret_cast<float *>(smem + C::RED_OFF);
+    float *hand = reinterpret_cast<float *>(smem + C::HAND_OFF);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, c = blockIdx.x;
+    const TqSplit split(p.items, G);
+    const long long i0 = split.start(c), i1 = split.start(c + 1);
+    const int nitems = (int)(i1 - i0);
+    // Tile segments of the slice: segment s holds slice items [sb(s), sb(s + 1)).
+    const int tile0 = (int)(i0 / p.units);
+    auto seg_begin = [&](int s) { // slice-relative first item of segment s
+        return s == 0 ? 0 : (int)((long long)(tile0 + s) * p.units - i0);
+    };
+    const int nseg = (int)((i1 - 1) / p.units) - tile0 + 1;
+    const long long ft0 = (long long)tile0 * p.units;
+    const bool first_shared = split.owner(ft0) != split.owner(ft0 + p.units - 1);
+    const bool handoff = first_shared && nseg > 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < R; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 2); // both halves consumed
+        }
+        mbar_init(hand_full, 1);
+        *abort = 0;
+        cnt[0] = cnt[1] = 0;
+        ready[0] = 0;
+        ready[1] = 1;
+        *issued = 0;
+        *first_last = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        // ---------------- producer: the weights depend on nothing ----------------
+        if (lane == 0) {
+            // The next kernel on the stream may be scheduled now: its CTAs fit
+            // beside this one and only stream their weights until this kernel
+            // completes (griddepcontrol.wait).
+            pdl_trigger();
+            for (int j = 0; j < nitems; j++) {
+                const int s = j % R;
+                if (j >= R && !wait_bar(&empty[s], ((j / R) & 1) ^ 1, abort, p.status)) continue;
+                const long long it = i0 + j;
+                uint8_t *dst = smem + C::RING_OFF + s * C::SLOT;
+                mbar_arrive_expect_tx(&full[s], C::SLOT);
+                bulk_load(dst, p.codes + it * kItem, kItem, &full[s]);
+                if (BITS == 4) bulk_load(dst + kItem, p.scale + it * (2 * kCols), 1024, &full[s]);
+                *issued = j + 1;
+            }
+        }
+    } else if (warp <= W) {
+        // ---------------- consumers ----------------
+        const int cw = warp - 1;
+        const uint32_t mg = p.magic;
+        pdl_wait(); // x, the output and the scratch belong to the previous kernel until here
+        // Warp cw takes half h = cw % 2 (rows 32h..32h+31) of items js, js + WI,
+        // ... with js = cw / 2: the work units k = 2j + h with k = cw (mod W).
+        const int hf = cw & 1, js = cw >> 1;
+        // Activations of this warp's half items: ring slot t % XD holds item t's
+        // rows 32h..32h+31 for every m ([m][32] floats), copied by cp.async
+        // XD - 1 items ahead; lane l copies row 32h + l and reads all rows
+        // after cp.async.wait_group and __syncwarp.
+        float *xs = reinterpret_cast<float *>(smem + C::X_OFF + cw * C::XSLOT);
+        int unit_x = (int)((i0 + js) % p.units); // unit (64-row group) of the next item to copy activations for
+        int tx = 0;                            // items of this warp whose activations were issued
+        const int nmine = js < nitems ? (nitems - 1 - js) / WI + 1 : 0;
+        const float *xrow = p.x + hf * kHalf + lane; // + unit * 64 + m * rows
+        auto issue_x = [&]() { // one cp.async group per call (empty past this warp's last item)
+            if (tx < nmine) {
+                float *dst = xs + (tx & (C::XD - 1)) * M * kHalf + lane;
+                const int row = unit_x * kRows + hf * kHalf + lane;
+                const bool v = row < p.rows;
+                const float *src = xrow + (v ? unit_x * kRows : -(hf * kHalf + lane));
+#pragma unroll
+                for (int m = 0; m < M; m++) cp_async_f32(dst + m * kHalf, src + (size_t)m * p.rows, v);
+                unit_x += WI; // next item of this warp: WI units on, modulo the units of a tile
+                while (unit_x >= p.units) unit_x -= p.units;
+            }
+            cp_async_commit();
+            tx++;
+        };
+        static_assert((C::XD & (C::XD - 1)) == 0, "XD must be a power of two");
+        for (int i = 0; i < C::XD - 1; i++) issue_x();
+        // byte offset of this lane's code word (bytes 4l..4l+3) in row k of an
+        // 8-row group: chunk l/4 of row r sits at chunk (l/4) ^ (r % 8)
+        uint32_t ofs[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) ofs[k] = k * kCols + 4 * (lane ^ (k << 2));
+
+        float acc[M][NP];
+#pragma unroll
+        for (int m = 0; m < M; m++)
+#pragma unroll
+            for (int j = 0; j < NP; j++) acc[m][j] = 0.f;
+
+        // Deposits this warp's sums of segment s; the last warp to deposit
+        // reduces the segment and hands it on.
+        auto deposit = [&](int s) {
+            const int sb = 2 * seg_begin(s), se = 2 * (s + 1 < nseg ? seg_begin(s + 1) : nitems); // work units
+            const int len = se - sb;
+            const int parts = len < W ? len : W; // warps with work in the segment
+            // warps with work: cw = (sb + i) % W, i < len
+            const bool mine = len >= W || ((cw - sb % W + W) % W) < len;
+            if (!mine) return;
+            const int b = s & 1;
+            // buffer b is free once segment s - 2 was reduced
+            if (ready[b] < s) {
+                const unsigned long long t0 = global_ns();
+                while (ready[b] < s) {
+                    if (*abort) break;
+                    if (global_ns() - t0 > kWaitNs) {
+                        atomicOr(p.status, TQ_STATUS_TIMEOUT);
+                        *abort = 1;
+                        break;
+                    }
+                }
+            }
+            float *rb = red + (size_t)(b * W + cw) * E + lane;
+#pragma unroll
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int j = 0; j < NP; j++) rb[(m * NP + j) * 32] = acc[m][j];
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) {
+                __threadfence_block(); // this warp's deposit before its count
+                last = atomicAdd(&cnt[b], 1) == parts - 1;
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) return;
+            __threadfence_block(); // every other warp's deposit before the reads below
+            // reduce the deposits in warp order
+            float v[M][NP];
+#pragma unroll
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int j = 0; j < NP; j++) v[m][j] = 0.f;
+            for (int i = 0; i < parts; i++) { // warps in a fixed order
+                const int w = len >= W ? i : (sb + i) % W;
+                const float *src = red + (size_t)(b * W + w) * E + lane;
+#pragma unroll
+                for (int m = 0; m < M; m++)
+#pragma unroll
+                    for (int j = 0; j < NP; j++) v[m][j] += src[(m * NP + j) * 32];
+            }
+            __syncwarp();
+            if (lane == 0) {
+                cnt[b] = 0;
+                __threadfence_block();
+                ready[b] = s + 2;
+            }
+            const int tile = tile0 + s;
+            const long long t0 = (long long)tile * p.units;
+            if (split.owner(t0) == split.owner(t0 + p.units - 1)) {
+                write_out<BITS, M>(p, tile, lane, v);
+            } else if (s == 0 && handoff) {
+                float *hb = hand + lane;
+#pragma unroll
+                for (int m = 0; m < M; m++)
+#pragma unroll
+                    for (int j = 0; j < NP; j++) hb[(m * NP + j) * 32] = v[m][j];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(hand_full);
+            } else {
+                publish_shared<BITS, M>(p, split, c, tile, lane, v);
+            }
+        };
+
+        int s = 0;                                   // segment of the next item
+        int next_sb = nseg > 1 ? seg_begin(1) : nitems; // first item of segment s + 1
+        const uint8_t *ring = smem + C::RING_OFF;
+        static_assert(R >= WI, "ring shorter than the item streams");
+        int slot = js % R, ph = (js / R) & 1; // ring slot and full-barrier parity of item j
+        for (int j = js, t_it = 0; j < nitems; j += WI, t_it++) {
+            while (j >= next_sb) {
+                deposit(s);
+#pragma unroll
+                for (int m = 0; m < M; m++)
+#pragma unroll
+                    for (int q = 0; q < NP; q++) acc[m][q] = 0.f;
+                s++;
+                next_sb = s + 1 < nseg ? next_sb + p.units : nitems;
+            }
+            issue_x(); // activations of this warp's item t_it + XD - 1
+            cp_async_wait<C::XD - 1>(); // this item's have landed (this lane's copies)
+            if (*issued <= j) { // bounded: the producer is normally far ahead
+                const unsigned long long t0 = global_ns();
+                while (*issued <= j && !*abort) {
+                    if (global_ns() - t0 > kWaitNs) {
+                        atomicOr(p.status, TQ_STATUS_TIMEOUT);
+                        *abort = 1;
+                    }
+                }
+            }
+            const bool ok = wait_bar(&full[slot], ph, abort, p.status);
+            __syncwarp(); // every lane's activation copies visible to the whole warp
+            const uint8_t *item = ring + slot * C::SLOT;
+            const float *xr = xs + (t_it & (C::XD - 1)) * M * kHalf;
+            if (ok) {
+                float2 t[M][NP];
+#pragma unroll
+                for (int m = 0; m < M; m++)
+#pragma unroll
+                    for (int q = 0; q < NP; q++) t[m][q] = f2(0.f, 0.f);
+                // all 32 rows of the half: rows past the matrix have zero codes and zero activations
+                const uint8_t *half = item + hf * kHalf * kCols;
+#pragma unroll
+                for (int g = 0; g < kHalf / 8; g++) {
+#pragma unroll
+                    for (int k = 0; k < 8; k += 4) {
+                        const int r = 8 * g + k; // row within the half
+                        uint32_t w[4];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) w[i] = *reinterpret_cast<const uint32_t *>(half + g * 8 * kCols + ofs[k + i]);
+                        float2 xa[M], xb[M];
+#pragma unroll
+                        for (int m = 0; m < M; m++) {
+                            const float4 v = *reinterpret_cast<const float4 *>(xr + m * kHalf + r);
+                            xa[m] = f2(v.x, v.y);
+                            xb[m] = f2(v.z, v.w);
+                        }
+                        row_pair<BITS, M>(w[0], w[1], xa, t, mg);
+                        row_pair<BITS, M>(w[2], w[3], xb, t, mg);
+                    }
+                }
+#pragma unroll
+                for (int m = 0; m < M; m++) {
+                    float tmp[NP];
+#pragma unroll
+                    for (int q = 0; q < NP; q++) tmp[q] = t[m][q].x + t[m][q].y;
+                    if (BITS == 4) {
+                        // group fold with 16^-k taken into the scale (exact)
+                        const float4 slo = *reinterpret_cast<const float4 *>(item + kItem + 16 * lane);
+                        const float4 shi = *reinterpret_cast<const float4 *>(item + kItem + 512 + 16 * lane);
+                        const float sc[8] = {slo.x, slo.y, slo.z, slo.w, shi.x, shi.y, shi.z, shi.w};
+#pragma unroll
+                        for (int q = 0; q < NP; q++) acc[m][q] = fmaf(tmp[q], sc[q] * pos_scale(q), acc[m][q]);
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < NP; q++) acc[m][q] += tmp[q];
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            __syncwarp(); // the x slot is reused XD - 1 items later
+            slot += WI;
+            if (slot >= R) {
+                slot -= R;
+                ph ^= 1;
+            }
+        }
+        // segments before the last one that this warp has not deposited yet
+        for (; s < nseg - 1; s++) {
+            deposit(s);
+#pragma unroll
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int q = 0; q < NP; q++) acc[m][q] = 0.f;
+        }
+        // The last CTA to arrive at a shared tile adds every contributor's sums
+        // in CTA order, one entry per thread, all contributor loads in flight.
+        auto reduce_all = [&](int tile) {
+            const long long t0 = (long long)tile * p.units;
+            const int cf = split.owner(t0), cl = split.owner(t0 + p.units - 1);
+            const int slot_f = split.slot(cf, t0);
+            for (int e = threadIdx.x - 32; e < E; e += W * 32) {
+                constexpr int CH = 16; // contributor loads in flight per thread
+                float v = 0.f;
+                for (int cc = cf; cc <= cl; cc += CH) {
+                    float pv[CH];
+#pragma unroll
+                    for (int u = 0; u < CH; u++) {
+                        const int c2 = cc + u;
+                        pv[u] = c2 <= cl ? __ldcg(p.partial + (size_t)(c2 == cf ? slot_f : 2 * c2) * E + e) : 0.f;
+                    }
+#pragma unroll
+                    for (int u = 0; u < CH; u++) v += pv[u];
+                }
+                const int l = e & 31, q = (e >> 5) % NP, m = (e >> 5) / NP;
+                const int col = out_col<BITS>(p, tile, l, q);
+                if (col >= 0) p.out[(size_t)m * p.cols + col] = BITS == 8 ? v * __ldg(p.scale + col) : v;
+            }
+        };
+        // The slice's last segment, by all consumer warps: every warp's sums
+        // (zero if it had no item there) are added in warp order, one entry per
+        // thread, and a shared tile is published and, by the last CTA to
+        // arrive, reduced with every contributor's load in flight at once.
+        {
+            const int sl = nseg - 1, b = sl & 1;
+            if (ready[b] < sl) { // buffer b is free once segment sl - 2 was reduced
+                const unsigned long long t0 = global_ns();
+                while (ready[b] < sl && !*abort) {
+                    if (global_ns() - t0 > kWaitNs) {
+                        atomicOr(p.status, TQ_STATUS_TIMEOUT);
+                        *abort = 1;
+                    }
+                }
+            }
+            float *rb = red + (size_t)(b * W + cw) * E + lane;
+#pragma unroll
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int q = 0; q < NP; q++) rb[(m * NP + q) * 32] = acc[m][q];
+            named_sync(1, W * 32);
+            const int tile = tile0 + sl;
+            const long long t0 = (long long)tile * p.units;
+            const int cf = split.owner(t0), cl = split.owner(t0 + p.units - 1);
+            const int ct = threadIdx.x - 32; // 0 .. W*32-1
+            float *part = p.partial + (size_t)split.slot(c, t0) * E;
+            for (int e = ct; e < E; e += W * 32) { // entry e = (m*NP + q)*32 + l
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < W; w++) v += red[(size_t)(b * W + w) * E + e];
+                if (cf == cl) {
+                    const int l = e & 31, q = (e >> 5) % NP, m = (e >> 5) / NP;
+                    const int col = out_col<BITS>(p, tile, l, q);
+                    if (col >= 0) p.out[(size_t)m * p.cols + col] = BITS == 8 ? v * __ldg(p.scale + col) : v;
+                } else {
+                    part[e] = v;
+                }
+            }
+            if (cf != cl) {
+                // The barrier orders every thread's partial stores before thread
+                // 0's acq_rel arrival, whose release is cumulative over them; for
+                // the last CTA its acquire, followed by the second barrier,
+                // orders the other CTAs' partials before every thread's loads.
+                named_sync(1, W * 32);
+                if (ct == 0) *lastflag = tq_arrive_last(&p.counters[tile], (unsigned)(cl - cf + 1)) ? 1 : 0;
+                named_sync(1, W * 32);
+                if (*lastflag) reduce_all(tile);
+            }
+        }
+        if (handoff) { // the first segment, published by the fixup warp
+            named_sync(2, W * 32 + 32);
+            if (*first_last) reduce_all(tile0);
+        }
+    } else {
+        // ---------------- fixup: the first segment, when shared and not last ----------------
+        if (handoff) {
+            pdl_wait();
+            wait_bar(hand_full, 0, abort, p.status);
+            float v[M][NP];
+#pragma unroll
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int j = 0; j < NP; j++) v[m][j] = hand[(m * NP + j) * 32 + lane];
+            // publish this CTA's sums; if it is the last to arrive, the
+            // consumer warps add the contributors (all loads in flight)
+            const int cf = split.owner(ft0), cl = split.owner(ft0 + p.units - 1);
+            float *dst = p.partial + (size_t)split.slot(c, ft0) * E + lane;
+#pragma unroll
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int j = 0; j < NP; j++) dst[(m * NP + j) * 32] = v[m][j];
+            __syncwarp(); // the lanes' stores before lane 0's cumulative acq_rel arrival
+            if (lane == 0) *first_last = tq_arrive_last(&p.counters[tile0], (unsigned)(cl - cf + 1)) ? 1 : 0;
+            __syncwarp();
+            named_arrive(2, W * 32 + 32);
+        }
+    }
+    __syncthreads();
+}
+
+template <int BITS, int M>
+cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st) {
+    using C = CCfg<BITS, M>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static int configured[64] = {};
+    static int sm_count[64] = {};
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(cmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        configured[dev] = 1;
+    }
+    CmvParams prm;
+    prm.codes = mat.codes;
+    prm.scale = mat.scale;
+    prm.x = x;
+    prm.out = out;
+    prm.partial = scr.partial;
+    prm.counters = scr.counters;
+    prm.status = scr.status;
+    prm.rows = mat.rows;
+    prm.cols = mat.cols;
+    prm.half = mat.cols / 2;
+    prm.units = mat.units;
+    prm.tiles = mat.tiles;
+    prm.items = (long long)mat.tiles * mat.units;
+    prm.magic = 0x4B000000u;
+    const int sms = sm_count[dev];
+    if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS) return cudaErrorInvalidValue;
+    if ((size_t)2 * sms * C::E > TQ_SCRATCH_PARTIAL_FLOATS) return cudaErrorInvalidValue;
+    const int ctas = (int)(prm.items < sms ? prm.items : sms);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    return cudaLaunchKernelEx(&cfg, cmv_kernel<BITS, M>, prm);
+}
+
+} // namespace
+
+// CUDA-core matvec for M <= 2 rows per launch (more rows: consecutive 2-row launches).
+cudaError_t tq_launch_cmv(const TqMatrixDev &mat, const float *x, float *out, int M, const TqScratch &scr,
+                          cudaStream_t st) {
+    if (M <= 0 || mat.cols == 0) return cudaSuccess;
+    if (mat.rows == 0) return cudaMemsetAsync(out, 0, sizeof(float) * (size_t)M * mat.cols, st);
+    for (int m0 = 0; m0 < M; m0 += 2) {
+        const int mm = M - m0 < 2 ? M - m0 : 2;
+        const float *xm = x + (size_t)m0 * mat.rows;
+        float *om = out + (size_t)m0 * mat.cols;
+        cudaError_t e;
+        if (mat.bits == 8)
+            e = mm == 1 ? launch_cmv<8, 1>(mat, xm, om, scr, st) : launch_cmv<8, 2>(mat, xm, om, scr, st);
+        else
+            e = mm == 1 ? launch_cmv<4, 1>(mat, xm, om, scr, st) : launch_cmv<4, 2>(mat, xm, om, scr, st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}

@@ -140,6 +140,12 @@ cudaError_t tq_launch_matvec(const TqMatrixDev &m, const float *x, float *out, i
                              cudaStream_t st);
 cudaError_t tq_launch_igemv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                             cudaStream_t st);
+// Single-launch tensor-core matvec for M <= 8 rows per launch (tq_gemv.cu).
+cudaError_t tq_launch_gemv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
+                           cudaStream_t st);
+// CUDA-core matvec for M <= 2 rows per launch (tq_cmv.cu).
+cudaError_t tq_launch_cmv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
+                          cudaStream_t st);
 // Matmul for M >= 16 rows on tcgen05 kind::tf32 (needs scr.mm_partial).
 cudaError_t tq_launch_mm(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                          cudaStream_t st);

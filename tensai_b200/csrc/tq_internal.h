@@ -25,6 +25,9 @@ std::shared_ptr<Handle> tq_lookup_checked(uint64_t h, int *rc);
 // The matvec scratch of (device, stream), created on first use (with the
 // M >= 16 matmul partials when m >= TQ_MM_MIN_ROWS). Not inside a capture.
 int tq_scratch_for(int device, cudaStream_t st, TqScratch *out, int m);
+// Frees and forgets the scratch of (device, stream); before destroying a stream
+// whose scratch tq_scratch_for created, after its work has finished.
+void tq_scratch_release(int device, cudaStream_t st);
 // out[M][cols] = x @ W with the kernel the library would pick for M rows.
 cudaError_t tq_launch_matmul(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                              cudaStream_t st);

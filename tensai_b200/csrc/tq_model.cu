@@ -215,6 +215,7 @@ void destroy(Gpt2 &m) {
     tq_release_matrix(&m.wteT.q);
     for (void *p : m.allocs) cudaFree(p);
     m.allocs.clear();
+    if (m.st) tq_scratch_release(m.device, m.st);
     if (m.st) cudaStreamDestroy(m.st);
     m.st = nullptr;
 }

@@ -36,6 +36,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// As mbar_try_wait, but the thread may stay suspended in hardware for up to
+// `hint_ns` while the phase is incomplete instead of polling (a polling warp
+// takes issue slots from the warps that work).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -44,12 +58,11 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // Bounded wait for phase `parity`. On timeout (or if the CTA already
 // aborted) sets the CTA's abort flag, records TQ_STATUS_TIMEOUT and returns
 // false; every later wait of the CTA then returns false at once.
-__device__ __noinline__ bool wait_slow(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *status) {
+static __device__ __noinline__ bool wait_slow(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *status) {
     if (*abort) return false;
     const unsigned long long t0 = global_ns();
     for (;;) {
-        for (int i = 0; i < 64; i++)
-            if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_hint(bar, parity, 200000u)) return true; // up to 0.2 ms asleep per try
         if (*abort) return false;
         if (global_ns() - t0 > kWaitNs) {
             atomicOr(status, TQ_STATUS_TIMEOUT);

@@ -231,6 +231,7 @@ void destroy(Qwen &m) {
     tq_release_matrix(&m.lm);
     for (void *p : m.allocs) cudaFree(p);
     m.allocs.clear();
+    if (m.st) tq_scratch_release(m.device, m.st);
     if (m.st) cudaStreamDestroy(m.st);
     m.st = nullptr;
 }

@@ -38,8 +38,11 @@ def device():
     _lib.check(_lib.load().tq_set_device(0))
 
 
-# 0: tensor-core integer-MMA matvec (default), 1: CUDA-core fp32 matvec.
-@pytest.fixture(params=[0, 1], ids=["tcgen05", "cudacore"])
+# 0: the default choice per row count, 1: CUDA-core matvec with per-warp
+# copies, 2: single-launch tensor-core matvec (digit planes made in the
+# kernel), 3: single-launch CUDA-core matvec (2 rows per launch), 4: tensor-core
+# matvec with a digit-plane launch.
+@pytest.fixture(params=[0, 1, 2, 3, 4], ids=["default", "cudacore", "tcgen05-1launch", "cudacore-1launch", "tcgen05"])
 def kernel(request):
     L = _lib.load()
     _lib.check(L.tq_set_matvec_kernel(request.param))
