@@ -13,9 +13,10 @@ Each step is one CUDA-graph replay of the 64 launches.
            host buffers: every call copies x host->device and out device->host
   roofline the matvec's achieved GB/s: algorithmic bytes of one call over the
            mean device time of a call inside the timed graph (CUDA events on
-           the launching stream around K replays of 64 calls; one call = the
-           digit-plane kernel plus the tcgen05 matvec kernel it chains to),
-           against the measured HBM copy bandwidth
+           the launching stream around K replays of 64 calls; one call = one
+           launch of the CUDA-core matvec kernel, whose next call on the stream
+           streams its weights while this one finishes), against the measured
+           HBM copy bandwidth
   cpu_baseline  the CPU oracle (AVX2 restatement of quant4_simd.go with the
            reference's worker split) on the host cores, bounded sample
 
@@ -44,7 +45,7 @@ METRIC = "int8/int4 dequant-matvec HBM GB/s (% of peak); decode tokens/s at 1/2/
 K_UP, N_UP = 4096, 11008
 LAYERS = 32
 FALLBACK_HBM_GBS = 6650.0
-LAUNCHES_PER_CALL = 2  # planes_kernel + igemv_kernel per int4 M=1 matvec
+LAUNCHES_PER_CALL = 1  # cmv_kernel: one launch per int4 M=1 matvec
 WORKLOAD = ("int4 g64 MLP pair (up 4096x11008 + down 11008x4096), M=1, fp32 accumulate; "
             "32 resident layer copies streamed per step")
 
@@ -73,7 +74,7 @@ def load_traffic():
     """Per-launch DRAM bytes (read + write) of the matvec kernel from the
     committed ncu summary (its `traffic_bytes_per_launch:` line), or None."""
     import re
-    path = os.path.join(ROOT, "profiles", "igemv_int4_m1_mlp_pair.md")
+    path = os.path.join(ROOT, "profiles", "cmv_int4_m1_mlp_pair.md")
     try:
         with open(path) as f:
             m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", f.read())
@@ -477,8 +478,8 @@ def run_gpu(args, rank: int, world: int):
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "frac_of_8tbs": round(achieved / 8000.0, 4),
                          "traffic": traffic,
-                         "kernel": "igemv_kernel<4,1> (int4 dequant-matvec on tcgen05 kind::i8, M=1) "
-                                   "with its planes_kernel<1>",
+                         "kernel": "cmv_kernel<4,1> (int4 dequant-matvec on the CUDA cores, M=1, "
+                                   "one launch per call)",
                          "call_us_mean": round(kavg * 1e3, 3),
                          "algorithmic_bytes_per_launch": per_launch},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
