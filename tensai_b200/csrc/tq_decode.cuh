@@ -18,6 +18,54 @@ namespace TQD_NS {
 
 constexpr int kThreads = 256;
 
+// ---- programmatic dependent launch -------------------------------------------
+// With TQ_DECODE_PDL set by the including engine, every kernel of a decode step
+// is launched with programmatic stream serialization and starts with
+// step_entry: it lets the next kernel on the stream be scheduled at once, then
+// waits until its predecessor has completed and its memory is visible
+// (griddepcontrol.wait) before touching anything. A step's matvec is then
+// resident and streams its weights while the small kernels before it run. A
+// dependent grid is scheduled only after every CTA of its predecessor has
+// started, so waiting CTAs never block an unscheduled predecessor. Without
+// TQ_DECODE_PDL, launches are plain and step_entry is empty.
+#ifndef TQ_DECODE_PDL
+#error "define TQ_DECODE_PDL (0 or 1) before including tq_decode.cuh"
+#endif
+__device__ __forceinline__ void step_entry() {
+#if TQ_DECODE_PDL
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+// For grids of hundreds of CTAs (the attention passes): wait only, so the
+// successor is scheduled when this grid completes rather than early, and its
+// CTAs do not sit resident beside this grid's.
+__device__ __forceinline__ void step_entry_wait() {
+#if TQ_DECODE_PDL
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t step_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               Args... args) {
+#if TQ_DECODE_PDL
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+#else
+    kernel<<<grid, block, smem, st>>>(static_cast<KArgs>(args)...);
+    return cudaGetLastError();
+#endif
+}
+
 // ---- reductions ---------------------------------------------------------------
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -49,16 +97,19 @@ __device__ inline double block_reduce_d(double v, double *sh, int kind) {
 // ---- elementwise ------------------------------------------------------------------
 // x += y + b (bias into the matvec output, then the residual add; b may be null).
 __global__ void residual_kernel(float *x, const float *y, const float *b, int n, size_t total) {
+    step_entry();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
         x[i] = __fadd_rn(x[i], b ? __fadd_rn(y[i], b[i % n]) : y[i]);
 }
 
 __global__ void fill_kernel(float *p, float v, size_t n) {
+    step_entry();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
 }
 
 // state = {token to feed, its position, tokens generated}
 __global__ void set_state_kernel(int *state, int token, int pos, int generated) {
+    step_entry();
     state[0] = token;
     state[1] = pos;
     state[2] = generated;
@@ -74,6 +125,7 @@ __global__ void set_state_kernel(int *state, int token, int pos, int generated) 
 __global__ void attention_kernel(const float *q, int qstride, const float *kc, const float *vc, int kvstride,
                                  float *out, int outstride, const int *state, int hd, int group, double scale,
                                  int prefill, int ctx) {
+    step_entry();
     extern __shared__ double sc[];
     __shared__ double sh[32];
     const int h = blockIdx.x, r = blockIdx.y, kvh = h / group;
@@ -125,6 +177,7 @@ constexpr int kAttChunk = 128;
 __global__ void __launch_bounds__(128) att_scores_kernel(const float *q, const float *kc, int kvstride, const int *state,
                                                          int hd, int group, double scale, double *scores,
                                                          double *stats, int ctx, int nchunks) {
+    step_entry_wait();
     __shared__ double ss[kAttChunk];
     __shared__ double sh[32];
     const int h = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttChunk;
@@ -158,6 +211,7 @@ __global__ void __launch_bounds__(128) att_scores_kernel(const float *q, const f
 __global__ void __launch_bounds__(128) att_weighted_kernel(const float *vc, int kvstride, const int *state, int hd,
                                                            int group, const double *scores, const double *stats,
                                                            float *partial, int ctx, int nchunks) {
+    step_entry_wait();
     __shared__ float ps[kAttChunk];
     const int h = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttChunk, kvh = h / group;
     if (t0 > pos) return;
@@ -180,6 +234,7 @@ __global__ void __launch_bounds__(128) att_weighted_kernel(const float *vc, int 
 }
 
 __global__ void att_combine_kernel(const float *partial, const int *state, int hd, float *out, int nchunks) {
+    step_entry();
     const int h = blockIdx.x, nb = state[1] / kAttChunk + 1;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         float acc = 0.f;
@@ -215,12 +270,13 @@ inline AttScratch att_scratch(void *buf, int heads, int ctx, int hd) {
 inline cudaError_t decode_attention(const float *q, const float *kc, const float *vc, int kvstride, float *out,
                                     const int *state, int heads, int hd, int group, double scale, const AttScratch &a,
                                     cudaStream_t st) {
-    att_scores_kernel<<<dim3(heads, a.nchunks), 128, 0, st>>>(q, kc, kvstride, state, hd, group, scale, a.scores,
-                                                              a.stats, a.ctx, a.nchunks);
-    att_weighted_kernel<<<dim3(heads, a.nchunks), 128, 0, st>>>(vc, kvstride, state, hd, group, a.scores, a.stats,
-                                                                a.partial, a.ctx, a.nchunks);
-    att_combine_kernel<<<heads, 128, 0, st>>>(a.partial, state, hd, out, a.nchunks);
-    return cudaGetLastError();
+    cudaError_t e = step_launch(att_scores_kernel, dim3(heads, a.nchunks), dim3(128), 0, st, q, kc, kvstride, state, hd, group,
+                        scale, a.scores, a.stats, a.ctx, a.nchunks);
+    if (e == cudaSuccess)
+        e = step_launch(att_weighted_kernel, dim3(heads, a.nchunks), dim3(128), 0, st, vc, kvstride, state, hd, group, a.scores,
+                a.stats, a.partial, a.ctx, a.nchunks);
+    if (e == cudaSuccess) e = step_launch(att_combine_kernel, dim3(heads), dim3(128), 0, st, a.partial, state, hd, out, a.nchunks);
+    return e;
 }
 
 // ---- greedy pick ------------------------------------------------------------------------
@@ -230,6 +286,7 @@ inline cudaError_t decode_attention(const float *q, const float *kc, const float
 // (position = set_pos if >= 0, else + 1).
 __global__ void argmax_kernel(const float *logits, int n, int offset, int *cand, int *state, int *tokens,
                               int set_pos, int final) {
+    step_entry();
     __shared__ float bv[32];
     __shared__ int bi[32];
     float best = -INFINITY;
@@ -270,6 +327,7 @@ __global__ void argmax_kernel(const float *logits, int n, int offset, int *cand,
 constexpr int kArgBlocks = 128;
 
 __global__ void argmax_part_kernel(const float *logits, int n, int *part) {
+    step_entry();
     __shared__ float bv[32];
     __shared__ int bi[32];
     const int per = (n + gridDim.x - 1) / gridDim.x;
@@ -299,6 +357,7 @@ __global__ void argmax_part_kernel(const float *logits, int n, int *part) {
 
 __global__ void argmax_final_kernel(const int *part, int nparts, int offset, int *cand, int *state, int *tokens,
                                     int set_pos, int final) {
+    step_entry();
     if (threadIdx.x != 0) return;
     float best = -INFINITY;
     int idx = 0x7fffffff;
@@ -323,15 +382,18 @@ __global__ void argmax_final_kernel(const int *part, int nparts, int offset, int
 // kArgBlocks ints of scratch.
 inline cudaError_t greedy_pick(const float *logits, int n, int offset, int *part, int *cand, int *state, int *tokens,
                                int set_pos, int final, cudaStream_t st) {
-    argmax_part_kernel<<<kArgBlocks, 256, 0, st>>>(logits, n, part);
-    argmax_final_kernel<<<1, 32, 0, st>>>(part, kArgBlocks, offset, cand, state, tokens, set_pos, final);
-    return cudaGetLastError();
+    cudaError_t e = step_launch(argmax_part_kernel, dim3(kArgBlocks), dim3(256), 0, st, logits, n, part);
+    if (e == cudaSuccess)
+        e = step_launch(argmax_final_kernel, dim3(1), dim3(32), 0, st, part, kArgBlocks, offset, cand, state, tokens, set_pos,
+                final);
+    return e;
 }
 
 // The best of w candidates (value, global index) from the shards of a
 // column-split head: larger value, ties to the lower index. Advances the
 // state like argmax_kernel's final form.
 __global__ void pick_kernel(const int *cands, int w, int *state, int *tokens, int set_pos) {
+    step_entry();
     if (threadIdx.x != 0) return;
     float best = __int_as_float(cands[0]);
     int idx = cands[1];

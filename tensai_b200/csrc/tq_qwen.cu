@@ -36,6 +36,10 @@
 
 #include "../../include/tensai_cuda.h"
 #define TQD_NS tqd_qwen
+// Plain launches for the Qwen2 step: letting each step's matvec become resident
+// early beside the small kernels (TQ_DECODE_PDL 1) measured 10% fewer tokens/s
+// at the 7B shape on B200 (277 vs 310), though it helps GPT-2.
+#define TQ_DECODE_PDL 0
 #include "tq_decode.cuh"
 #include "tq_internal.h"
 
@@ -79,6 +83,7 @@ int load_nccl() {
 // ---- kernels ------------------------------------------------------------------
 // x = embed[token] (model.go:239-240).
 __global__ void embed_row_kernel(const float *embed, const int *state, float *x, int d) {
+    step_entry();
     const float *row = embed + (size_t)state[0] * d;
     for (int i = threadIdx.x; i < d; i += blockDim.x) x[i] = row[i];
 }
@@ -87,6 +92,7 @@ __global__ void embed_row_kernel(const float *embed, const int *state, float *x,
 // inv) * w. With y: first the residual add x += y (model.go:276-278 /
 // 301-303), then the norm of the new x, in one launch.
 __global__ void rmsnorm_kernel(float *x, const float *y, const float *w, float *out, int n, double eps) {
+    step_entry();
     __shared__ double sh[32];
     double ss = 0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -104,6 +110,7 @@ __global__ void rmsnorm_kernel(float *x, const float *y, const float *w, float *
 // cache at the state's position.
 __global__ void qkv_rope_kernel(float *qkv, const float *bias, float *kc, float *vc, const int *state, int nq, int nkv,
                                 int hd, double theta) {
+    step_entry();
     const int pos = state[1], half = hd / 2, qd = nq * hd, kvd = nkv * hd;
     const int pairs = (nq + nkv) * half;
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < pairs + kvd; e += gridDim.x * blockDim.x) {
@@ -134,6 +141,7 @@ __global__ void qkv_rope_kernel(float *qkv, const float *bias, float *kc, float 
 
 // h = float32(silu(gate)) * up over the fused [gate | up] row (model.go:296-299).
 __global__ void silu_mul_kernel(const float *gu, float *h, int n) {
+    step_entry();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const double g = (double)gu[i];
         h[i] = __fmul_rn((float)__ddiv_rn(g, __dadd_rn(1.0, exp(-g))), gu[n + i]);
@@ -144,6 +152,7 @@ __global__ void silu_mul_kernel(const float *gu, float *h, int n) {
 // (main.go:229-231), else the best candidate of the w shards (value, id;
 // ties to the lower id), recorded as generated. Position + 1.
 __global__ void advance_kernel(const int *cands, int w, int *state, int *tokens, const int *prompt, int n_prompt) {
+    step_entry();
     if (threadIdx.x != 0) return;
     const int pos = state[1];
     if (pos + 1 < n_prompt) {
@@ -166,6 +175,7 @@ __global__ void advance_kernel(const int *cands, int w, int *state, int *tokens,
 // out[r][out_col0 + j] = in[r][in_col0 + j] for j < ncols.
 __global__ void copy_cols_kernel(const float *in, int in_cols, int in_col0, float *out, int out_cols, int out_col0,
                                  int rows, int ncols) {
+    step_entry();
     const size_t total = (size_t)rows * ncols;
     for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
         const int r = (int)(e / ncols), j = (int)(e % ncols);
@@ -338,33 +348,33 @@ cudaError_t nccl_err(ncclResult_t r) { return r == ncclSuccess ? cudaSuccess : c
 // One step (model.go:232-307) for the state's token at the state's position.
 cudaError_t step(Qwen &m, int n_prompt) {
     const int d = m.c.d;
-    embed_row_kernel<<<1, kThreads, 0, m.st>>>(m.embed, m.state, m.x, d);
+    TRY(step_launch(embed_row_kernel, dim3(1), dim3(kThreads), 0, m.st, m.embed, m.state, m.x, d));
     const float *pending = nullptr; // residual still to be added to x (the previous down_proj output)
     for (Layer &ly : m.L) {
-        rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.x, pending, m.ones, m.a, d, m.c.eps);
+        TRY(step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, pending, m.ones, m.a, d, m.c.eps));
         TRY(tq_launch_matmul(ly.qkv, m.a, m.qkv, 1, m.scr, m.st));
-        qkv_rope_kernel<<<grid_for((size_t)(m.nq + m.nkv) * m.hd / 2 + m.kvd), kThreads, 0, m.st>>>(
-            m.qkv, m.zeros, ly.kc, ly.vc, m.state, m.nq, m.nkv, m.hd, m.c.theta);
+        TRY(step_launch(qkv_rope_kernel, dim3(grid_for((size_t)(m.nq + m.nkv) * m.hd / 2 + m.kvd)), dim3(kThreads), 0, m.st,
+                m.qkv, m.zeros, ly.kc, ly.vc, m.state, m.nq, m.nkv, m.hd, m.c.theta));
         TRY(decode_attention(m.qkv, ly.kc, ly.vc, m.kvd, m.att, m.state, m.nq, m.hd, m.group,
                              1.0 / sqrt((double)m.hd), m.att_scr, m.st));
         TRY(tq_launch_matmul(ly.o, m.att + m.arow, m.y, 1, m.scr, m.st));
         if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
-        rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.x, m.y, m.ones, m.a, d, m.c.eps); // x += o_proj, then norm
+        TRY(step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, m.y, m.ones, m.a, d, m.c.eps)); // x += o_proj, then norm
         TRY(tq_launch_matmul(ly.gu, m.a, m.gu, 1, m.scr, m.st));
-        silu_mul_kernel<<<grid_for(m.fcols), kThreads, 0, m.st>>>(m.gu, m.h, m.fcols);
+        TRY(step_launch(silu_mul_kernel, dim3(grid_for(m.fcols)), dim3(kThreads), 0, m.st, m.gu, m.h, m.fcols));
         TRY(tq_launch_matmul(ly.down, m.h, m.y, 1, m.scr, m.st));
         if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
         pending = m.y;
         TRY(cudaGetLastError());
     }
-    rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.x, pending, m.ones, m.a, d, m.c.eps);
+    TRY(step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, pending, m.ones, m.a, d, m.c.eps));
     TRY(tq_launch_matmul(m.lm, m.a, m.logits, 1, m.scr, m.st));
     TRY(greedy_pick(m.logits, m.vcols, m.voff, m.part, m.cand, m.state, m.tokens, -1, 0, m.st));
     if (m.world > 1)
         TRY(nccl_err(g_nccl.allGather(m.cand, m.cands, 2, ncclInt32, m.comm, m.st)));
     else
         TRY(cudaMemcpyAsync(m.cands, m.cand, sizeof(int) * 2, cudaMemcpyDeviceToDevice, m.st));
-    advance_kernel<<<1, 32, 0, m.st>>>(m.cands, m.world, m.state, m.tokens, m.prompt, n_prompt);
+    TRY(step_launch(advance_kernel, dim3(1), dim3(32), 0, m.st, m.cands, m.world, m.state, m.tokens, m.prompt, n_prompt));
     return cudaGetLastError();
 }
 
