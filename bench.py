@@ -217,10 +217,12 @@ SIDE_CONFIGS = [
 ]
 
 
-def measure_side_configs(L, Q, torch, stream, peak):
+def measure_side_configs(L, Q, torch, stream, peak, only=None):
     out = {}
     sp = ctypes.c_void_p(stream.cuda_stream)
     for name, bits, rows, cols, m in SIDE_CONFIGS:
+        if only and not name.startswith(only + " "):
+            continue
         per = algo_bytes(bits, rows, cols, m)
         copies = max(2, int(160e6 // (rows * cols // (1 if bits == 8 else 2))) + 1)  # > L2 in total
         w = torch.empty(rows, cols, device="cuda")
@@ -454,11 +456,13 @@ def run_gpu(args, rank: int, world: int):
     e2e_value = bytes_step * world * e2e_steps / float(e2e_t.item()) / 1e9
 
     side = None
-    if rank == 0 and not args.no_side_configs:
+    if rank == 0 and args.side_config:
+        side = measure_side_configs(L, Q, torch, stream, load_peak()[0], args.side_config)
+    elif rank == 0 and not args.no_side_configs:
         side = measure_side_configs(L, Q, torch, stream, load_peak()[0])
         side["C4 GPT-2-small int8 greedy decode"] = measure_gpt2(world == 1 and not args.no_cpu_baseline)
     qwen = None
-    if not args.no_side_configs:
+    if not args.no_side_configs and not args.side_config:
         qwen = measure_qwen(rank, world, load_peak()[0])  # collective over all ranks
         if side is not None:
             side[f"C5 Qwen2.5-7B int4 greedy decode TP={world}"] = qwen
@@ -511,6 +515,8 @@ def main():
                     help="resident MLP pairs per step (default 32 = 1.63 GB; small values for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-side-configs", action="store_true")
+    ap.add_argument("--side-config", default=None,
+                    help="run only this kernel side config (C1, C2, C3) after the headline, e.g. for profiling")
     ap.add_argument("--kernel", type=int, default=None,
                     help="matvec kernel for M <= 15 (tq_set_matvec_kernel); default: the library's")
     args = ap.parse_args()

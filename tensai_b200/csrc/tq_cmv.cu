@@ -276,6 +276,12 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
     const long long ft0 = (long long)tile0 * p.units;
     const bool first_shared = split.owner(ft0) != split.owner(ft0 + p.units - 1);
     const bool handoff = first_shared && nseg > 1;
+    // The slice's last tile segment: its owners and this CTA's partial slot,
+    // worked out now rather than on the reduction's critical path at the end.
+    const int last_tile = tile0 + nseg - 1;
+    const long long lt0 = (long long)last_tile * p.units;
+    const int last_cf = split.owner(lt0), last_cl = split.owner(lt0 + p.units - 1);
+    const int last_slot = split.slot(c, lt0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < R; s++) {
@@ -566,11 +572,9 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
 #pragma unroll
                 for (int q = 0; q < NP; q++) rb[(m * NP + q) * 32] = acc[m][q];
             named_sync(1, W * 32);
-            const int tile = tile0 + sl;
-            const long long t0 = (long long)tile * p.units;
-            const int cf = split.owner(t0), cl = split.owner(t0 + p.units - 1);
+            const int tile = last_tile, cf = last_cf, cl = last_cl;
             const int ct = threadIdx.x - 32; // 0 .. W*32-1
-            float *part = p.partial + (size_t)split.slot(c, t0) * E;
+            float *part = p.partial + (size_t)last_slot * E;
             for (int e = ct; e < E; e += W * 32) { // entry e = (m*NP + q)*32 + l
                 float v = 0.f;
 #pragma unroll
