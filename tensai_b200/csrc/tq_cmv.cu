@@ -94,6 +94,7 @@ struct CmvParams {
     long long items;
     int rows, cols, half, units, tiles;
     uint32_t magic; // 0x4B000000 (2^23), passed in so it sits in a register: one LOP3 per nibble
+    int k;          // cluster split: CTAs per column tile (kcmv_kernel)
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -236,6 +237,57 @@ __device__ void publish_shared(const CmvParams &p, const TqSplit &split, int c, 
                 for (int j = 0; j < NP; j++) s[m][j] += pv[u][m][j];
     }
     write_out<BITS, M>(p, tile, lane, s);
+}
+
+// One warp's half item (rows 32h..32h+31 of a 64-row item in shared memory)
+// into the lane's column sums acc (int4: through the group fold).
+template <int BITS, int M>
+__device__ __forceinline__ void half_item(const uint8_t *item, int hf, const float *xr, const uint32_t (&ofs)[8],
+                                          uint32_t mg, int lane, float (&acc)[M][BITS == 8 ? 4 : 8]) {
+    constexpr int NP = BITS == 8 ? 4 : 8;
+    float2 t[M][NP];
+#pragma unroll
+    for (int m = 0; m < M; m++)
+#pragma unroll
+        for (int q = 0; q < NP; q++) t[m][q] = f2(0.f, 0.f);
+    // all 32 rows of the half: rows past the matrix have zero codes and zero activations
+    const uint8_t *half = item + hf * kHalf * kCols;
+#pragma unroll
+    for (int g = 0; g < kHalf / 8; g++) {
+#pragma unroll
+        for (int k = 0; k < 8; k += 4) {
+            const int r = 8 * g + k; // row within the half
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) w[i] = *reinterpret_cast<const uint32_t *>(half + g * 8 * kCols + ofs[k + i]);
+            float2 xa[M], xb[M];
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                const float4 v = *reinterpret_cast<const float4 *>(xr + m * kHalf + r);
+                xa[m] = f2(v.x, v.y);
+                xb[m] = f2(v.z, v.w);
+            }
+            row_pair<BITS, M>(w[0], w[1], xa, t, mg);
+            row_pair<BITS, M>(w[2], w[3], xb, t, mg);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        float tmp[NP];
+#pragma unroll
+        for (int q = 0; q < NP; q++) tmp[q] = t[m][q].x + t[m][q].y;
+        if (BITS == 4) {
+            // group fold with 16^-k taken into the scale (exact)
+            const float4 slo = *reinterpret_cast<const float4 *>(item + kItem + 16 * lane);
+            const float4 shi = *reinterpret_cast<const float4 *>(item + kItem + 512 + 16 * lane);
+            const float sc[8] = {slo.x, slo.y, slo.z, slo.w, shi.x, shi.y, shi.z, shi.w};
+#pragma unroll
+            for (int q = 0; q < NP; q++) acc[m][q] = fmaf(tmp[q], sc[q] * pos_scale(q), acc[m][q]);
+        } else {
+#pragma unroll
+            for (int q = 0; q < NP; q++) acc[m][q] += tmp[q];
+        }
+    }
 }
 
 template <int BITS, int M>
@@ -465,51 +517,7 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
             __syncwarp(); // every lane's activation copies visible to the whole warp
             const uint8_t *item = ring + slot * C::SLOT;
             const float *xr = xs + (t_it & (C::XD - 1)) * M * kHalf;
-            if (ok) {
-                float2 t[M][NP];
-#pragma unroll
-                for (int m = 0; m < M; m++)
-#pragma unroll
-                    for (int q = 0; q < NP; q++) t[m][q] = f2(0.f, 0.f);
-                // all 32 rows of the half: rows past the matrix have zero codes and zero activations
-                const uint8_t *half = item + hf * kHalf * kCols;
-#pragma unroll
-                for (int g = 0; g < kHalf / 8; g++) {
-#pragma unroll
-                    for (int k = 0; k < 8; k += 4) {
-                        const int r = 8 * g + k; // row within the half
-                        uint32_t w[4];
-#pragma unroll
-                        for (int i = 0; i < 4; i++) w[i] = *reinterpret_cast<const uint32_t *>(half + g * 8 * kCols + ofs[k + i]);
-                        float2 xa[M], xb[M];
-#pragma unroll
-                        for (int m = 0; m < M; m++) {
-                            const float4 v = *reinterpret_cast<const float4 *>(xr + m * kHalf + r);
-                            xa[m] = f2(v.x, v.y);
-                            xb[m] = f2(v.z, v.w);
-                        }
-                        row_pair<BITS, M>(w[0], w[1], xa, t, mg);
-                        row_pair<BITS, M>(w[2], w[3], xb, t, mg);
-                    }
-                }
-#pragma unroll
-                for (int m = 0; m < M; m++) {
-                    float tmp[NP];
-#pragma unroll
-                    for (int q = 0; q < NP; q++) tmp[q] = t[m][q].x + t[m][q].y;
-                    if (BITS == 4) {
-                        // group fold with 16^-k taken into the scale (exact)
-                        const float4 slo = *reinterpret_cast<const float4 *>(item + kItem + 16 * lane);
-                        const float4 shi = *reinterpret_cast<const float4 *>(item + kItem + 512 + 16 * lane);
-                        const float sc[8] = {slo.x, slo.y, slo.z, slo.w, shi.x, shi.y, shi.z, shi.w};
-#pragma unroll
-                        for (int q = 0; q < NP; q++) acc[m][q] = fmaf(tmp[q], sc[q] * pos_scale(q), acc[m][q]);
-                    } else {
-#pragma unroll
-                        for (int q = 0; q < NP; q++) acc[m][q] += tmp[q];
-                    }
-                }
-            }
+            if (ok) half_item<BITS, M>(item, hf, xr, ofs, mg, lane, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             __syncwarp(); // the x slot is reused XD - 1 items later
@@ -629,6 +637,258 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
     __syncthreads();
 }
 
+// ---------------------------------------------------------------------------
+// Cluster split, for matrices with fewer column tiles than SMs: column tile t
+// goes to cluster t of k CTAs (k <= 8, k * tiles <= SMs), and CTA rank r of
+// the cluster takes the tile's 64-row units [r*units/k, (r+1)*units/k). Each
+// CTA runs the same item pipeline as cmv_kernel (producer ring filled before
+// griddepcontrol.wait, eight consumer warps on half items) and adds its warps'
+// sums in warp order in shared memory; the k CTAs' sums then meet in
+// distributed shared memory: after a cluster barrier, CTA r adds the k CTAs'
+// sums of its 1/k of the tile's entries in rank order and writes them, and a
+// second cluster barrier keeps every CTA's shared memory alive until all
+// reads are done. No global scratch and no atomics: the reduction costs two
+// cluster barriers instead of global round trips.
+// ---------------------------------------------------------------------------
+template <int BITS, int M> struct KCfg {
+    static constexpr int NP = BITS == 8 ? 4 : 8;
+    static constexpr int E = M * NP * 32;
+    static constexpr int SLOT = BITS == 4 ? kItem + 1024 : kItem;
+    static constexpr int XD = 4;
+    static constexpr int XSLOT = XD * kHalf * M * 4;
+    static constexpr int RED = W * E * 4;  // per-warp sums
+    static constexpr int CPART = E * 4;    // this CTA's sums, read across the cluster
+    static constexpr int FIXED = W * XSLOT + RED + CPART + 1024;
+    static constexpr int R0 = (kSmemCap - FIXED) / SLOT;
+    static constexpr int R = R0 < 16 ? R0 : 16; // ring slots
+    static constexpr int RING_OFF = 0;
+    static constexpr int X_OFF = R * SLOT;
+    static constexpr int RED_OFF = X_OFF + W * XSLOT;
+    static constexpr int CPART_OFF = RED_OFF + RED;
+    static constexpr int BAR_OFF = CPART_OFF + CPART;
+    static constexpr int MISC_OFF = BAR_OFF + 2 * R * 8;
+    static constexpr int SMEM = MISC_OFF + 32;
+    static_assert(R >= 6, "ring too shallow");
+    static_assert(SMEM <= kSmemCap, "shared memory budget");
+};
+constexpr int kKThreads = (W + 1) * 32; // producer warp + consumer warps
+constexpr int kMaxCluster = 8;
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// A float of the shared memory of cluster CTA `rank` at this CTA's address p.
+__device__ __forceinline__ float ld_cluster(const float *p, uint32_t rank) {
+    uint32_t remote;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+template <int BITS, int M>
+__global__ void __launch_bounds__(kKThreads, 2) kcmv_kernel(CmvParams p) {
+    using C = KCfg<BITS, M>;
+    constexpr int R = C::R, NP = C::NP, E = C::E;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *empty = full + R;
+    volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF);
+    volatile int *issued = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 4); // see cmv_kernel
+    float *red = reinterpret_cast<float *>(smem + C::RED_OFF);
+    float *cpart = reinterpret_cast<float *>(smem + C::CPART_OFF);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int k = p.k;
+    const int tile = blockIdx.x / k, r = blockIdx.x % k; // r is the cluster rank: clusters are k consecutive CTAs
+    const int u0 = (int)((long long)r * p.units / k), u1 = (int)((long long)(r + 1) * p.units / k);
+    const int nitems = u1 - u0;
+    const long long i0 = (long long)tile * p.units + u0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < R; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 2); // both halves consumed
+        }
+        *abort = 0;
+        *issued = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        // ---------------- producer: the weights depend on nothing ----------------
+        if (lane == 0) {
+            pdl_trigger(); // the next kernel on the stream may be scheduled beside this one
+            for (int j = 0; j < nitems; j++) {
+                const int s = j % R;
+                if (j >= R && !wait_bar(&empty[s], ((j / R) & 1) ^ 1, abort, p.status)) continue;
+                const long long it = i0 + j;
+                uint8_t *dst = smem + C::RING_OFF + s * C::SLOT;
+                mbar_arrive_expect_tx(&full[s], C::SLOT);
+                bulk_load(dst, p.codes + it * kItem, kItem, &full[s]);
+                if (BITS == 4) bulk_load(dst + kItem, p.scale + it * (2 * kCols), 1024, &full[s]);
+                *issued = j + 1;
+            }
+        }
+    } else {
+        // ---------------- consumers: warp cw takes half h = cw % 2 of items cw/2, cw/2 + WI, ... ----------------
+        const int cw = warp - 1;
+        const uint32_t mg = p.magic;
+        const int hf = cw & 1, js = cw >> 1;
+        pdl_wait(); // x belongs to the previous kernel until here
+        float *xs = reinterpret_cast<float *>(smem + C::X_OFF + cw * C::XSLOT);
+        int unit_x = u0 + js; // unit of the next item to copy activations for
+        int tx = 0;
+        const int nmine = js < nitems ? (nitems - 1 - js) / WI + 1 : 0;
+        const float *xrow = p.x + hf * kHalf + lane;
+        auto issue_x = [&]() {
+            if (tx < nmine) {
+                float *dst = xs + (tx & (C::XD - 1)) * M * kHalf + lane;
+                const int row = unit_x * kRows + hf * kHalf + lane;
+                const bool v = row < p.rows;
+                const float *src = xrow + (v ? unit_x * kRows : -(hf * kHalf + lane));
+#pragma unroll
+                for (int m = 0; m < M; m++) cp_async_f32(dst + m * kHalf, src + (size_t)m * p.rows, v);
+                unit_x += WI;
+            }
+            cp_async_commit();
+            tx++;
+        };
+        for (int i = 0; i < C::XD - 1; i++) issue_x();
+        uint32_t ofs[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) ofs[q] = q * kCols + 4 * (lane ^ (q << 2));
+        float acc[M][NP];
+#pragma unroll
+        for (int m = 0; m < M; m++)
+#pragma unroll
+            for (int q = 0; q < NP; q++) acc[m][q] = 0.f;
+        const uint8_t *ring = smem + C::RING_OFF;
+        int slot = js % R, ph = (js / R) & 1;
+        for (int j = js, t_it = 0; j < nitems; j += WI, t_it++) {
+            issue_x();
+            cp_async_wait<C::XD - 1>();
+            if (*issued <= j) {
+                const unsigned long long t0 = global_ns();
+                while (*issued <= j && !*abort) {
+                    if (global_ns() - t0 > kWaitNs) {
+                        atomicOr(p.status, TQ_STATUS_TIMEOUT);
+                        *abort = 1;
+                    }
+                }
+            }
+            const bool ok = wait_bar(&full[slot], ph, abort, p.status);
+            __syncwarp();
+            const uint8_t *item = ring + slot * C::SLOT;
+            if (ok) half_item<BITS, M>(item, hf, xs + (t_it & (C::XD - 1)) * M * kHalf, ofs, mg, lane, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            __syncwarp();
+            slot += WI;
+            if (slot >= R) {
+                slot -= R;
+                ph ^= 1;
+            }
+        }
+        cp_async_wait<0>();
+        float *rb = red + (size_t)cw * E + lane;
+#pragma unroll
+        for (int m = 0; m < M; m++)
+#pragma unroll
+            for (int q = 0; q < NP; q++) rb[(m * NP + q) * 32] = acc[m][q];
+    }
+    __syncthreads(); // every warp's sums are in red
+    pdl_wait();      // the output belongs to the previous kernel until here (consumers waited already)
+    // this CTA's sums: entries e = (m*NP + q)*32 + l, warps added in order
+    for (int e = threadIdx.x; e < E; e += kKThreads) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < W; w++) v += red[w * E + e];
+        cpart[e] = v;
+    }
+    auto write_entry = [&](int e, float v) {
+        const int l = e & 31, q = (e >> 5) % NP, m = (e >> 5) / NP;
+        const int col = out_col<BITS>(p, tile, l, q);
+        if (col >= 0) p.out[(size_t)m * p.cols + col] = BITS == 8 ? v * __ldg(p.scale + col) : v;
+    };
+    if (k == 1) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < E; e += kKThreads) write_entry(e, cpart[e]);
+        return;
+    }
+    cluster_sync_all(); // every CTA's cpart is complete and visible to the cluster
+    const int lo = r * E / k, hi = (r + 1) * E / k;
+    for (int e = lo + threadIdx.x; e < hi; e += kKThreads) {
+        float v = 0.f;
+        for (int q = 0; q < k; q++) v += ld_cluster(cpart + e, (uint32_t)q);
+        write_entry(e, v);
+    }
+    cluster_sync_all(); // no CTA leaves (and frees its shared memory) while others still read it
+}
+
+template <int BITS, int M>
+cudaError_t launch_kcmv(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
+                        int k) {
+    using C = KCfg<BITS, M>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static int configured[64] = {};
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(kcmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return e;
+        configured[dev] = 1;
+    }
+    CmvParams prm = {};
+    prm.codes = mat.codes;
+    prm.scale = mat.scale;
+    prm.x = x;
+    prm.out = out;
+    prm.status = scr.status;
+    prm.rows = mat.rows;
+    prm.cols = mat.cols;
+    prm.half = mat.cols / 2;
+    prm.units = mat.units;
+    prm.tiles = mat.tiles;
+    prm.items = (long long)mat.tiles * mat.units;
+    prm.magic = 0x4B000000u;
+    prm.k = k;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = k;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cfg.gridDim = dim3(mat.tiles * k);
+    cfg.blockDim = dim3(kKThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    return cudaLaunchKernelEx(&cfg, kcmv_kernel<BITS, M>, prm);
+}
+
+// Cluster size for the cluster split, or 0 for the stream-K kernel. With
+// fewer column tiles than SMs each tile gets k = min(8, SMs / tiles, units)
+// CTAs, so k * tiles <= SMs: the reduction is cheap but up to a few SMs idle
+// and each CTA takes a little more. Measured on B200, that wins for int8 (the
+// unpack is cheap, the call is latency-bound) and for small int4 matrices,
+// and loses for int4 matrices of more than 12 items per SM under stream-K
+// (the unpack is ALU-bound): 4096 x 11008 took 14.3 us per call split by
+// clusters against 10.0 us by stream-K.
+inline int cluster_split(const TqMatrixDev &mat, int sms) {
+    if (mat.tiles >= sms) return 0;
+    if (mat.bits == 4 && (long long)mat.tiles * mat.units > 12LL * sms) return 0;
+    int k = sms / mat.tiles;
+    if (k > kMaxCluster) k = kMaxCluster;
+    if (k > mat.units) k = mat.units;
+    return k < 1 ? 1 : k;
+}
+
 template <int BITS, int M>
 cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st) {
     using C = CCfg<BITS, M>;
@@ -645,7 +905,7 @@ cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const
         if (e != cudaSuccess) return e;
         configured[dev] = 1;
     }
-    CmvParams prm;
+    CmvParams prm = {};
     prm.codes = mat.codes;
     prm.scale = mat.scale;
     prm.x = x;
@@ -662,6 +922,7 @@ cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const
     prm.magic = 0x4B000000u;
     const int sms = sm_count[dev];
     if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS) return cudaErrorInvalidValue;
+    if (const int k = cluster_split(mat, sms)) return launch_kcmv<BITS, M>(mat, x, out, scr, st, k);
     if ((size_t)2 * sms * C::E > TQ_SCRATCH_PARTIAL_FLOATS) return cudaErrorInvalidValue;
     const int ctas = (int)(prm.items < sms ? prm.items : sms);
     cudaLaunchAttribute attr[1];
