@@ -231,11 +231,14 @@ def test_more_than_8_rows_runs_in_chunks(kernel):
     _check_matmul(4, 512, 640, 15)
 
 
-def test_results_are_bit_reproducible(kernel):
-    rows, cols = 4096, 11008
+# int4 4096 x 11008 runs the stream-K split (cross-CTA partials in CTA order);
+# int8 4096 x 4096 and int4 1000 x 1030 the cluster split (distributed shared
+# memory, rank order) of the default kernel.
+@pytest.mark.parametrize("bits,rows,cols", [(4, 4096, 11008), (8, 4096, 4096), (4, 1000, 1030)])
+def test_results_are_bit_reproducible(kernel, bits, rows, cols):
     w = O.synth((rows, cols), 3, 1, 0.02)
-    q, s = O.quantize4(w)
-    qm = Q4Matrix(rows, cols, q, s)
+    q, s = (O.quantize8 if bits == 8 else O.quantize4)(w)
+    qm = (QMatrix if bits == 8 else Q4Matrix)(rows, cols, q, s)
     x = O.synth((rows,), 3, 2, 1.0)
     outs = []
     for _ in range(3):
