@@ -28,3 +28,12 @@ def pytest_collection_modifyitems(config, items):
 TESTS = os.path.dirname(os.path.abspath(__file__))
 if TESTS not in sys.path:
     sys.path.insert(0, TESTS)
+
+
+def free_port() -> int:
+    """A TCP port on 127.0.0.1 that the OS reports free now (for the
+    rendezvous of multi-process tests)."""
+    import socket
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]

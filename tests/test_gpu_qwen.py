@@ -8,6 +8,8 @@ import os
 import numpy as np
 import pytest
 
+from conftest import free_port
+
 from oracle import oracle as O
 from tensai_b200 import _lib
 from tensai_b200.decode import QWEN_7B, Qwen, synth_tokens
@@ -93,7 +95,7 @@ def run_tp(cfg, seed, prompt, n, world):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29500 + os.getpid() % 500
+    port = free_port()
     procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q, cfg, seed, prompt, n)) for r in range(world)]
     for p in procs:
         p.start()

@@ -4,6 +4,8 @@ NCCL id reaches every rank of a world-size-2 gloo process group."""
 import os
 
 import pytest
+
+from conftest import free_port
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
@@ -49,7 +51,7 @@ def _worker(rank, world, port, q):
 def test_nccl_id_reaches_every_rank():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29000 + os.getpid() % 1000
+    port = free_port()
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
