@@ -95,7 +95,15 @@ struct CmvParams {
     int rows, cols, half, units, tiles;
     uint32_t magic; // 0x4B000000 (2^23), passed in so it sits in a register: one LOP3 per nibble
     int k;          // cluster split: CTAs per column tile (kcmv_kernel)
+    int epi;        // TQ_EPI_* (M = 1)
 };
+
+// silu(g) * u as the Go code forms it (model.go:296-299): silu in float64,
+// the product in float32.
+__device__ __forceinline__ float swiglu(float g, float u) {
+    const double gd = (double)g;
+    return __fmul_rn((float)__ddiv_rn(gd, __dadd_rn(1.0, exp(-gd))), u);
+}
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -174,10 +182,41 @@ __device__ __forceinline__ int out_col(const CmvParams &p, int tile, int lane, i
     return hi ? p.half + pair : pair;
 }
 
+// Entry e = (m*NP + q)*32 + l of a finished tile to the output. With the
+// SwiGLU epilogue (int4, M = 1) the gate entries (q < 4) write silu(v) * u,
+// u being the sum of their up partner e + kUp, and the up entries nothing.
+constexpr int kUp = 4 * 32;
+template <int BITS>
+__device__ __forceinline__ void write_entry(const CmvParams &p, int tile, int e, float v, float u) {
+    constexpr int NP = BITS == 8 ? 4 : 8;
+    const int l = e & 31, q = (e >> 5) % NP, m = (e >> 5) / NP;
+    if (BITS == 4 && p.epi == TQ_EPI_SWIGLU) {
+        const int c = tile * kCols + 4 * l + q;
+        if (q < 4 && c < p.half) p.out[c] = swiglu(v, u);
+        return;
+    }
+    const int col = out_col<BITS>(p, tile, l, q);
+    if (col >= 0) p.out[(size_t)m * p.cols + col] = BITS == 8 ? v * __ldg(p.scale + col) : v;
+}
+// Whether entry e needs its up partner's sum too (SwiGLU gate entries).
+template <int BITS> __device__ __forceinline__ bool needs_up(const CmvParams &p, int e) {
+    return BITS == 4 && p.epi == TQ_EPI_SWIGLU && e < kUp;
+}
+
 // Sums of a finished tile (entry (m, j, lane) in the order [m][j][lane]) to the output.
 template <int BITS, int M>
 __device__ __forceinline__ void write_out(const CmvParams &p, int tile, int lane, const float (&v)[M][BITS == 8 ? 4 : 8]) {
     constexpr int NP = BITS == 8 ? 4 : 8;
+    if constexpr (BITS == 4 && M == 1) {
+        if (p.epi == TQ_EPI_SWIGLU) { // sums e (gate column c) and 4 + e (up column c)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int c = tile * kCols + 4 * lane + e;
+                if (c < p.half) p.out[c] = swiglu(v[0][e], v[0][4 + e]);
+            }
+            return;
+        }
+    }
 #pragma unroll
     for (int j = 0; j < NP; j++) {
         const int col = out_col<BITS>(p, tile, lane, j);
@@ -541,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
             const long long t0 = (long long)tile * p.units;
             const int cf = split.owner(t0), cl = split.owner(t0 + p.units - 1);
             const int slot_f = split.slot(cf, t0);
-            for (int e = threadIdx.x - 32; e < E; e += W * 32) {
+            auto sum_entry = [&](int e) {
                 constexpr int CH = 16; // contributor loads in flight per thread
                 float v = 0.f;
                 for (int cc = cf; cc <= cl; cc += CH) {
@@ -554,9 +593,12 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
 #pragma unroll
                     for (int u = 0; u < CH; u++) v += pv[u];
                 }
-                const int l = e & 31, q = (e >> 5) % NP, m = (e >> 5) / NP;
-                const int col = out_col<BITS>(p, tile, l, q);
-                if (col >= 0) p.out[(size_t)m * p.cols + col] = BITS == 8 ? v * __ldg(p.scale + col) : v;
+                return v;
+            };
+            for (int e = threadIdx.x - 32; e < E; e += W * 32) {
+                if (BITS == 4 && p.epi == TQ_EPI_SWIGLU && e >= kUp) continue; // taken by its gate entry
+                const float v = sum_entry(e);
+                write_entry<BITS>(p, tile, e, v, needs_up<BITS>(p, e) ? sum_entry(e + kUp) : 0.f);
             }
         };
         // The slice's last segment, by all consumer warps: every warp's sums
@@ -583,14 +625,17 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
             const int tile = last_tile, cf = last_cf, cl = last_cl;
             const int ct = threadIdx.x - 32; // 0 .. W*32-1
             float *part = p.partial + (size_t)last_slot * E;
-            for (int e = ct; e < E; e += W * 32) { // entry e = (m*NP + q)*32 + l
+            auto warp_sum = [&](int e) {
                 float v = 0.f;
 #pragma unroll
                 for (int w = 0; w < W; w++) v += red[(size_t)(b * W + w) * E + e];
+                return v;
+            };
+            for (int e = ct; e < E; e += W * 32) { // entry e = (m*NP + q)*32 + l
+                const float v = warp_sum(e);
                 if (cf == cl) {
-                    const int l = e & 31, q = (e >> 5) % NP, m = (e >> 5) / NP;
-                    const int col = out_col<BITS>(p, tile, l, q);
-                    if (col >= 0) p.out[(size_t)m * p.cols + col] = BITS == 8 ? v * __ldg(p.scale + col) : v;
+                    if (!(BITS == 4 && p.epi == TQ_EPI_SWIGLU && e >= kUp))
+                        write_entry<BITS>(p, tile, e, v, needs_up<BITS>(p, e) ? warp_sum(e + kUp) : 0.f);
                 } else {
                     part[e] = v;
                 }
@@ -807,29 +852,29 @@ __global__ void __launch_bounds__(kKThreads, 2) kcmv_kernel(CmvParams p) {
         for (int w = 0; w < W; w++) v += red[w * E + e];
         cpart[e] = v;
     }
-    auto write_entry = [&](int e, float v) {
-        const int l = e & 31, q = (e >> 5) % NP, m = (e >> 5) / NP;
-        const int col = out_col<BITS>(p, tile, l, q);
-        if (col >= 0) p.out[(size_t)m * p.cols + col] = BITS == 8 ? v * __ldg(p.scale + col) : v;
-    };
+    // entries written: with SwiGLU the gate entries, each taking its up partner
+    const bool sw = BITS == 4 && p.epi == TQ_EPI_SWIGLU;
+    const int EW = sw ? kUp : E;
     if (k == 1) {
         __syncthreads();
-        for (int e = threadIdx.x; e < E; e += kKThreads) write_entry(e, cpart[e]);
-        return;
+        for (int e = threadIdx.x; e < EW; e += kKThreads) write_entry<BITS>(p, tile, e, cpart[e], sw ? cpart[e + kUp] : 0.f);
+    } else {
+        cluster_sync_all(); // every CTA's cpart is complete and visible to the cluster
+        const int lo = r * EW / k, hi = (r + 1) * EW / k;
+        for (int e = lo + threadIdx.x; e < hi; e += kKThreads) {
+            float v = 0.f, u = 0.f;
+            for (int q = 0; q < k; q++) v += ld_cluster(cpart + e, (uint32_t)q);
+            if (sw)
+                for (int q = 0; q < k; q++) u += ld_cluster(cpart + e + kUp, (uint32_t)q);
+            write_entry<BITS>(p, tile, e, v, u);
+        }
+        cluster_sync_all(); // no CTA leaves (and frees its shared memory) while others still read it
     }
-    cluster_sync_all(); // every CTA's cpart is complete and visible to the cluster
-    const int lo = r * E / k, hi = (r + 1) * E / k;
-    for (int e = lo + threadIdx.x; e < hi; e += kKThreads) {
-        float v = 0.f;
-        for (int q = 0; q < k; q++) v += ld_cluster(cpart + e, (uint32_t)q);
-        write_entry(e, v);
-    }
-    cluster_sync_all(); // no CTA leaves (and frees its shared memory) while others still read it
 }
 
 template <int BITS, int M>
 cudaError_t launch_kcmv(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
-                        int k) {
+                        int k, int epi) {
     using C = KCfg<BITS, M>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -855,6 +900,7 @@ cudaError_t launch_kcmv(const TqMatrixDev &mat, const float *x, float *out, cons
     prm.items = (long long)mat.tiles * mat.units;
     prm.magic = 0x4B000000u;
     prm.k = k;
+    prm.epi = epi;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -890,7 +936,8 @@ inline int cluster_split(const TqMatrixDev &mat, int sms) {
 }
 
 template <int BITS, int M>
-cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st) {
+cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
+                       int epi) {
     using C = CCfg<BITS, M>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -920,9 +967,10 @@ cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const
     prm.tiles = mat.tiles;
     prm.items = (long long)mat.tiles * mat.units;
     prm.magic = 0x4B000000u;
+    prm.epi = epi;
     const int sms = sm_count[dev];
     if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS) return cudaErrorInvalidValue;
-    if (const int k = cluster_split(mat, sms)) return launch_kcmv<BITS, M>(mat, x, out, scr, st, k);
+    if (const int k = cluster_split(mat, sms)) return launch_kcmv<BITS, M>(mat, x, out, scr, st, k, epi);
     if ((size_t)2 * sms * C::E > TQ_SCRATCH_PARTIAL_FLOATS) return cudaErrorInvalidValue;
     const int ctas = (int)(prm.items < sms ? prm.items : sms);
     cudaLaunchAttribute attr[1];
@@ -951,10 +999,18 @@ cudaError_t tq_launch_cmv(const TqMatrixDev &mat, const float *x, float *out, in
         float *om = out + (size_t)m0 * mat.cols;
         cudaError_t e;
         if (mat.bits == 8)
-            e = mm == 1 ? launch_cmv<8, 1>(mat, xm, om, scr, st) : launch_cmv<8, 2>(mat, xm, om, scr, st);
+            e = mm == 1 ? launch_cmv<8, 1>(mat, xm, om, scr, st, TQ_EPI_NONE) : launch_cmv<8, 2>(mat, xm, om, scr, st, TQ_EPI_NONE);
         else
-            e = mm == 1 ? launch_cmv<4, 1>(mat, xm, om, scr, st) : launch_cmv<4, 2>(mat, xm, om, scr, st);
+            e = mm == 1 ? launch_cmv<4, 1>(mat, xm, om, scr, st, TQ_EPI_NONE) : launch_cmv<4, 2>(mat, xm, om, scr, st, TQ_EPI_NONE);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+// One activation row with an epilogue (TQ_EPI_*): the decode steps' matvecs.
+cudaError_t tq_launch_cmv_epi(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
+                              int epi) {
+    if (epi == TQ_EPI_NONE) return tq_launch_cmv(mat, x, out, 1, scr, st);
+    if (epi != TQ_EPI_SWIGLU || mat.bits != 4 || mat.cols % 2 || mat.rows == 0) return cudaErrorInvalidValue;
+    return launch_cmv<4, 1>(mat, x, out, scr, st, epi);
 }

@@ -138,6 +138,17 @@ cudaError_t tq_launch_to_tiled(const TqMatrixDev &m, const uint8_t *ref_q, const
 cudaError_t tq_launch_from_tiled(const TqMatrixDev &m, uint8_t *ref_q, float *ref_scale, cudaStream_t st);
 cudaError_t tq_launch_matvec(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                              cudaStream_t st);
+
+// What a single-row (M = 1) CUDA-core matvec does with its output, for the
+// decode steps:
+//   TQ_EPI_NONE    out = x W;
+//   TQ_EPI_SWIGLU  int4 [gate | up] matrix of 2F columns (column c and F + c
+//                  share a code byte): out[c] = float32(silu(gate_c)) * up_c,
+//                  c < F, silu in float64 (_example/qwen/model.go:296-299).
+#define TQ_EPI_NONE 0
+#define TQ_EPI_SWIGLU 1
+cudaError_t tq_launch_cmv_epi(const TqMatrixDev &m, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
+                              int epi);
 cudaError_t tq_launch_igemv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                             cudaStream_t st);
 // Single-launch tensor-core matvec for M <= 8 rows per launch (tq_gemv.cu).

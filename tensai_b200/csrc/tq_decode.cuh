@@ -161,121 +161,224 @@ __global__ void attention_kernel(const float *q, int qstride, const float *kc, c
 inline size_t attention_smem(int ctx) { return (sizeof(double) + sizeof(float)) * (size_t)ctx; }
 
 // ---- split-K decode attention -------------------------------------------------------
-// The same attention for the decode step's single query row, spread over
-// chunks of kAttChunk cached positions so that long contexts use every SM:
-//   scores:   per (head, chunk): s_t = (q . k_t in float64) * scale, and the
-//             chunk's max m_b and sum l_b = sum exp(s_t - m_b);
-//   weights:  per (head, chunk): the softmax's global max M and sum
-//             L = sum_b l_b exp(m_b - M) (chunks in order), p_t = float32(
-//             exp(s_t - M) / L) as the Go code forms it, and the chunk's
-//             float32 partial sum_t p_t * v_t (positions in order);
-//   combine:  per head: the chunk partials summed in chunk order.
+// The attention of the decode step's single query row, spread over chunks of
+// kAttChunk cached positions so that long contexts use every SM. Two passes:
+//   scores:   per (head, chunk), one thread per position: s_t = (q . k_t, the
+//             float64 products added in dimension order) * scale, then the
+//             chunk's max m_b and sum l_b = sum exp(s_t - m_b). With RoPE
+//             (Qwen2) the pass first rotates this step's q head (and, in the
+//             chunk holding the position, its k head) from the fused row with
+//             the step's cos/sin table, and the first head of each KV group
+//             stores the rotated k and the biased v in the caches;
+//   weights:  per (head, chunk): the softmax's global max M and sum L =
+//             sum_b l_b exp(m_b - M), p_t = float32(exp(s_t - M) / L) as the
+//             Go code forms it, and the chunk's float32 sums p_t * v_t over
+//             its positions in order (in sub-chunks added in order); the last
+//             chunk of a head to finish adds the chunk sums in chunk order.
 // Scratch (per engine): scores [heads][ctx] doubles, stats [heads][chunks][2]
-// doubles, partials [heads][chunks][hd] floats.
+// doubles, partials [heads][chunks][hd] floats, arrival counters [heads].
 constexpr int kAttChunk = 128;
+constexpr int kAttMaxHd = 256;
+constexpr int kAttWThreads = 512;
 
-__global__ void __launch_bounds__(128) att_scores_kernel(const float *q, const float *kc, int kvstride, const int *state,
-                                                         int hd, int group, double scale, double *scores,
-                                                         double *stats, int ctx, int nchunks) {
+// RoPE of the scores pass (Qwen2, model.go:219-229: half-split pairs (i, i +
+// hd/2)); cs == nullptr for none (GPT-2, whose q, k and v are stored already).
+struct AttRope {
+    const double *cs = nullptr; // [hd/2][2]: cos, sin of pos * theta^(-2i/hd)
+    const float *k = nullptr;   // this position's raw k heads [n_kv][hd] and v heads
+    const float *v = nullptr;
+    const float *qbias = nullptr, *kbias = nullptr, *vbias = nullptr;
+    float *kc = nullptr, *vc = nullptr; // caches [ctx][kvstride]
+};
+
+// cs[2i], cs[2i + 1] = cos, sin of pos * theta^(-2i/hd), i < hd/2 (model.go:221-224).
+__device__ __forceinline__ void rope_table(double *cs, int pos, int hd, double theta) {
+    for (int i = threadIdx.x; i < hd / 2; i += blockDim.x) {
+        const double freq = pow(theta, __ddiv_rn(-2.0 * (double)i, (double)hd));
+        double s, c;
+        sincos(__dmul_rn((double)pos, freq), &s, &c);
+        cs[2 * i] = c;
+        cs[2 * i + 1] = s;
+    }
+}
+
+// Rotated pair (a, b) of dimension i with the table: (a c - b s, b c + a s).
+__device__ __forceinline__ void rope_pair(const double *cs, int i, float a, float b, float &r0, float &r1) {
+    const double c = cs[2 * i], s = cs[2 * i + 1], ad = (double)a, bd = (double)b;
+    r0 = (float)__dsub_rn(__dmul_rn(ad, c), __dmul_rn(bd, s));
+    r1 = (float)__dadd_rn(__dmul_rn(bd, c), __dmul_rn(ad, s));
+}
+
+__global__ void __launch_bounds__(kAttChunk) att_scores_kernel(const float *q, const float *kc, int kvstride,
+                                                               const int *state, int hd, int group, double scale,
+                                                               double *scores, double *stats, int ctx, int nchunks,
+                                                               AttRope rope) {
     step_entry_wait();
-    __shared__ double ss[kAttChunk];
+    __shared__ __align__(16) float qs[kAttMaxHd];
+    __shared__ __align__(16) float kp[kAttMaxHd];
     __shared__ double sh[32];
     const int h = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttChunk;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, kvh = h / group;
+    const int kvh = h / group, half = hd / 2;
     if (t0 > pos) return;
-    const int t1 = min(t0 + kAttChunk, pos + 1);
-    const float *qh = q + h * hd;
-    for (int t = t0 + warp; t < t1; t += 4) {
-        const float *kt = kc + (size_t)t * kvstride + kvh * hd;
-        double s = 0;
-        for (int i = lane; i < hd; i += 32) s = __dadd_rn(s, __dmul_rn((double)qh[i], (double)kt[i]));
-        s = warp_sum_d(s);
-        if (lane == 0) ss[t - t0] = __dmul_rn(s, scale);
+    const bool here = pos < t0 + kAttChunk; // this chunk holds the step's own position
+    if (rope.cs) {
+        for (int i = threadIdx.x; i < half; i += blockDim.x) {
+            const int j = h * hd + i;
+            rope_pair(rope.cs, i, __fadd_rn(q[j], rope.qbias[j]), __fadd_rn(q[j + half], rope.qbias[j + half]), qs[i],
+                      qs[i + half]);
+            if (here) {
+                const int kj = kvh * hd + i;
+                rope_pair(rope.cs, i, __fadd_rn(rope.k[kj], rope.kbias[kj]),
+                          __fadd_rn(rope.k[kj + half], rope.kbias[kj + half]), kp[i], kp[i + half]);
+            }
+        }
+        if (here && h % group == 0) { // the KV group's first head stores this position's k and v
+            __syncthreads();
+            float *kd = rope.kc + (size_t)pos * kvstride + kvh * hd;
+            float *vd = rope.vc + (size_t)pos * kvstride + kvh * hd;
+            for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+                kd[i] = kp[i];
+                vd[i] = __fadd_rn(rope.v[kvh * hd + i], rope.vbias[kvh * hd + i]);
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) qs[i] = q[h * hd + i];
     }
     __syncthreads();
-    double mx = -INFINITY;
-    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) mx = fmax(mx, ss[t - t0]);
-    mx = block_reduce_d(mx, sh, 1);
-    double l = 0;
-    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
-        l = __dadd_rn(l, exp(__dsub_rn(ss[t - t0], mx)));
-        scores[(size_t)h * ctx + t] = ss[t - t0];
+    const int t = t0 + threadIdx.x;
+    double s = -INFINITY;
+    if (t <= pos) {
+        const float *kt = (rope.cs && t == pos) ? kp : kc + (size_t)t * kvstride + kvh * hd;
+        double acc = 0;
+        for (int i0 = 0; i0 < hd; i0 += 32) { // 8 loads in flight, then the products in order
+            float4 kv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) kv[u] = *reinterpret_cast<const float4 *>(kt + i0 + 4 * u);
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float4 qv = *reinterpret_cast<const float4 *>(qs + i0 + 4 * u);
+                acc = __dadd_rn(acc, __dmul_rn((double)qv.x, (double)kv[u].x));
+                acc = __dadd_rn(acc, __dmul_rn((double)qv.y, (double)kv[u].y));
+                acc = __dadd_rn(acc, __dmul_rn((double)qv.z, (double)kv[u].z));
+                acc = __dadd_rn(acc, __dmul_rn((double)qv.w, (double)kv[u].w));
+            }
+        }
+        s = __dmul_rn(acc, scale);
+        scores[(size_t)h * ctx + t] = s;
     }
-    l = block_reduce_d(l, sh, 0);
+    const double mx = block_reduce_d(s, sh, 1);
+    const double l = block_reduce_d(t <= pos ? exp(__dsub_rn(s, mx)) : 0.0, sh, 0);
     if (threadIdx.x == 0) {
         stats[((size_t)h * nchunks + b) * 2] = mx;
         stats[((size_t)h * nchunks + b) * 2 + 1] = l;
     }
 }
 
-__global__ void __launch_bounds__(128) att_weighted_kernel(const float *vc, int kvstride, const int *state, int hd,
-                                                           int group, const double *scores, const double *stats,
-                                                           float *partial, int ctx, int nchunks) {
+// One CTA's arrival at a counter after a barrier that ordered the CTA's
+// stores; acq_rel at gpu scope, the last of n arrivals re-arms the counter.
+__device__ __forceinline__ bool att_arrive_last(unsigned *counter, unsigned n) {
+    unsigned prev;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
+    const bool last = prev == n - 1;
+    if (last) asm volatile("st.relaxed.gpu.u32 [%0], %1;" ::"l"(counter), "r"(0u) : "memory");
+    return last;
+}
+
+__global__ void __launch_bounds__(kAttWThreads) att_weighted_kernel(const float *vc, int kvstride, const int *state,
+                                                                    int hd, int group, const double *scores,
+                                                                    const double *stats, float *partial,
+                                                                    unsigned *count, float *out, int ctx,
+                                                                    int nchunks) {
     step_entry_wait();
     __shared__ float ps[kAttChunk];
+    __shared__ float sub[kAttWThreads];
+    __shared__ double ml[2];
+    __shared__ int last;
     const int h = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttChunk, kvh = h / group;
     if (t0 > pos) return;
     const int t1 = min(t0 + kAttChunk, pos + 1), nb = pos / kAttChunk + 1;
-    const double *st = stats + (size_t)h * nchunks * 2;
-    double M = -INFINITY;
-    for (int c = 0; c < nb; c++) M = fmax(M, st[2 * c]);
-    double L = 0;
-    for (int c = 0; c < nb; c++) L = __dadd_rn(L, __dmul_rn(st[2 * c + 1], exp(__dsub_rn(st[2 * c], M))));
-    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x)
-        ps[t - t0] = (float)__ddiv_rn(exp(__dsub_rn(scores[(size_t)h * ctx + t], M)), L);
-    __syncthreads();
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        const float *v = vc + kvh * hd + i;
-        float acc = 0.f;
-#pragma unroll 8
-        for (int t = t0; t < t1; t++) acc = __fadd_rn(acc, __fmul_rn(ps[t - t0], v[(size_t)t * kvstride]));
-        partial[((size_t)h * nchunks + b) * hd + i] = acc;
+    if (threadIdx.x < 32) { // the softmax's max and sum over the chunks' stats
+        const int lane = threadIdx.x;
+        const double *st = stats + (size_t)h * nchunks * 2;
+        double M = -INFINITY;
+        for (int c = lane; c < nb; c += 32) M = fmax(M, st[2 * c]);
+        M = warp_max_d(M);
+        double L = 0;
+        for (int c = lane; c < nb; c += 32) L = __dadd_rn(L, __dmul_rn(st[2 * c + 1], exp(__dsub_rn(st[2 * c], M))));
+        L = warp_sum_d(L);
+        if (lane == 0) ml[0] = M, ml[1] = L;
     }
-}
-
-__global__ void att_combine_kernel(const float *partial, const int *state, int hd, float *out, int nchunks) {
-    step_entry();
-    const int h = blockIdx.x, nb = state[1] / kAttChunk + 1;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        float acc = 0.f;
-        for (int c = 0; c < nb; c++) acc = __fadd_rn(acc, partial[((size_t)h * nchunks + c) * hd + i]);
-        out[h * hd + i] = acc;
+    __syncthreads();
+    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x)
+        ps[t - t0] = (float)__ddiv_rn(exp(__dsub_rn(scores[(size_t)h * ctx + t], ml[0])), ml[1]);
+    __syncthreads();
+    // nsub sub-chunks of sz positions, each summed in order by hd threads
+    const int nsub = blockDim.x / hd, sz = kAttChunk / nsub;
+    const int sc = threadIdx.x / hd, i = threadIdx.x % hd;
+    const int ta = t0 + sc * sz, tb = min(ta + sz, t1);
+    float acc = 0.f;
+    const float *v = vc + kvh * hd + i;
+    for (int tt = ta; tt < tb; tt += 32) {
+        float vv[32];
+#pragma unroll
+        for (int u = 0; u < 32; u++) vv[u] = tt + u < tb ? v[(size_t)(tt + u) * kvstride] : 0.f;
+#pragma unroll
+        for (int u = 0; u < 32; u++)
+            if (tt + u < tb) acc = __fadd_rn(acc, __fmul_rn(ps[tt + u - t0], vv[u]));
+    }
+    sub[threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.x < hd) {
+        float a = 0.f;
+        for (int c = 0; c < nsub; c++) a = __fadd_rn(a, sub[c * hd + threadIdx.x]);
+        partial[((size_t)h * nchunks + b) * hd + threadIdx.x] = a;
+    }
+    __syncthreads(); // every thread's partial store before the arrival
+    if (threadIdx.x == 0) last = att_arrive_last(count + h, (unsigned)nb) ? 1 : 0;
+    __syncthreads();
+    if (!last) return;
+    for (int j = threadIdx.x; j < hd; j += blockDim.x) {
+        float a = 0.f;
+        for (int c = 0; c < nb; c++) a = __fadd_rn(a, __ldcg(partial + ((size_t)h * nchunks + c) * hd + j));
+        out[h * hd + j] = a;
     }
 }
 
 struct AttScratch {
     double *scores = nullptr, *stats = nullptr;
     float *partial = nullptr;
+    unsigned *count = nullptr;
     int ctx = 0, nchunks = 0;
 };
 
 inline size_t att_scratch_bytes(int heads, int ctx, int hd) {
     const int nc = (ctx + kAttChunk - 1) / kAttChunk;
     return sizeof(double) * (size_t)heads * ctx + sizeof(double) * 2 * (size_t)heads * nc +
-           sizeof(float) * (size_t)heads * nc * hd;
+           sizeof(float) * (size_t)heads * nc * hd + sizeof(unsigned) * (size_t)heads;
 }
 
-// Carves the scratch out of one device buffer of att_scratch_bytes().
-inline AttScratch att_scratch(void *buf, int heads, int ctx, int hd) {
-    AttScratch a;
-    a.ctx = ctx;
-    a.nchunks = (ctx + kAttChunk - 1) / kAttChunk;
-    a.scores = static_cast<double *>(buf);
-    a.stats = a.scores + (size_t)heads * ctx;
-    a.partial = reinterpret_cast<float *>(a.stats + 2 * (size_t)heads * a.nchunks);
-    return a;
+// Carves the scratch out of one device buffer of att_scratch_bytes() and
+// zeroes the arrival counters on stream st.
+inline cudaError_t att_scratch(void *buf, int heads, int ctx, int hd, cudaStream_t st, AttScratch *a) {
+    a->ctx = ctx;
+    a->nchunks = (ctx + kAttChunk - 1) / kAttChunk;
+    a->scores = static_cast<double *>(buf);
+    a->stats = a->scores + (size_t)heads * ctx;
+    a->partial = reinterpret_cast<float *>(a->stats + 2 * (size_t)heads * a->nchunks);
+    a->count = reinterpret_cast<unsigned *>(a->partial + (size_t)heads * a->nchunks * hd);
+    return cudaMemsetAsync(a->count, 0, sizeof(unsigned) * heads, st);
 }
 
 // The decode-step attention of q (heads x hd) over cached positions 0..state[1].
 inline cudaError_t decode_attention(const float *q, const float *kc, const float *vc, int kvstride, float *out,
                                     const int *state, int heads, int hd, int group, double scale, const AttScratch &a,
-                                    cudaStream_t st) {
-    cudaError_t e = step_launch(att_scores_kernel, dim3(heads, a.nchunks), dim3(128), 0, st, q, kc, kvstride, state, hd, group,
-                        scale, a.scores, a.stats, a.ctx, a.nchunks);
+                                    cudaStream_t st, const AttRope &rope = AttRope()) {
+    if (hd % 32 || hd > kAttMaxHd || kAttWThreads % hd) return cudaErrorInvalidValue;
+    cudaError_t e = step_launch(att_scores_kernel, dim3(heads, a.nchunks), dim3(kAttChunk), 0, st, q, kc, kvstride,
+                                state, hd, group, scale, a.scores, a.stats, a.ctx, a.nchunks, rope);
     if (e == cudaSuccess)
-        e = step_launch(att_weighted_kernel, dim3(heads, a.nchunks), dim3(128), 0, st, vc, kvstride, state, hd, group, a.scores,
-                a.stats, a.partial, a.ctx, a.nchunks);
-    if (e == cudaSuccess) e = step_launch(att_combine_kernel, dim3(heads), dim3(128), 0, st, a.partial, state, hd, out, a.nchunks);
+        e = step_launch(att_weighted_kernel, dim3(heads, a.nchunks), dim3(kAttWThreads), 0, st, vc, kvstride, state, hd,
+                        group, a.scores, a.stats, a.partial, a.count, out, a.ctx, a.nchunks);
     return e;
 }
 

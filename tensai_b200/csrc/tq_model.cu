@@ -57,8 +57,21 @@ __global__ void layernorm_kernel(float *x, const float *w, const float *b, float
     __shared__ double sh[32];
     float *xr = x + (size_t)blockIdx.x * n;
     float *o = out + (size_t)blockIdx.x * n;
-    if (y) {
-        for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __fadd_rn(xr[i], __fadd_rn(y[i], yb[i]));
+    if (y) { // loads in batches of 4 per thread ahead of the stores (xr may alias y as far as nvcc knows)
+        const int bd = blockDim.x;
+        for (int i0 = threadIdx.x; i0 < n; i0 += 4 * bd) {
+            float a[4], c[4], e[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = i0 + u * bd;
+                a[u] = i < n ? xr[i] : 0.f;
+                c[u] = i < n ? y[i] : 0.f;
+                e[u] = i < n ? yb[i] : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (i0 + u * bd < n) xr[i0 + u * bd] = __fadd_rn(a[u], __fadd_rn(c[u], e[u]));
+        }
         __syncthreads();
     }
     double s = 0;
@@ -294,7 +307,7 @@ cudaError_t build(Gpt2 &m, uint64_t seed, float sigma, int *rc) {
     TRY(dalloc(m, (void **)&m.part, sizeof(int) * 2 * kArgBlocks));
     void *ab = nullptr;
     TRY(dalloc(m, &ab, att_scratch_bytes(c.n_head, c.ctx, d / c.n_head)));
-    m.att_scr = att_scratch(ab, c.n_head, c.ctx, d / c.n_head);
+    TRY(att_scratch(ab, c.n_head, c.ctx, d / c.n_head, m.st, &m.att_scr));
     TRY(dalloc(m, (void **)&m.tokens, sizeof(int) * (size_t)(c.ctx + 1)));
     if ((*rc = tq_scratch_for(m.device, m.st, &m.scr, 1)) != TQ_OK) return cudaErrorMemoryAllocation;
     const size_t smem = attn_smem(m);
