@@ -45,7 +45,7 @@ METRIC = "int8/int4 dequant-matvec HBM GB/s (% of peak); decode tokens/s at 1/2/
 K_UP, N_UP = 4096, 11008
 LAYERS = 32
 FALLBACK_HBM_GBS = 6650.0
-LAUNCHES_PER_CALL = 1  # cmv_kernel: one launch per int4 M=1 matvec
+LAUNCHES_PER_CALL = 1  # cmv_kernel<4,1,true>: one launch per int4 M=1 matvec
 WORKLOAD = ("int4 g64 MLP pair (up 4096x11008 + down 11008x4096), M=1, fp32 accumulate; "
             "32 resident layer copies streamed per step")
 
@@ -74,7 +74,7 @@ def load_traffic():
     """Per-launch DRAM bytes (read + write) of the matvec kernel from the
     committed ncu summary (its `traffic_bytes_per_launch:` line), or None."""
     import re
-    path = os.path.join(ROOT, "profiles", "cmv_int4_m1_mlp_pair.md")
+    path = os.path.join(ROOT, "profiles", "tmv_int4_m1_mlp_pair.md")
     try:
         with open(path) as f:
             m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", f.read())
@@ -482,8 +482,8 @@ def run_gpu(args, rank: int, world: int):
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "frac_of_8tbs": round(achieved / 8000.0, 4),
                          "traffic": traffic,
-                         "kernel": "cmv_kernel<4,1> (int4 dequant-matvec on the CUDA cores, M=1, "
-                                   "one launch per call)",
+                         "kernel": "cmv_kernel<4,1,true> (int4 matvec on the tensor cores by mma.sync "
+                                   "u8 x s8 over the K-packed codes, M=1, one launch per call)",
                          "call_us_mean": round(kavg * 1e3, 3),
                          "algorithmic_bytes_per_launch": per_launch},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",

@@ -147,13 +147,15 @@ TQ_EXPORT int tq_matmul_dev_fixed(uint64_t handle, const float *x, float *out, i
 
 /* Selects the GPU kernel behind tq_matvec / tq_matmul / tq_matmul_dev for
  * m <= 15 rows (process-wide). 0 (default) = the fastest measured choice per
- * row count: single-launch CUDA-core fp32 FMA for m <= 2, tensor-core integer
- * MMA (weights used as stored, activations split into exact int8 digit
- * planes) for 3 <= m <= 15. 1 = CUDA-core fp32 FMA with per-warp copies;
+ * row count: int4 single rows as 5 below, otherwise single-launch CUDA-core
+ * fp32 FMA for m <= 2 and tensor-core integer MMA (weights used as stored,
+ * activations split into exact int8 digit planes) for 3 <= m <= 15. 1 = CUDA-core fp32 FMA with per-warp copies;
  * 2 = single-launch tensor-core integer MMA; 3 = single-launch CUDA-core fp32
  * FMA, 2 rows per launch; 4 = tensor-core integer MMA with a digit-plane
- * launch. All are GPU implementations with the same contract; there is no CPU
- * path. */
+ * launch; 5 = int4 on the tensor cores by mma.sync (codes from a K-packed
+ * device copy that every int4 matrix holds, activations as exact int8 digits
+ * per 64-row group), one row per launch, int8 as 3. All are GPU
+ * implementations with the same contract; there is no CPU path. */
 TQ_EXPORT int tq_set_matvec_kernel(int which);
 
 /* ---- synthetic inputs ----------------------------------------------------- */

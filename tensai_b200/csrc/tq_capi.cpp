@@ -142,12 +142,16 @@ static cudaError_t read_status(const TqScratch &scr, cudaStream_t st, unsigned *
 }
 
 // Matvec kernel for M <= 15 rows (tq_set_matvec_kernel):
-//   0 (default): single-launch CUDA-core matvec (tq_cmv.cu) for M <= 2, the
-//                tensor-core matvec (tq_igemv.cu) for 3 <= M <= 15;
+//   0 (default): int4 single rows on the tensor cores by mma.sync (tq_cmv.cu,
+//                K-packed copy), otherwise the single-launch CUDA-core matvec
+//                (tq_cmv.cu) for M <= 2 and the tcgen05 matvec (tq_igemv.cu)
+//                for 3 <= M <= 15;
 //   1: CUDA-core matvec with per-warp copies (tq_matvec.cu);
 //   2: single-launch tensor-core matvec (tq_gemv.cu);
 //   3: single-launch CUDA-core matvec (tq_cmv.cu), 2 rows per launch;
-//   4: tensor-core matvec with a digit-plane launch (tq_igemv.cu).
+//   4: tensor-core matvec with a digit-plane launch (tq_igemv.cu);
+//   5: int4 on the tensor cores by mma.sync (tq_cmv.cu), one row per launch;
+//      int8 as 3.
 std::atomic<int> g_matvec_kernel{0};
 
 // M >= TQ_MM_MIN_ROWS: the tf32 tensor-core matmul; fewer rows: the matvec
@@ -160,7 +164,10 @@ static cudaError_t launch_matvec(const TqMatrixDev &m, const float *x, float *ou
     case 2: return tq_launch_gemv(m, x, out, M, scr, st);
     case 3: return tq_launch_cmv(m, x, out, M, scr, st);
     case 4: return tq_launch_igemv(m, x, out, M, scr, st);
-    default: return M <= 2 ? tq_launch_cmv(m, x, out, M, scr, st) : tq_launch_igemv(m, x, out, M, scr, st);
+    case 5: return tq_launch_tmv(m, x, out, M, scr, st);
+    default:
+        if (M == 1 && m.bits == 4 && m.kcodes) return tq_launch_tmv(m, x, out, M, scr, st);
+        return M <= 2 ? tq_launch_cmv(m, x, out, M, scr, st) : tq_launch_igemv(m, x, out, M, scr, st);
     }
 }
 
@@ -179,6 +186,11 @@ void tq_scratch_release(int device, cudaStream_t st) {
 }
 
 cudaError_t tq_read_status(const TqScratch &scr, cudaStream_t st, unsigned *out) { return read_status(scr, st, out); }
+
+bool tq_matvec_uses_tmv() {
+    const int k = g_matvec_kernel.load();
+    return k == 0 || k == 5;
+}
 
 cudaError_t tq_launch_matmul(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                              cudaStream_t st) {
@@ -239,6 +251,13 @@ static int check_dims(int bits, int rows, int cols) {
     return TQ_OK;
 }
 
+static void release_matrix(TqMatrixDev *m) {
+    for (void *p : {(void *)m->codes, (void *)m->scale, (void *)m->kcodes, (void *)m->kscale})
+        if (p) cudaFree(p);
+    m->codes = m->kcodes = nullptr;
+    m->scale = m->kscale = nullptr;
+}
+
 // Allocates a device matrix on the calling thread's device and clears it on
 // stream st (ordered before whatever the caller enqueues next on st).
 static int alloc_matrix(int bits, int rows, int cols, TqMatrixDev *m, cudaStream_t st) {
@@ -250,28 +269,23 @@ static int alloc_matrix(int bits, int rows, int cols, TqMatrixDev *m, cudaStream
     m->units = tq_units(rows);
     const size_t cbytes = tq_code_bytes(bits, rows, cols);
     const size_t sfloats = tq_scale_floats(bits, rows, cols);
-    cudaError_t e = tq_dev_malloc((void **)&m->codes, cbytes);
-    if (e != cudaSuccess) return tq_cuda_fail(e, "code allocation");
-    e = tq_dev_malloc((void **)&m->scale, sfloats * sizeof(float));
-    if (e != cudaSuccess) {
-        cudaFree(m->codes);
-        m->codes = nullptr;
-        return tq_cuda_fail(e, "scale allocation");
+    // int4 matrices also hold a K-packed copy of codes and scales for the
+    // tensor-core matvec (filled by the quantize / upload launchers)
+    const int copies = bits == 4 ? 2 : 1;
+    uint8_t **cp[2] = {&m->codes, &m->kcodes};
+    float **sp[2] = {&m->scale, &m->kscale};
+    cudaError_t e = cudaSuccess;
+    for (int c = 0; c < copies && e == cudaSuccess; c++) {
+        e = tq_dev_malloc((void **)cp[c], cbytes);
+        if (e == cudaSuccess) e = tq_dev_malloc((void **)sp[c], sfloats * sizeof(float));
+        if (e == cudaSuccess) e = cudaMemsetAsync(*cp[c], 0, cbytes, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(*sp[c], 0, sfloats * sizeof(float), st);
     }
-    if ((e = cudaMemsetAsync(m->codes, 0, cbytes, st)) != cudaSuccess ||
-        (e = cudaMemsetAsync(m->scale, 0, sfloats * sizeof(float), st)) != cudaSuccess) {
-        cudaFree(m->codes);
-        cudaFree(m->scale);
-        return tq_cuda_fail(e, "matrix clear");
+    if (e != cudaSuccess) {
+        release_matrix(m);
+        return tq_cuda_fail(e, "matrix allocation");
     }
     return TQ_OK;
-}
-
-static void release_matrix(TqMatrixDev *m) {
-    if (m->codes) cudaFree(m->codes);
-    if (m->scale) cudaFree(m->scale);
-    m->codes = nullptr;
-    m->scale = nullptr;
 }
 
 int tq_alloc_matrix(int bits, int rows, int cols, TqMatrixDev *m, cudaStream_t st) {
@@ -597,7 +611,7 @@ int tq_device_status(unsigned *bits) {
 }
 
 int tq_set_matvec_kernel(int which) {
-    if (which < 0 || which > 4) return tq_fail(TQ_ERR_ARG, "tensai: matvec kernel must be 0..4, got %d", which);
+    if (which < 0 || which > 5) return tq_fail(TQ_ERR_ARG, "tensai: matvec kernel must be 0..5, got %d", which);
     g_matvec_kernel.store(which);
     return TQ_OK;
 }

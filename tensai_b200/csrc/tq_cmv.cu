@@ -60,27 +60,36 @@ constexpr int kThreads = (W + 2) * 32;
 // the stream (programmatic dependent launch) is resident while this one
 // computes and reduces, and fills its ring meanwhile.
 constexpr int kSmemCap = 113 * 1024; // 2 x (113 + 1 reserved) KB <= 228 KB per SM
+// The tensor-core variant needs a quarter of the CUDA-core variant's issue
+// slots per code, so it runs one CTA per SM instead, with a ring deep enough to
+// have its whole stream-K slice in flight at once.
+constexpr int kSmemCapTc = 226 * 1024;
 
-template <int BITS, int M> struct CCfg {
+template <int BITS, int M, bool TC = false> struct CCfg {
     static constexpr int NP = BITS == 8 ? 4 : 8;       // columns per lane
     static constexpr int E = M * NP * 32;              // sums of one tile segment
     static constexpr int SLOT = BITS == 4 ? kItem + 1024 : kItem; // codes (+ int4 scales)
-    static constexpr int XD = 4;                      // per-warp activation ring (half items)
-    static constexpr int XSLOT = XD * kHalf * M * 4;  // [XD][M][32] floats per warp
+    static constexpr int XD = 4;                      // per-warp activation ring (half items; TC: whole items)
+    static constexpr int XROWS = TC ? kRows : kHalf;
+    static constexpr int XSLOT = XD * XROWS * M * 4;  // [XD][M][XROWS] floats per warp
+    static constexpr int PLANES = TC ? 3 * kRows : 0;  // TC: per-warp activation digit planes [3][64] bytes
     static constexpr int RED = 2 * W * E * 4;          // two deposit buffers
     static constexpr int HAND = E * 4;
-    static constexpr int FIXED = W * XSLOT + RED + HAND + 1024;
-    static constexpr int R0 = (kSmemCap - FIXED) / SLOT;
-    static constexpr int R = R0 < 16 ? R0 : 16;       // ring slots
+    static constexpr int FIXED = W * XSLOT + W * PLANES + RED + HAND + 1024;
+    static constexpr int CAP = TC ? kSmemCapTc : kSmemCap;
+    static constexpr int RMAX = TC ? 24 : 16;
+    static constexpr int R0 = (CAP - FIXED) / SLOT;
+    static constexpr int R = R0 < RMAX ? R0 : RMAX;   // ring slots
     static constexpr int RING_OFF = 0;
     static constexpr int X_OFF = R * SLOT;
-    static constexpr int RED_OFF = X_OFF + W * XSLOT;
+    static constexpr int PL_OFF = X_OFF + W * XSLOT;
+    static constexpr int RED_OFF = PL_OFF + W * PLANES;
     static constexpr int HAND_OFF = RED_OFF + RED;
     static constexpr int BAR_OFF = HAND_OFF + HAND;
     static constexpr int MISC_OFF = BAR_OFF + (2 * R + 1) * 8;
     static constexpr int SMEM = MISC_OFF + 64;
     static_assert(R >= 6, "ring too shallow");
-    static_assert(SMEM <= kSmemCap, "shared memory budget");
+    static_assert(SMEM <= CAP, "shared memory budget");
 };
 
 struct CmvParams {
@@ -329,9 +338,128 @@ __device__ __forceinline__ void half_item(const uint8_t *item, int hf, const flo
     }
 }
 
-template <int BITS, int M>
-__global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
-    using C = CCfg<BITS, M>;
+// ---------------------------------------------------------------------------
+// Tensor-core variant (int4, one activation row): the same schedule, with each
+// item's codes multiplied on the tensor cores by mma.sync m16n8k32 (u8 codes x
+// s8 activation digits, exact s32 sums), which issues about four times more
+// codes per SM cycle than the CUDA-core unpack above.
+//
+// Activations: per 64-row group, X = round(x * 2^s) with |X| <= 2^22 (s from
+// the group's largest |x|), cut into three signed byte digits, X = d0 + 256 d1
+// + 65536 d2 (bytes of X + 0x808080, each xor 0x80). The digits are the MMA's
+// B columns n = 0, 1, 2 (n = 3..7 zero).
+// Codes: a second, K-packed copy of the matrix (tq_launch_repack4): in item
+// (tile, unit), warp half hf (item columns 128hf..), MMA block cb (0..7) and
+// lane (g, t) = (lane / 4, lane % 4) hold 16 bytes: the words of MMA rows g and
+// g + 8 for rows 8t..8t+7 and 32+8t..32+8t+7 of the group. Word (j, k) packs
+// rows 8k..8k+7 of item column j, byte r = code(8k + 2r) | code(8k + 2r + 1) << 4,
+// so w & 0x0F0F0F0F (even rows) and (w >> 4) & 0x0F0F0F0F (odd rows) are A
+// fragments as they stand. MMA row rho of block cb is item column
+//   128 hf + 4 (4 (rho % 8) + cb % 4) + 2 (cb / 4) + rho / 8,
+// which puts every sum in the lane that owns it in the CUDA-core layout
+// (lane l: item columns 4l + e, 128 + 4l + e), so deposits and reductions are
+// shared. Scales: per item, [hf][cb % 4][g][2 (cb / 4) + rho / 8].
+// Per group and block the D fragment holds, in lane t = 0, sum n*d0 and sum
+// n*d1 (n the unsigned code) and in lane t = 1 sum n*d2; each lane adds
+//   scale * ((D_a + 256 D_b) * K_t + O_t),  K_0 = 2^-s, K_1 = 2^(16-s),
+//   O_1 = -8 * sum(X) * 2^-s (the code offset 8), K and O zero for t >= 2,
+// and the four lanes of a quad are added when a tile segment is deposited.
+// The integer sums are exact; |X| <= 2^22 keeps 22 bits of every group.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 64-row item, item columns of half hf, into this lane's partial sums
+// accp[cb][rh] (MMA rows g + 8 rh of block cb). xr: the group's 64
+// activations; pl: this warp's 192 bytes of digit planes.
+__device__ __forceinline__ void tmv_item(const uint8_t *item, int hf, const float *xr, uint8_t *pl, int lane,
+                                         float (&accp)[8][2]) {
+    const int g = lane >> 2, t = lane & 3;
+    const float2 xv = *reinterpret_cast<const float2 *>(xr + 2 * lane); // rows 2l, 2l + 1
+    const uint32_t ax = max(__float_as_uint(xv.x) & 0x7FFFFFFFu, __float_as_uint(xv.y) & 0x7FFFFFFFu);
+    uint32_t amax;
+    asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(amax) : "r"(ax));
+    // |x| < 2^(e - 126) for the largest biased exponent e: 2^s with s = 148 - e
+    // keeps |X| <= 2^22 (s at most 126 so that 2^-s is a normal float)
+    int sh = 148 - (int)(amax >> 23);
+    sh = sh > 126 ? 126 : sh;
+    const float up = __uint_as_float((uint32_t)(127 + sh) << 23), dn = __uint_as_float((uint32_t)(127 - sh) << 23);
+    const int X0 = __float2int_rn(xv.x * up), X1 = __float2int_rn(xv.y * up);
+    int sx;
+    asm volatile("redux.sync.add.s32 %0, %1, 0xffffffff;" : "=r"(sx) : "r"(X0 + X1));
+    const uint32_t dg0 = (uint32_t)(X0 + 0x808080) ^ 0x808080u, dg1 = (uint32_t)(X1 + 0x808080) ^ 0x808080u;
+    uint16_t *pl16 = reinterpret_cast<uint16_t *>(pl);
+    pl16[lane] = (uint16_t)__byte_perm(dg0, dg1, 0x0040); // plane p, bytes 2l, 2l + 1
+    pl16[32 + lane] = (uint16_t)__byte_perm(dg0, dg1, 0x0051);
+    pl16[64 + lane] = (uint16_t)__byte_perm(dg0, dg1, 0x0062);
+    __syncwarp();
+    uint32_t be0 = 0, bo0 = 0, be1 = 0, bo1 = 0; // B: digit g at even / odd rows of the two 32-row halves
+    if (g < 3) {
+        const uint2 q0 = *reinterpret_cast<const uint2 *>(pl + g * 64 + 8 * t);
+        const uint2 q1 = *reinterpret_cast<const uint2 *>(pl + g * 64 + 32 + 8 * t);
+        be0 = __byte_perm(q0.x, q0.y, 0x6420);
+        bo0 = __byte_perm(q0.x, q0.y, 0x7531);
+        be1 = __byte_perm(q1.x, q1.y, 0x6420);
+        bo1 = __byte_perm(q1.x, q1.y, 0x7531);
+    }
+    __syncwarp(); // the planes are read before the next item writes them
+    const float K = t == 0 ? dn : t == 1 ? dn * 65536.f : 0.f;
+    const float O = t == 1 ? -8.f * (float)sx * dn : 0.f;
+    const uint8_t *cw = item + hf * (kItem / 2) + lane * 16;
+    const float *scl = reinterpret_cast<const float *>(item + kItem) + hf * 128 + g * 4;
+    float4 sc[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) sc[u] = *reinterpret_cast<const float4 *>(scl + u * 32);
+    constexpr uint32_t LO = 0x0F0F0F0Fu;
+#pragma unroll
+    for (int cb = 0; cb < 8; cb++) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(cw + cb * 512);
+        int d[4] = {0, 0, 0, 0};
+        mma_u8s8(d, w.x & LO, w.y & LO, (w.x >> 4) & LO, (w.y >> 4) & LO, be0, bo0);
+        mma_u8s8(d, w.z & LO, w.w & LO, (w.z >> 4) & LO, (w.w >> 4) & LO, be1, bo1);
+        const float vg = fmaf((float)(d[0] + (d[1] << 8)), K, O);
+        const float vg8 = fmaf((float)(d[2] + (d[3] << 8)), K, O);
+        const float4 s4 = sc[cb & 3];
+        accp[cb][0] = fmaf(vg, cb < 4 ? s4.x : s4.z, accp[cb][0]);
+        accp[cb][1] = fmaf(vg8, cb < 4 ? s4.y : s4.w, accp[cb][1]);
+    }
+}
+
+// The lane's partial sums accp (all lanes of a quad hold parts of the same
+// columns) into its sums acc in the CUDA-core layout: quad-added, blocks t and
+// t + 4 kept (item columns 4l + 2k + rh of half hf), the other half zero.
+// accp is zeroed.
+__device__ __forceinline__ void tmv_flush(float (&accp)[8][2], float (&acc)[1][8], int lane, int hf) {
+    const int t = lane & 3;
+    float tot[8][2];
+#pragma unroll
+    for (int cb = 0; cb < 8; cb++)
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) {
+            float v = accp[cb][rh];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            tot[cb][rh] = v;
+            accp[cb][rh] = 0.f;
+        }
+#pragma unroll
+    for (int k = 0; k < 2; k++)
+#pragma unroll
+        for (int rh = 0; rh < 2; rh++) {
+            const float v = t == 0 ? tot[4 * k][rh] : t == 1 ? tot[4 * k + 1][rh] : t == 2 ? tot[4 * k + 2][rh] : tot[4 * k + 3][rh];
+            acc[0][2 * k + rh] = hf ? 0.f : v;
+            acc[0][4 + 2 * k + rh] = hf ? v : 0.f;
+        }
+}
+
+template <int BITS, int M, bool TC = false>
+__global__ void __launch_bounds__(kThreads, TC ? 1 : 2) cmv_kernel(CmvParams p) {
+    using C = CCfg<BITS, M, TC>;
+    static_assert(!TC || (BITS == 4 && M == 1), "the tensor-core variant is int4, one row");
     constexpr int R = C::R, NP = C::NP, E = C::E;
     // 16-byte alignment is all the bulk copies and vector loads need; indexing
     // the array directly keeps every access in the shared state space.
@@ -427,12 +555,19 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
         const float *xrow = p.x + hf * kHalf + lane; // + unit * 64 + m * rows
         auto issue_x = [&]() { // one cp.async group per call (empty past this warp's last item)
             if (tx < nmine) {
-                float *dst = xs + (tx & (C::XD - 1)) * M * kHalf + lane;
-                const int row = unit_x * kRows + hf * kHalf + lane;
-                const bool v = row < p.rows;
-                const float *src = xrow + (v ? unit_x * kRows : -(hf * kHalf + lane));
+                if constexpr (TC) { // all 64 rows: lane l copies rows l and 32 + l
+                    float *dst = xs + (tx & (C::XD - 1)) * kRows + lane;
+                    const int r0 = unit_x * kRows + lane, r1 = r0 + kHalf;
+                    cp_async_f32(dst, p.x + (r0 < p.rows ? r0 : 0), r0 < p.rows);
+                    cp_async_f32(dst + kHalf, p.x + (r1 < p.rows ? r1 : 0), r1 < p.rows);
+                } else {
+                    float *dst = xs + (tx & (C::XD - 1)) * M * kHalf + lane;
+                    const int row = unit_x * kRows + hf * kHalf + lane;
+                    const bool v = row < p.rows;
+                    const float *src = xrow + (v ? unit_x * kRows : -(hf * kHalf + lane));
 #pragma unroll
-                for (int m = 0; m < M; m++) cp_async_f32(dst + m * kHalf, src + (size_t)m * p.rows, v);
+                    for (int m = 0; m < M; m++) cp_async_f32(dst + m * kHalf, src + (size_t)m * p.rows, v);
+                }
                 unit_x += WI; // next item of this warp: WI units on, modulo the units of a tile
                 while (unit_x >= p.units) unit_x -= p.units;
             }
@@ -452,6 +587,14 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
         for (int m = 0; m < M; m++)
 #pragma unroll
             for (int j = 0; j < NP; j++) acc[m][j] = 0.f;
+        // TC: the lane's partial sums per MMA block and row half, moved into
+        // acc (quad-added, the lane's own columns) before each deposit
+        float accp[TC ? 8 : 1][2];
+#pragma unroll
+        for (int cb = 0; cb < (TC ? 8 : 1); cb++) accp[cb][0] = accp[cb][1] = 0.f;
+        auto flush = [&]() {
+            if constexpr (TC) tmv_flush(accp, acc, lane, hf);
+        };
 
         // Deposits this warp's sums of segment s; the last warp to deposit
         // reduces the segment and hands it on.
@@ -533,6 +676,7 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
         int slot = js % R, ph = (js / R) & 1; // ring slot and full-barrier parity of item j
         for (int j = js, t_it = 0; j < nitems; j += WI, t_it++) {
             while (j >= next_sb) {
+                flush();
                 deposit(s);
 #pragma unroll
                 for (int m = 0; m < M; m++)
@@ -555,8 +699,13 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
             const bool ok = wait_bar(&full[slot], ph, abort, p.status);
             __syncwarp(); // every lane's activation copies visible to the whole warp
             const uint8_t *item = ring + slot * C::SLOT;
-            const float *xr = xs + (t_it & (C::XD - 1)) * M * kHalf;
-            if (ok) half_item<BITS, M>(item, hf, xr, ofs, mg, lane, acc);
+            if constexpr (TC) {
+                const float *xr = xs + (t_it & (C::XD - 1)) * kRows;
+                if (ok) tmv_item(item, hf, xr, smem + C::PL_OFF + cw * C::PLANES, lane, accp);
+            } else {
+                const float *xr = xs + (t_it & (C::XD - 1)) * M * kHalf;
+                if (ok) half_item<BITS, M>(item, hf, xr, ofs, mg, lane, acc);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             __syncwarp(); // the x slot is reused XD - 1 items later
@@ -567,6 +716,7 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
             }
         }
         // segments before the last one that this warp has not deposited yet
+        flush();
         for (; s < nseg - 1; s++) {
             deposit(s);
 #pragma unroll
@@ -695,26 +845,30 @@ __global__ void __launch_bounds__(kThreads, 2) cmv_kernel(CmvParams p) {
 // reads are done. No global scratch and no atomics: the reduction costs two
 // cluster barriers instead of global round trips.
 // ---------------------------------------------------------------------------
-template <int BITS, int M> struct KCfg {
+template <int BITS, int M, bool TC = false> struct KCfg {
     static constexpr int NP = BITS == 8 ? 4 : 8;
     static constexpr int E = M * NP * 32;
     static constexpr int SLOT = BITS == 4 ? kItem + 1024 : kItem;
     static constexpr int XD = 4;
-    static constexpr int XSLOT = XD * kHalf * M * 4;
+    static constexpr int XSLOT = XD * (TC ? kRows : kHalf) * M * 4;
+    static constexpr int PLANES = TC ? 3 * kRows : 0;
     static constexpr int RED = W * E * 4;  // per-warp sums
     static constexpr int CPART = E * 4;    // this CTA's sums, read across the cluster
-    static constexpr int FIXED = W * XSLOT + RED + CPART + 1024;
-    static constexpr int R0 = (kSmemCap - FIXED) / SLOT;
-    static constexpr int R = R0 < 16 ? R0 : 16; // ring slots
+    static constexpr int FIXED = W * XSLOT + W * PLANES + RED + CPART + 1024;
+    static constexpr int CAP = TC ? kSmemCapTc : kSmemCap;
+    static constexpr int RMAX = TC ? 24 : 16;
+    static constexpr int R0 = (CAP - FIXED) / SLOT;
+    static constexpr int R = R0 < RMAX ? R0 : RMAX; // ring slots
     static constexpr int RING_OFF = 0;
     static constexpr int X_OFF = R * SLOT;
-    static constexpr int RED_OFF = X_OFF + W * XSLOT;
+    static constexpr int PL_OFF = X_OFF + W * XSLOT;
+    static constexpr int RED_OFF = PL_OFF + W * PLANES;
     static constexpr int CPART_OFF = RED_OFF + RED;
     static constexpr int BAR_OFF = CPART_OFF + CPART;
     static constexpr int MISC_OFF = BAR_OFF + 2 * R * 8;
     static constexpr int SMEM = MISC_OFF + 32;
     static_assert(R >= 6, "ring too shallow");
-    static_assert(SMEM <= kSmemCap, "shared memory budget");
+    static_assert(SMEM <= CAP, "shared memory budget");
 };
 constexpr int kKThreads = (W + 1) * 32; // producer warp + consumer warps
 constexpr int kMaxCluster = 8;
@@ -731,9 +885,10 @@ __device__ __forceinline__ float ld_cluster(const float *p, uint32_t rank) {
     return v;
 }
 
-template <int BITS, int M>
-__global__ void __launch_bounds__(kKThreads, 2) kcmv_kernel(CmvParams p) {
-    using C = KCfg<BITS, M>;
+template <int BITS, int M, bool TC = false>
+__global__ void __launch_bounds__(kKThreads, TC ? 1 : 2) kcmv_kernel(CmvParams p) {
+    using C = KCfg<BITS, M, TC>;
+    static_assert(!TC || (BITS == 4 && M == 1), "the tensor-core variant is int4, one row");
     constexpr int R = C::R, NP = C::NP, E = C::E;
     extern __shared__ __align__(16) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
@@ -789,12 +944,19 @@ __global__ void __launch_bounds__(kKThreads, 2) kcmv_kernel(CmvParams p) {
         const float *xrow = p.x + hf * kHalf + lane;
         auto issue_x = [&]() {
             if (tx < nmine) {
-                float *dst = xs + (tx & (C::XD - 1)) * M * kHalf + lane;
-                const int row = unit_x * kRows + hf * kHalf + lane;
-                const bool v = row < p.rows;
-                const float *src = xrow + (v ? unit_x * kRows : -(hf * kHalf + lane));
+                if constexpr (TC) { // all 64 rows: lane l copies rows l and 32 + l
+                    float *dst = xs + (tx & (C::XD - 1)) * kRows + lane;
+                    const int r0 = unit_x * kRows + lane, r1 = r0 + kHalf;
+                    cp_async_f32(dst, p.x + (r0 < p.rows ? r0 : 0), r0 < p.rows);
+                    cp_async_f32(dst + kHalf, p.x + (r1 < p.rows ? r1 : 0), r1 < p.rows);
+                } else {
+                    float *dst = xs + (tx & (C::XD - 1)) * M * kHalf + lane;
+                    const int row = unit_x * kRows + hf * kHalf + lane;
+                    const bool v = row < p.rows;
+                    const float *src = xrow + (v ? unit_x * kRows : -(hf * kHalf + lane));
 #pragma unroll
-                for (int m = 0; m < M; m++) cp_async_f32(dst + m * kHalf, src + (size_t)m * p.rows, v);
+                    for (int m = 0; m < M; m++) cp_async_f32(dst + m * kHalf, src + (size_t)m * p.rows, v);
+                }
                 unit_x += WI;
             }
             cp_async_commit();
@@ -809,6 +971,9 @@ __global__ void __launch_bounds__(kKThreads, 2) kcmv_kernel(CmvParams p) {
         for (int m = 0; m < M; m++)
 #pragma unroll
             for (int q = 0; q < NP; q++) acc[m][q] = 0.f;
+        float accp[TC ? 8 : 1][2]; // TC: partial sums per MMA block and row half (see tmv_flush)
+#pragma unroll
+        for (int cb = 0; cb < (TC ? 8 : 1); cb++) accp[cb][0] = accp[cb][1] = 0.f;
         const uint8_t *ring = smem + C::RING_OFF;
         int slot = js % R, ph = (js / R) & 1;
         for (int j = js, t_it = 0; j < nitems; j += WI, t_it++) {
@@ -826,7 +991,11 @@ __global__ void __launch_bounds__(kKThreads, 2) kcmv_kernel(CmvParams p) {
             const bool ok = wait_bar(&full[slot], ph, abort, p.status);
             __syncwarp();
             const uint8_t *item = ring + slot * C::SLOT;
-            if (ok) half_item<BITS, M>(item, hf, xs + (t_it & (C::XD - 1)) * M * kHalf, ofs, mg, lane, acc);
+            if constexpr (TC) {
+                if (ok) tmv_item(item, hf, xs + (t_it & (C::XD - 1)) * kRows, smem + C::PL_OFF + cw * C::PLANES, lane, accp);
+            } else {
+                if (ok) half_item<BITS, M>(item, hf, xs + (t_it & (C::XD - 1)) * M * kHalf, ofs, mg, lane, acc);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             __syncwarp();
@@ -837,6 +1006,7 @@ __global__ void __launch_bounds__(kKThreads, 2) kcmv_kernel(CmvParams p) {
             }
         }
         cp_async_wait<0>();
+        if constexpr (TC) tmv_flush(accp, acc, lane, hf);
         float *rb = red + (size_t)cw * E + lane;
 #pragma unroll
         for (int m = 0; m < M; m++)
@@ -874,8 +1044,10 @@ __global__ void __launch_bounds__(kKThreads, 2) kcmv_kernel(CmvParams p) {
 
 template <int BITS, int M>
 cudaError_t launch_kcmv(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
-                        int k, int epi) {
+                        int k, int epi, bool tc = false) {
     using C = KCfg<BITS, M>;
+    constexpr bool kHasTc = BITS == 4 && M == 1;
+    using CT = KCfg<4, 1, true>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -884,11 +1056,15 @@ cudaError_t launch_kcmv(const TqMatrixDev &mat, const float *x, float *out, cons
     if (!configured[dev]) {
         e = cudaFuncSetAttribute(kcmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
+        if constexpr (kHasTc) {
+            e = cudaFuncSetAttribute(kcmv_kernel<4, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
+            if (e != cudaSuccess) return e;
+        }
         configured[dev] = 1;
     }
     CmvParams prm = {};
-    prm.codes = mat.codes;
-    prm.scale = mat.scale;
+    prm.codes = tc ? mat.kcodes : mat.codes;
+    prm.scale = tc ? mat.kscale : mat.scale;
     prm.x = x;
     prm.out = out;
     prm.status = scr.status;
@@ -914,6 +1090,12 @@ cudaError_t launch_kcmv(const TqMatrixDev &mat, const float *x, float *out, cons
     cfg.numAttrs = 2;
     cfg.gridDim = dim3(mat.tiles * k);
     cfg.blockDim = dim3(kKThreads);
+    if constexpr (kHasTc) {
+        if (tc) {
+            cfg.dynamicSmemBytes = CT::SMEM;
+            return cudaLaunchKernelEx(&cfg, kcmv_kernel<4, 1, true>, prm);
+        }
+    }
     cfg.dynamicSmemBytes = C::SMEM;
     return cudaLaunchKernelEx(&cfg, kcmv_kernel<BITS, M>, prm);
 }
@@ -935,10 +1117,25 @@ inline int cluster_split(const TqMatrixDev &mat, int sms) {
     return k < 1 ? 1 : k;
 }
 
+// Cluster size for the tensor-core variant: with fewer column tiles than SMs
+// and at most 12 items per SM, k = min(8, SMs / tiles, units) CTAs per tile;
+// 0 = stream-K. Measured on B200: the 4096 x 11008 / 11008 x 4096 pair (19
+// items per SM) took 11.7 us per call by clusters and 9.4 by stream-K.
+inline int cluster_split_tc(const TqMatrixDev &mat, int sms) {
+    if (mat.tiles >= sms || (long long)mat.tiles * mat.units > 12LL * sms) return 0;
+    int k = sms / mat.tiles;
+    if (k > kMaxCluster) k = kMaxCluster;
+    if (k > mat.units) k = mat.units;
+    return k < 1 ? 1 : k;
+}
+
 template <int BITS, int M>
 cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
-                       int epi) {
+                       int epi, bool tc = false) {
     using C = CCfg<BITS, M>;
+    constexpr bool kHasTc = BITS == 4 && M == 1;
+    using CT = CCfg<4, 1, true>;
+    tc = tc && kHasTc && mat.kcodes && mat.kscale;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -948,13 +1145,17 @@ cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const
     if (!configured[dev]) {
         e = cudaFuncSetAttribute(cmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
+        if constexpr (kHasTc) {
+            e = cudaFuncSetAttribute(cmv_kernel<4, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
+            if (e != cudaSuccess) return e;
+        }
         e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
         configured[dev] = 1;
     }
     CmvParams prm = {};
-    prm.codes = mat.codes;
-    prm.scale = mat.scale;
+    prm.codes = tc ? mat.kcodes : mat.codes;
+    prm.scale = tc ? mat.kscale : mat.scale;
     prm.x = x;
     prm.out = out;
     prm.partial = scr.partial;
@@ -970,7 +1171,8 @@ cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const
     prm.epi = epi;
     const int sms = sm_count[dev];
     if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS) return cudaErrorInvalidValue;
-    if (const int k = cluster_split(mat, sms)) return launch_kcmv<BITS, M>(mat, x, out, scr, st, k, epi);
+    if (const int k = tc ? cluster_split_tc(mat, sms) : cluster_split(mat, sms))
+        return launch_kcmv<BITS, M>(mat, x, out, scr, st, k, epi, tc);
     if ((size_t)2 * sms * C::E > TQ_SCRATCH_PARTIAL_FLOATS) return cudaErrorInvalidValue;
     const int ctas = (int)(prm.items < sms ? prm.items : sms);
     cudaLaunchAttribute attr[1];
@@ -982,11 +1184,74 @@ cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const
     cfg.numAttrs = 1;
     cfg.gridDim = dim3(ctas);
     cfg.blockDim = dim3(kThreads);
+    if constexpr (kHasTc) {
+        if (tc) {
+            cfg.dynamicSmemBytes = CT::SMEM;
+            return cudaLaunchKernelEx(&cfg, cmv_kernel<4, 1, true>, prm);
+        }
+    }
     cfg.dynamicSmemBytes = C::SMEM;
     return cudaLaunchKernelEx(&cfg, cmv_kernel<BITS, M>, prm);
 }
 
+// Item column of MMA row rho of block cb in warp half hf (tensor-core variant).
+TQ_HD int tmv_col(int hf, int cb, int rho) { return 128 * hf + 4 * (4 * (rho & 7) + (cb & 3)) + 2 * (cb >> 2) + (rho >> 3); }
+
+// The K-packed copy of an int4 matrix (see the tensor-core variant above):
+// one thread per 4-byte word of kcodes (8 codes of one item column), then one
+// per kscale float.
+__global__ void repack4_kernel(const uint8_t *__restrict__ codes, const float *__restrict__ scale,
+                               uint8_t *__restrict__ kcodes, float *__restrict__ kscale, long long items) {
+    const long long words = items * (kItem / 4), stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < words; i += stride) {
+        const long long it = i / (kItem / 4);
+        const int wi = (int)(i % (kItem / 4));
+        const int q = wi & 3, lane = (wi >> 2) & 31, cb = (wi >> 7) & 7, hf = wi >> 10;
+        const int rho = (lane >> 2) + 8 * (q & 1), kb = (lane & 3) + 4 * (q >> 1);
+        const int j = tmv_col(hf, cb, rho), b = j & 127, hi = j >> 7;
+        const uint8_t *src = codes + it * kItem;
+        uint32_t w = 0;
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+            const uint32_t byte = src[tq_item_offset(8 * kb + r, b)];
+            w |= (hi ? byte >> 4 : byte & 15u) << (4 * r);
+        }
+        reinterpret_cast<uint32_t *>(kcodes + it * kItem)[wi] = w;
+    }
+    const long long nsc = items * 256;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nsc; i += stride) {
+        const long long it = i / 256;
+        const int ks = (int)(i % 256);
+        const int hf = ks >> 7, tq = (ks >> 5) & 3, g = (ks >> 2) & 7, e = ks & 3;
+        kscale[i] = scale[it * 256 + tmv_col(hf, tq + 4 * (e >> 1), g + 8 * (e & 1))];
+    }
+}
+
 } // namespace
+
+cudaError_t tq_launch_repack4(const TqMatrixDev &m, cudaStream_t st) {
+    if (m.bits != 4 || !m.kcodes || !m.kscale) return cudaSuccess;
+    const long long items = (long long)m.tiles * m.units;
+    if (items == 0) return cudaSuccess;
+    const long long words = items * (kItem / 4);
+    const unsigned grid = (unsigned)(words / 256 < 148 * 8 ? (words + 255) / 256 : 148 * 8);
+    repack4_kernel<<<grid, 256, 0, st>>>(m.codes, m.scale, m.kcodes, m.kscale, items);
+    return cudaGetLastError();
+}
+
+// int4, one row per launch, on the tensor cores (the K-packed copy).
+cudaError_t tq_launch_tmv(const TqMatrixDev &mat, const float *x, float *out, int M, const TqScratch &scr,
+                          cudaStream_t st) {
+    if (mat.bits != 4 || !mat.kcodes) return tq_launch_cmv(mat, x, out, M, scr, st);
+    if (M <= 0 || mat.cols == 0) return cudaSuccess;
+    if (mat.rows == 0) return cudaMemsetAsync(out, 0, sizeof(float) * (size_t)M * mat.cols, st);
+    for (int m0 = 0; m0 < M; m0++) {
+        const cudaError_t e = launch_cmv<4, 1>(mat, x + (size_t)m0 * mat.rows, out + (size_t)m0 * mat.cols, scr, st,
+                                               TQ_EPI_NONE, true);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
 
 // CUDA-core matvec for M <= 2 rows per launch (more rows: consecutive 2-row launches).
 cudaError_t tq_launch_cmv(const TqMatrixDev &mat, const float *x, float *out, int M, const TqScratch &scr,
@@ -1009,8 +1274,8 @@ cudaError_t tq_launch_cmv(const TqMatrixDev &mat, const float *x, float *out, in
 
 // One activation row with an epilogue (TQ_EPI_*): the decode steps' matvecs.
 cudaError_t tq_launch_cmv_epi(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
-                              int epi) {
-    if (epi == TQ_EPI_NONE) return tq_launch_cmv(mat, x, out, 1, scr, st);
+                              int epi, bool tc) {
+    if (epi == TQ_EPI_NONE) return tc ? tq_launch_tmv(mat, x, out, 1, scr, st) : tq_launch_cmv(mat, x, out, 1, scr, st);
     if (epi != TQ_EPI_SWIGLU || mat.bits != 4 || mat.cols % 2 || mat.rows == 0) return cudaErrorInvalidValue;
-    return launch_cmv<4, 1>(mat, x, out, scr, st, epi);
+    return launch_cmv<4, 1>(mat, x, out, scr, st, epi, tc);
 }

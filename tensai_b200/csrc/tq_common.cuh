@@ -58,6 +58,8 @@ struct TqMatrixDev {
     int units;      // ceil(rows/64) (= scale groups for int4)
     uint8_t *codes; // tiles*units*8192 bytes, tiled (see above)
     float *scale;   // see above
+    uint8_t *kcodes; // int4: the same codes K-packed for the tensor-core matvec (tq_cmv.cu), or null
+    float *kscale;   // int4: the scales in that matvec's per-item order, or null
 };
 
 #ifdef __CUDACC__
@@ -148,7 +150,14 @@ cudaError_t tq_launch_matvec(const TqMatrixDev &m, const float *x, float *out, i
 #define TQ_EPI_NONE 0
 #define TQ_EPI_SWIGLU 1
 cudaError_t tq_launch_cmv_epi(const TqMatrixDev &m, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
-                              int epi);
+                              int epi, bool tc);
+// int4 matvec on the tensor cores (mma.sync over the K-packed copy), one row
+// per launch; matrices without the copy go to tq_launch_cmv.
+cudaError_t tq_launch_tmv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
+                          cudaStream_t st);
+// Fills kcodes / kscale of an int4 matrix from its codes and scales (no-op
+// without them); the quantize and upload launchers end with it.
+cudaError_t tq_launch_repack4(const TqMatrixDev &m, cudaStream_t st);
 cudaError_t tq_launch_igemv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                             cudaStream_t st);
 // Single-launch tensor-core matvec for M <= 8 rows per launch (tq_gemv.cu).

@@ -29,6 +29,8 @@ int tq_scratch_for(int device, cudaStream_t st, TqScratch *out, int m);
 // whose scratch tq_scratch_for created, after its work has finished.
 void tq_scratch_release(int device, cudaStream_t st);
 // out[M][cols] = x @ W with the kernel the library would pick for M rows.
+// Whether the selected matvec kernel runs int4 rows on the tensor cores (tq_set_matvec_kernel).
+bool tq_matvec_uses_tmv();
 cudaError_t tq_launch_matmul(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                              cudaStream_t st);
 // A zeroed device matrix (shape checked) on the current device / its release.

@@ -140,6 +140,9 @@ cudaError_t tq_launch_quantize(const TqMatrixDev &m, const float *w, cudaStream_
         if (half == 0) return cudaSuccess;
         dim3 grid((half + 127) / 128, m.units);
         tq_quantize4_kernel<<<grid, 128, 0, st>>>(m, w);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        return tq_launch_repack4(m, st); // the tensor-core matvec's K-packed copy
     }
     return cudaGetLastError();
 }
@@ -188,7 +191,8 @@ static cudaError_t layout(const TqMatrixDev &m, uint8_t *ref_q, float *ref_scale
 }
 
 cudaError_t tq_launch_to_tiled(const TqMatrixDev &m, const uint8_t *ref_q, const float *ref_scale, cudaStream_t st) {
-    return layout(m, const_cast<uint8_t *>(ref_q), const_cast<float *>(ref_scale), true, st);
+    const cudaError_t e = layout(m, const_cast<uint8_t *>(ref_q), const_cast<float *>(ref_scale), true, st);
+    return e != cudaSuccess ? e : tq_launch_repack4(m, st);
 }
 
 cudaError_t tq_launch_from_tiled(const TqMatrixDev &m, uint8_t *ref_q, float *ref_scale, cudaStream_t st) {

@@ -399,7 +399,7 @@ cudaError_t step(Qwen &m, int n_prompt) {
         TRY(tq_launch_matmul(ly.o, m.att + m.arow, m.y, 1, m.scr, m.st));
         if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
         TRY(step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, m.y, m.ones, m.a, d, m.c.eps)); // x += o_proj, then norm
-        TRY(tq_launch_cmv_epi(ly.gu, m.a, m.h, m.scr, m.st, TQ_EPI_SWIGLU));
+        TRY(tq_launch_cmv_epi(ly.gu, m.a, m.h, m.scr, m.st, TQ_EPI_SWIGLU, tq_matvec_uses_tmv()));
         TRY(tq_launch_matmul(ly.down, m.h, m.y, 1, m.scr, m.st));
         if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
         pending = m.y;

@@ -41,8 +41,10 @@ def device():
 # 0: the default choice per row count, 1: CUDA-core matvec with per-warp
 # copies, 2: single-launch tensor-core matvec (digit planes made in the
 # kernel), 3: single-launch CUDA-core matvec (2 rows per launch), 4: tensor-core
-# matvec with a digit-plane launch.
-@pytest.fixture(params=[0, 1, 2, 3, 4], ids=["default", "cudacore", "tcgen05-1launch", "cudacore-1launch", "tcgen05"])
+# matvec with a digit-plane launch, 5: int4 rows on the tensor cores by
+# mma.sync over the K-packed copy (int8 as 3).
+@pytest.fixture(params=[0, 1, 2, 3, 4, 5],
+                ids=["default", "cudacore", "tcgen05-1launch", "cudacore-1launch", "tcgen05", "mma-int4"])
 def kernel(request):
     L = _lib.load()
     _lib.check(L.tq_set_matvec_kernel(request.param))
