@@ -415,14 +415,25 @@ __device__ __forceinline__ void tmv_item(const uint8_t *item, int hf, const floa
 #pragma unroll
     for (int u = 0; u < 4; u++) sc[u] = *reinterpret_cast<const float4 *>(scl + u * 32);
     constexpr uint32_t LO = 0x0F0F0F0Fu;
+    // In phases over the eight blocks (all loads, all first-half MMAs, all
+    // second-half MMAs, then the sums), so that eight independent chains
+    // hide the shared-memory and MMA latencies of each.
+    uint4 w[8];
+#pragma unroll
+    for (int cb = 0; cb < 8; cb++) w[cb] = *reinterpret_cast<const uint4 *>(cw + cb * 512);
+    int d[8][4];
 #pragma unroll
     for (int cb = 0; cb < 8; cb++) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(cw + cb * 512);
-        int d[4] = {0, 0, 0, 0};
-        mma_u8s8(d, w.x & LO, w.y & LO, (w.x >> 4) & LO, (w.y >> 4) & LO, be0, bo0);
-        mma_u8s8(d, w.z & LO, w.w & LO, (w.z >> 4) & LO, (w.w >> 4) & LO, be1, bo1);
-        const float vg = fmaf((float)(d[0] + (d[1] << 8)), K, O);
-        const float vg8 = fmaf((float)(d[2] + (d[3] << 8)), K, O);
+        d[cb][0] = d[cb][1] = d[cb][2] = d[cb][3] = 0;
+        mma_u8s8(d[cb], w[cb].x & LO, w[cb].y & LO, (w[cb].x >> 4) & LO, (w[cb].y >> 4) & LO, be0, bo0);
+    }
+#pragma unroll
+    for (int cb = 0; cb < 8; cb++)
+        mma_u8s8(d[cb], w[cb].z & LO, w[cb].w & LO, (w[cb].z >> 4) & LO, (w[cb].w >> 4) & LO, be1, bo1);
+#pragma unroll
+    for (int cb = 0; cb < 8; cb++) {
+        const float vg = fmaf((float)(d[cb][0] + (d[cb][1] << 8)), K, O);
+        const float vg8 = fmaf((float)(d[cb][2] + (d[cb][3] << 8)), K, O);
         const float4 s4 = sc[cb & 3];
         accp[cb][0] = fmaf(vg, cb < 4 ? s4.x : s4.z, accp[cb][0]);
         accp[cb][1] = fmaf(vg8, cb < 4 ? s4.y : s4.w, accp[cb][1]);
