@@ -408,7 +408,9 @@ __device__ __forceinline__ void tmv_item(const uint8_t *item, int hf, const floa
     }
     __syncwarp(); // the planes are read before the next item writes them
     const float K = t == 0 ? dn : t == 1 ? dn * 65536.f : 0.f;
-    const float O = t == 1 ? -8.f * (float)sx * dn : 0.f;
+    // a NaN or infinity in the group has no digits: its columns become NaN,
+    // as the float products would make them
+    const float O = amax >= 0x7F800000u ? __uint_as_float(0x7FC00000u) : t == 1 ? -8.f * (float)sx * dn : 0.f;
     const uint8_t *cw = item + hf * (kItem / 2) + lane * 16;
     const float *scl = reinterpret_cast<const float *>(item + kItem) + hf * 128 + g * 4;
     float4 sc[4];
