@@ -432,6 +432,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GvParams p) {
                         }
                         unit_scale = e >= -120 ? __uint_as_float((uint32_t)(e + 121) << 23) : ldexpf(1.0f, e - 6);
                     }
+                    if (amax >= 0x7F800000u) { // a NaN or infinity: no digits; the unit's sums become NaN
+                        r0 = r1 = 0.f;
+                        unit_scale = __uint_as_float(0x7FC00000u);
+                    }
                     // |r| < 64: four signed 7-bit digits, round to nearest even, remainder x128 (exact)
 #pragma unroll
                     for (int q = 0; q < 4; q++) {

@@ -238,6 +238,7 @@ __global__ void __launch_bounds__(64) planes_kernel(const float *__restrict__ x,
                                                    uint8_t *__restrict__ planes) {
     using PL = Planes<M>;
     __shared__ float red_max[2][M];
+    __shared__ int red_bad[2][M];
     __shared__ int red_sum[2][M][4];
     pdl_trigger();
     pdl_wait(); // x is produced by the previous kernel on the stream
@@ -252,13 +253,19 @@ __global__ void __launch_bounds__(64) planes_kernel(const float *__restrict__ x,
         float mx = fabsf(v[m]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) red_max[w][m] = mx;
+        // fmaxf skips NaN: a NaN or infinity is flagged on its own
+        const int bad = __any_sync(0xffffffffu, !(fabsf(v[m]) <= 3.402823466e38f));
+        if (lane == 0) {
+            red_max[w][m] = mx;
+            red_bad[w][m] = bad;
+        }
     }
     __syncthreads();
     const int kk = t & 31, j = t >> 5;
 #pragma unroll
     for (int m = 0; m < M; m++) {
-        const float mx = fmaxf(red_max[0][m], red_max[1][m]);
+        const bool bad = red_bad[0][m] | red_bad[1][m];
+        const float mx = bad ? 0.f : fmaxf(red_max[0][m], red_max[1][m]);
         int e = 0;
         if (mx > 0.f) frexpf(mx, &e); // mx = f * 2^e, f in [0.5, 1)
         float r = mx > 0.f ? ldexpf(v[m], 6 - e) : 0.f; // exact: |r| < 64
@@ -274,7 +281,8 @@ __global__ void __launch_bounds__(64) planes_kernel(const float *__restrict__ x,
             for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
             if (lane == 0) red_sum[w][m][q] = sum;
         }
-        if (t == 0) meta[m] = mx > 0.f ? ldexpf(1.0f, e - 6) : 0.f;
+        // a NaN or infinity in the unit: no digits, and its sums become NaN
+        if (t == 0) meta[m] = bad ? __uint_as_float(0x7FC00000u) : mx > 0.f ? ldexpf(1.0f, e - 6) : 0.f;
     }
     __syncthreads();
     if (t < 4 * M) {

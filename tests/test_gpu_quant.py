@@ -250,27 +250,24 @@ def test_results_are_bit_reproducible(kernel, bits, rows, cols):
     assert same_bits(outs[0], outs[1]) and same_bits(outs[0], outs[2])
 
 
+@pytest.mark.parametrize("m", [1, 4])
 @pytest.mark.parametrize("bits", [8, 4])
-@pytest.mark.parametrize("which", [0, 3, 5], ids=["default", "cudacore-1launch", "mma-int4"])
-def test_nan_activation_makes_every_output_nan(bits, which):
-    """A NaN activation reaches every output, as in the reference's float
-    products (NaN times any code, zero included, is NaN); the tensor-core
-    path, which turns activations into integer digits, must not hide it."""
-    L = _lib.load()
-    _lib.check(L.tq_set_matvec_kernel(which))
-    try:
-        rows, cols = 1000, 1030
-        w = O.synth((rows, cols), 5, 1, 0.02)
-        q, s = (O.quantize8 if bits == 8 else O.quantize4)(w)
-        qm = (QMatrix if bits == 8 else Q4Matrix)(rows, cols, q, s)
-        x = O.synth((rows,), 5, 2, 1.0)
-        x[123] = np.nan
-        out = np.zeros(cols, np.float32)
-        assert qm.MatVec(x, out) is None
-        assert np.isnan(out).all()
-        qm.Free()
-    finally:
-        _lib.check(L.tq_set_matvec_kernel(0))
+def test_nan_activation_makes_every_output_nan(bits, m, kernel):
+    """A NaN activation reaches every output of its row, as in the
+    reference's float products (NaN times any code, zero included, is NaN);
+    the kernels that turn activations into integer digits must not hide it.
+    The other rows stay finite."""
+    rows, cols = 1000, 1030
+    w = O.synth((rows, cols), 5, 1, 0.02)
+    q, s = (O.quantize8 if bits == 8 else O.quantize4)(w)
+    qm = (QMatrix if bits == 8 else Q4Matrix)(rows, cols, q, s)
+    x = O.synth((m, rows), 5, 2, 1.0)
+    x[0, 123] = np.nan
+    out = np.zeros((m, cols), np.float32)
+    assert qm.MatMul(x, out, m) is None
+    assert np.isnan(out[0]).all()
+    assert np.isfinite(out[1:]).all()
+    qm.Free()
 
 
 def test_device_pointer_path_on_a_torch_stream():
