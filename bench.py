@@ -2,21 +2,25 @@
 """Benchmark of the int4 / int8 weight-only dequant-matvec hot path on B200.
 
 Workload (one step): one decode token through LAYERS=32 resident int4 MLP
-pairs — for each layer, up [4096 x 11008] then down [11008 x 4096], group-64
-scales, M=1 activation row, fp32 accumulation. 32 distinct weight copies
-(1.63 GB) are streamed per step, so every matvec reads HBM, not L2 (126 MB).
-Each step is one CUDA-graph replay of the 64 launches.
+pairs, each layer's output feeding the next layer's input: up [4096 x 11008]
+then down [11008 x 4096], group-64 scales, M=1 activation row, fp32
+accumulation (x0 -> up_0 -> h -> down_0 -> x1 -> up_1 -> ...). 32 distinct
+weight copies (1.63 GB) are streamed per step, so every matvec reads HBM, not
+L2 (126 MB).
 
   value    algorithmic GB/s over the device-timed region (CUDA events, max over
-           ranks), bytes per matvec = codes + scales + x + out (each once)
+           ranks), bytes per matvec = codes + scales + x + out (each once). The
+           step is ONE launch of the chain kernel (tq_chain_run: the 64
+           dependent matvecs, weights streamed back to back).
   e2e      the same bytes through the C-ABI MatVec entry point (tq_matvec) with
-           host buffers: every call copies x host->device and out device->host
-  roofline the matvec's achieved GB/s: algorithmic bytes of one call over the
-           mean device time of a call inside the timed graph (CUDA events on
-           the launching stream around K replays of 64 calls; one call = one
-           launch of the CUDA-core matvec kernel, whose next call on the stream
-           streams its weights while this one finishes), against the measured
-           HBM copy bandwidth
+           host buffers, one call per matvec as the Go MatVec makes them: every
+           call copies x host->device and out device->host, and each call's
+           output is the next call's input
+  roofline the chain kernel's achieved GB/s: algorithmic bytes of one launch
+           over its mean device time (CUDA events on the launching stream),
+           against the measured HBM copy bandwidth
+  single_call  the same dependent workload as 64 single-call launches
+           (tq_matmul_dev, one CUDA graph per step), for comparison
   cpu_baseline  the CPU oracle (AVX2 restatement of quant4_simd.go with the
            reference's worker split) on the host cores, bounded sample
 
@@ -45,9 +49,8 @@ METRIC = "int8/int4 dequant-matvec HBM GB/s (% of peak); decode tokens/s at 1/2/
 K_UP, N_UP = 4096, 11008
 LAYERS = 32
 FALLBACK_HBM_GBS = 6650.0
-LAUNCHES_PER_CALL = 1  # cmv_kernel<4,1,true>: one launch per int4 M=1 matvec
 WORKLOAD = ("int4 g64 MLP pair (up 4096x11008 + down 11008x4096), M=1, fp32 accumulate; "
-            "32 resident layer copies streamed per step")
+            "32 resident layer copies streamed per step, each layer's output the next one's input")
 
 
 def algo_bytes(bits: int, rows: int, cols: int, m: int) -> int:
@@ -71,10 +74,11 @@ def load_peak():
 
 
 def load_traffic():
-    """Per-launch DRAM bytes (read + write) of the matvec kernel from the
-    committed ncu summary (its `traffic_bytes_per_launch:` line), or None."""
+    """Per-launch DRAM bytes (read + write) of the chain kernel from the
+    committed ncu summary of the same workload (its
+    `traffic_bytes_per_launch:` line), or None."""
     import re
-    path = os.path.join(ROOT, "profiles", "tmv_int4_m1_mlp_pair.md")
+    path = os.path.join(ROOT, "profiles", "chain_int4_m1_mlp_pair.md")
     try:
         with open(path) as f:
             m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", f.read())
@@ -208,44 +212,85 @@ def run_reference(args, rank: int, world: int):
 
 # Side measurements of the other kernel configs (device time per call, CUDA
 # graph of back-to-back calls over enough distinct weight copies to exceed L2).
+# A config is one matrix shape, or the MLP pair (up then down, the down call
+# reading the up call's output).
 SIDE_CONFIGS = [
-    # name, bits, rows, cols, m
-    ("C1 int8 4096x4096 M=1", 8, 4096, 4096, 1),
-    ("C2 int4 up 4096x11008 M=4", 4, 4096, 11008, 4),
-    ("C2 int4 up 4096x11008 M=8", 4, 4096, 11008, 8),
-    ("C3 int4 4096x4096 M=64 (tf32)", 4, 4096, 4096, 64),
+    # name, bits, [(rows, cols), ...], m
+    ("C1 int8 4096x4096 M=1", 8, [(4096, 4096)], 1),
+    ("C2 int4 MLP pair M=4", 4, [(K_UP, N_UP), (N_UP, K_UP)], 4),
+    ("C2 int4 MLP pair M=8", 4, [(K_UP, N_UP), (N_UP, K_UP)], 8),
+    ("C3 int4 4096x4096 M=64 (tf32)", 4, [(4096, 4096)], 64),
 ]
 
 
-def measure_side_configs(L, Q, torch, stream, peak, only=None):
+def side_cpu_baseline(bits, shapes, m, seconds=1.5):
+    """The oracle's AVX2 MatVec on all host threads over the config's shapes
+    (m rows = m MatVec calls, as quant.go:77 is applied per row)."""
+    from oracle import oracle as O
+    threads = O.set_threads(0)
+    mats = []
+    for i, (r, c) in enumerate(shapes):
+        w = O.synth((r, c), 7, 300 + i, 0.02)
+        mats.append(((O.quantize8 if bits == 8 else O.quantize4)(w), r, c))
+    xs = [O.synth((m, r), 7, 299, 1.0) for _, r, _ in mats]
+    fn = O.q8_matmul if bits == 8 else O.q4_matmul
+    per = sum(algo_bytes(bits, r, c, m) for _, r, c in mats)
+
+    def one():
+        for ((q, sc), r, c), x in zip(mats, xs):
+            fn(q, sc, r, c, x, O.AVX2)
+
+    one()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        one()
+        n += 1
+    dt = time.perf_counter() - t0
+    rec = {"value": round(per * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+           "sample": f"{n} passes over the config's matrices ({m} rows each), {dt:.2f} s, oracle AVX2 "
+                     f"restatement of quant_simd.go / quant4_simd.go with the reference worker split"}
+    if m >= 16:
+        flops = sum(2.0 * m * r * c for _, r, c in mats)
+        rec["TFLOP/s"] = round(flops * n / dt / 1e12, 4)
+    return rec
+
+
+def measure_side_configs(L, Q, torch, stream, peak, only=None, cpu=False):
     out = {}
     sp = ctypes.c_void_p(stream.cuda_stream)
-    for name, bits, rows, cols, m in SIDE_CONFIGS:
+    for name, bits, shapes, m in SIDE_CONFIGS:
         if only and not name.startswith(only + " "):
             continue
-        per = algo_bytes(bits, rows, cols, m)
-        copies = max(2, int(160e6 // (rows * cols // (1 if bits == 8 else 2))) + 1)  # > L2 in total
-        w = torch.empty(rows, cols, device="cuda")
+        per = sum(algo_bytes(bits, r, c, m) for r, c in shapes)
+        code_bytes = sum(r * c // (1 if bits == 8 else 2) for r, c in shapes)
+        copies = max(2, int(160e6 // code_bytes) + 1)  # > L2 in total
         hs = []
         for i in range(copies):
-            Q.synth_dev(w, 7, 100 + i, 0.02)
-            hs.append(Q.quantize_dev(w, bits))
-        del w
-        x = torch.empty(m, rows, device="cuda")
-        Q.synth_dev(x, 7, 99, 1.0)
-        o = torch.empty(m, cols, device="cuda")
-        xp, op = ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(o.data_ptr())
+            for j, (r, c) in enumerate(shapes):
+                w = torch.empty(r, c, device="cuda")
+                Q.synth_dev(w, 7, 100 + len(shapes) * i + j, 0.02)
+                hs.append(Q.quantize_dev(w, bits))
+                del w
+        bufs = [torch.empty(m, shapes[0][0], device="cuda")] + [torch.empty(m, c, device="cuda") for _, c in shapes]
+        Q.synth_dev(bufs[0], 7, 99, 1.0)
+        ptr = [ctypes.c_void_p(b.data_ptr()) for b in bufs]
         torch.cuda.synchronize()
+
+        def calls():
+            for i in range(copies):
+                for j in range(len(shapes)):
+                    L.tq_matmul_dev(hs[len(shapes) * i + j], ptr[j], ptr[j + 1], m, sp)
+
         with torch.cuda.stream(stream):
-            for h in hs:
-                _check_rc(L, L.tq_matmul_dev(h, xp, op, m, sp))
+            for i in range(copies):
+                for j in range(len(shapes)):
+                    _check_rc(L, L.tq_matmul_dev(hs[len(shapes) * i + j], ptr[j], ptr[j + 1], m, sp))
         torch.cuda.synchronize()
         reps = 4
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             for _ in range(reps):
-                for h in hs:
-                    L.tq_matmul_dev(h, xp, op, m, sp)
+                calls()
         for _ in range(3):
             g.replay()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -255,16 +300,18 @@ def measure_side_configs(L, Q, torch, stream, peak, only=None):
             g.replay()
             e1.record(stream)
         torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (reps * len(hs))
-        rec = {"us_per_call": round(us, 3), "GB/s": round(per / us / 1e3, 1),
+        us = e0.elapsed_time(e1) * 1e3 / (reps * copies)  # per pass over the config's shapes
+        rec = {"us_per_pass": round(us, 3), "GB/s": round(per / us / 1e3, 1),
                "frac_hbm": round(per / us / 1e3 / peak, 4), "algorithmic_bytes": per,
-               "weight_copies": len(hs)}
+               "weight_copies": copies, "calls_per_pass": len(shapes)}
         if m >= 16:
-            rec["TFLOP/s"] = round(2.0 * m * rows * cols / us / 1e6, 2)
-        out[name] = rec
+            rec["TFLOP/s"] = round(sum(2.0 * m * r * c for r, c in shapes) / us / 1e6, 2)
         del g
         for h in hs:
             Q.free(h)
+        if cpu:
+            rec["cpu_baseline"] = side_cpu_baseline(bits, shapes, m)
+        out[name] = rec
     return out
 
 
@@ -371,77 +418,91 @@ def run_gpu(args, rank: int, world: int):
             handles.append(Q.quantize_dev(w, 4))
     torch.cuda.synchronize()
     del tmp
-    x_up = torch.empty(1, K_UP, device="cuda")
-    x_dn = torch.empty(1, N_UP, device="cuda")
-    Q.synth_dev(x_up, 1, 1000, 1.0)
-    Q.synth_dev(x_dn, 1, 1001, 1.0)
-    o_up = torch.empty(1, N_UP, device="cuda")
-    o_dn = torch.empty(1, K_UP, device="cuda")
+    # x0 -> up_0 -> h -> down_0 -> xa -> up_1 -> h -> ... (the step's dataflow)
+    x0 = torch.empty(K_UP, device="cuda")
+    Q.synth_dev(x0, 1, 1000, 1.0)
+    h = torch.empty(N_UP, device="cuda")
+    xa = torch.empty(K_UP, device="cuda")
+    ops = []
+    for l in range(LAYERS):
+        ops.append({"handle": handles[2 * l], "x": x0 if l == 0 else xa, "out": h})
+        ops.append({"handle": handles[2 * l + 1], "x": h, "out": xa})
+    chain = Q.Chain(ops)
 
     stream = torch.cuda.Stream()
     sp = ctypes.c_void_p(stream.cuda_stream)
     mm = L.tq_matmul_dev
-    xu, xd, ou, od = (ctypes.c_void_p(t.data_ptr()) for t in (x_up, x_dn, o_up, o_dn))
 
-    def step(ev=None):
-        for l in range(LAYERS):
-            for j in range(2):
-                h = handles[2 * l + j]
-                if ev is not None:
-                    ev[2 * (2 * l + j)].record(stream)
-                rc = mm(h, xu if j == 0 else xd, ou if j == 0 else od, 1, sp)
-                if ev is not None:
-                    ev[2 * (2 * l + j) + 1].record(stream)
-                if rc:
-                    _lib.check(rc)
+    def chain_step():
+        chain.run(stream)
 
-    with torch.cuda.stream(stream):
-        step()  # configures kernels outside capture
-    torch.cuda.synchronize()
+    def single_step():
+        for o in ops:
+            rc = mm(o["handle"], ctypes.c_void_p(o["x"].data_ptr()), ctypes.c_void_p(o["out"].data_ptr()), 1, sp)
+            if rc:
+                _lib.check(rc)
 
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step()
-    torch.cuda.synchronize()
-
-    for _ in range(max(args.warmup, 3)):
-        graph.replay()
-    torch.cuda.synchronize()
-
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(dev) as clocks:
+    def capture(fn):
         with torch.cuda.stream(stream):
-            start.record(stream)
-            for _ in range(args.steps):
-                graph.replay()
-            end.record(stream)
+            fn()  # kernel set-up and the stream's scratch, outside the capture
         torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ms = start.elapsed_time(end)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        torch.cuda.synchronize()
+        return g
 
-    ms_t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
+    def timed(g, steps, sample_clocks=False):
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(dev) if sample_clocks else _Null() as clocks:
+            with torch.cuda.stream(stream):
+                start.record(stream)
+                for _ in range(steps):
+                    g.replay()
+                end.record(stream)
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = start.elapsed_time(end)
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return ms, float(t.item()), clocks
+
+    g_single = capture(single_step)
+    ms_single, ms_single_max, _ = timed(g_single, args.steps)
+    del g_single
+    g_chain = capture(chain_step)
+    ms, ms_max, clocks = timed(g_chain, args.steps, sample_clocks=True)
+    del g_chain
+    # the chain and the single calls compute the same bits (same split and summation order)
+    out_chain = xa.clone()
+    with torch.cuda.stream(stream):
+        single_step()
+    torch.cuda.synchronize()
+    same_bits = bool(torch.equal(out_chain, xa))
+
     bytes_step = pair_bytes() * LAYERS
     value = bytes_step * world * args.steps / (ms_max * 1e-3) / 1e9
 
-    # End to end through the C-ABI MatVec (host buffers, synchronous calls).
-    hx_up = x_up.cpu().numpy().reshape(-1).copy()
-    hx_dn = x_dn.cpu().numpy().reshape(-1).copy()
-    ho_up = np.empty(N_UP, np.float32)
-    ho_dn = np.empty(K_UP, np.float32)
+    # End to end through the C-ABI MatVec (host buffers, synchronous calls),
+    # each call's output the next call's input.
+    hx0 = x0.cpu().numpy().copy()
+    hh = np.empty(N_UP, np.float32)
+    hxa = np.empty(K_UP, np.float32)
     pv = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
     e2e_steps = max(1, min(args.steps, 20))
 
     def e2e_step():
         for l in range(LAYERS):
-            _lib.check(L.tq_matvec(handles[2 * l], pv(hx_up), K_UP, pv(ho_up), N_UP))
-            _lib.check(L.tq_matvec(handles[2 * l + 1], pv(hx_dn), N_UP, pv(ho_dn), K_UP))
+            _lib.check(L.tq_matvec(handles[2 * l], pv(hx0 if l == 0 else hxa), K_UP, pv(hh), N_UP))
+            _lib.check(L.tq_matvec(handles[2 * l + 1], pv(hh), N_UP, pv(hxa), K_UP))
 
     e2e_step()
     if world > 1:
@@ -454,12 +515,13 @@ def run_gpu(args, rank: int, world: int):
     if world > 1:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_value = bytes_step * world * e2e_steps / float(e2e_t.item()) / 1e9
+    e2e_same = bool(np.array_equal(hxa, xa.cpu().numpy()))
 
     side = None
     if rank == 0 and args.side_config:
         side = measure_side_configs(L, Q, torch, stream, load_peak()[0], args.side_config)
     elif rank == 0 and not args.no_side_configs:
-        side = measure_side_configs(L, Q, torch, stream, load_peak()[0])
+        side = measure_side_configs(L, Q, torch, stream, load_peak()[0], cpu=world == 1 and not args.no_cpu_baseline)
         side["C4 GPT-2-small int8 greedy decode"] = measure_gpt2(world == 1 and not args.no_cpu_baseline)
     qwen = None
     if not args.no_side_configs and not args.side_config:
@@ -468,10 +530,10 @@ def run_gpu(args, rank: int, world: int):
             side[f"C5 Qwen2.5-7B int4 greedy decode TP={world}"] = qwen
     if rank == 0:
         peak, peak_src = load_peak()
-        per_launch = pair_bytes() / 2  # up and down carry the same algorithmic bytes
-        kavg = ms / (args.steps * 2 * LAYERS)  # ms per call on this rank
-        achieved = per_launch / (kavg * 1e-3) / 1e9
+        launch_ms = ms / args.steps  # one chain launch per step on this rank
+        achieved = bytes_step / (launch_ms * 1e-3) / 1e9
         traffic = load_traffic()
+        single_call_us = ms_single / (args.steps * 2 * LAYERS) * 1e3
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
@@ -482,15 +544,22 @@ def run_gpu(args, rank: int, world: int):
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "frac_of_8tbs": round(achieved / 8000.0, 4),
                          "traffic": traffic,
-                         "kernel": "cmv_kernel<4,1,true> (int4 matvec on the tensor cores by mma.sync "
-                                   "u8 x s8 over the K-packed codes, M=1, one launch per call)",
-                         "call_us_mean": round(kavg * 1e3, 3),
-                         "algorithmic_bytes_per_launch": per_launch},
+                         "kernel": "chain_kernel<4> (64 dependent int4 M=1 matvecs in one launch; each on the "
+                                   "tensor cores by mma.sync u8 x s8 over the K-packed codes)",
+                         "launch_us_mean": round(launch_ms * 1e3, 3),
+                         "matvec_us_mean": round(launch_ms * 1e3 / (2 * LAYERS), 3),
+                         "algorithmic_bytes_per_launch": bytes_step},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": LAYERS * 4 * (K_UP + N_UP),
                     "d2h_bytes_per_step": LAYERS * 4 * (N_UP + K_UP),
-                    "api": "tq_matvec (host x/out, synchronous), the MatVec drop-in", "steps": e2e_steps},
-            "gpu_launches": args.steps * 2 * LAYERS * LAUNCHES_PER_CALL,
+                    "api": "tq_matvec (host x/out, synchronous), the MatVec drop-in, one call per matvec",
+                    "steps": e2e_steps, "same_bits_as_device_chain": e2e_same},
+            "single_call": {"value": round(bytes_step * args.steps / (ms_single_max * 1e-3) / 1e9, 3), "unit": "GB/s",
+                            "us_per_matvec": round(single_call_us, 3),
+                            "frac": round(pair_bytes() / 2 / (single_call_us * 1e-6) / 1e9 / peak, 4),
+                            "kernel": "cmv_kernel<4,1,true>, one launch per matvec (tq_matmul_dev)",
+                            "same_bits_as_chain": same_bits},
+            "gpu_launches": args.steps,
             "clocks": clocks.summary(),
         }
         if side:
@@ -498,9 +567,17 @@ def run_gpu(args, rank: int, world: int):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         print(json.dumps(line), flush=True)
-    del graph
-    for h in handles:
-        Q.free(h)
+    chain.free()
+    for hd in handles:
+        Q.free(hd)
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        pass
 
 
 def main():

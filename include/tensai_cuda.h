@@ -145,6 +145,54 @@ TQ_EXPORT int tq_matmul_dev(uint64_t handle, const float *x, float *out, int m, 
  * not reported by tq_device_status. */
 TQ_EXPORT int tq_matmul_dev_fixed(uint64_t handle, const float *x, float *out, int m, void *stream);
 
+/* ---- chains of dependent matvecs ----------------------------------------- */
+
+/* One op of a chain: out = x @ W (one activation row, DEVICE pointers on the
+ * matrix's device). epilogue: TQ_CHAIN_EPI_NONE; TQ_CHAIN_EPI_SWIGLU (int4,
+ * even cols: W is [gate | up], out[c] = float32(silu(gate_c)) * up_c for
+ * c < cols/2, silu in float64, _example/qwen/model.go:296-299);
+ * TQ_CHAIN_EPI_RESID (out = resid + x @ W, resid may equal out: the residual
+ * adds of model.go:276-278 / 301-303). norm_w non-NULL: x is first replaced
+ * by its RMSNorm, float32(float64(x) * inv) * norm_w with inv =
+ * 1/sqrt(sum(x^2)/rows + eps) in float64 (model.go:182-193); x must then be
+ * the output of op norm_from, an earlier TQ_CHAIN_EPI_RESID op of the same
+ * chain. x must be 16-byte aligned. */
+typedef struct {
+    uint64_t matrix;
+    const float *x;
+    float *out;
+    int epilogue;
+    const float *resid;
+    const float *norm_w;
+    int norm_from;
+    double eps;
+} tq_chain_op;
+
+#define TQ_CHAIN_EPI_NONE 0
+#define TQ_CHAIN_EPI_SWIGLU 1
+#define TQ_CHAIN_EPI_RESID 2
+
+/* Builds a chain of n (1..4096) dependent matvecs, all int8 or all int4,
+ * on the device of their matrices: op j reads x only after op j - 1 has
+ * written all of its output, so the chain computes exactly what n
+ * consecutive MatVec calls (quant.go:77-103 / quant4.go:93-119) with the
+ * fused norms and epilogues compute, in the order the decode loops make them
+ * (_example/qwen/model.go:232-307). No counterpart call exists in the
+ * reference: it is the device-side form of that sequence, so that the
+ * weights of later ops stream while earlier ops finish. The matrices must
+ * outlive the chain. Synchronous; TQ_ERR_ARG names the first bad op. */
+TQ_EXPORT int tq_chain_create(const tq_chain_op *ops, int n, uint64_t *chain);
+
+/* Enqueues the whole chain as ONE kernel launch on stream (a cudaStream_t;
+ * NULL = legacy default stream). Does not synchronize. Uses the same
+ * per-(device, stream) scratch as tq_matmul_dev (so the first call on a
+ * stream must not be inside a capture); capturable in CUDA graphs
+ * afterwards. Launches of one chain on different streams must not overlap. */
+TQ_EXPORT int tq_chain_run(uint64_t chain, void *stream);
+
+/* Releases a chain (waits for the device first; a second call is a no-op). */
+TQ_EXPORT int tq_chain_free(uint64_t chain);
+
 /* Selects the GPU kernel behind tq_matvec / tq_matmul / tq_matmul_dev for
  * m <= 15 rows (process-wide). 0 (default) = the fastest measured choice per
  * row count: int4 single rows as 5 below, otherwise single-launch CUDA-core

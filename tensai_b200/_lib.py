@@ -60,11 +60,26 @@ SIGNATURES = {
     "tq_qwen_create": (I, [P, U64, F, I, I, P, PU64]),
     "tq_qwen_generate": (I, [U64, P, I, I, P, P]),
     "tq_qwen_free": (I, [U64]),
+    "tq_chain_create": (I, [P, I, PU64]),
+    "tq_chain_run": (I, [U64, P]),
+    "tq_chain_free": (I, [U64]),
     "tq_set_matvec_kernel": (I, [I]),
     "tq_debug_fail_allocs": (I, [I]),
 }
 
 ABI_VERSION = 1
+
+TQ_CHAIN_EPI_NONE = 0
+TQ_CHAIN_EPI_SWIGLU = 1
+TQ_CHAIN_EPI_RESID = 2
+
+
+class ChainOp(ctypes.Structure):
+    """tq_chain_op of include/tensai_cuda.h."""
+
+    _fields_ = [("matrix", ctypes.c_uint64), ("x", ctypes.c_void_p), ("out", ctypes.c_void_p),
+                ("epilogue", ctypes.c_int), ("resid", ctypes.c_void_p), ("norm_w", ctypes.c_void_p),
+                ("norm_from", ctypes.c_int), ("eps", ctypes.c_double)]
 
 
 class TensaiError(RuntimeError):

@@ -13,6 +13,7 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 #include "../../include/tensai_cuda.h"
 #include "tq_common.cuh"
@@ -27,6 +28,15 @@ std::atomic<int> g_fail_allocs{0};
 std::mutex g_mu;
 std::unordered_map<uint64_t, std::shared_ptr<Handle>> g_handles;
 uint64_t g_next_handle = 1;
+
+// Matvec chains (tq_chain_create) and the device they live on.
+struct ChainEntry {
+    TqChain *chain = nullptr;
+    int device = 0;
+};
+std::mutex g_chain_mu;
+std::unordered_map<uint64_t, std::shared_ptr<ChainEntry>> g_chains;
+uint64_t g_next_chain = 1;
 
 // Per-thread, per-device context for the host-pointer entry points.
 struct ThreadCtx {
@@ -607,6 +617,97 @@ int tq_device_status(unsigned *bits) {
         if (e != cudaSuccess) return tq_cuda_fail(e, "status read");
         *bits |= v;
     }
+    return TQ_OK;
+}
+
+int tq_chain_create(const tq_chain_op *ops, int n, uint64_t *chain) {
+    if (!chain || (!ops && n > 0)) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    if (n < 1 || n > TQ_CHAIN_MAX_OPS)
+        return tq_fail(TQ_ERR_ARG, "tensai: a chain takes 1 to %d ops, got %d", TQ_CHAIN_MAX_OPS, n);
+    std::vector<std::shared_ptr<Handle>> hs(n);
+    std::vector<TqChainSpec> spec(n);
+    int rc;
+    for (int j = 0; j < n; j++) {
+        if (!(hs[j] = tq_lookup_checked(ops[j].matrix, &rc))) return rc;
+        if (hs[j]->device != hs[0]->device)
+            return tq_fail(TQ_ERR_ARG, "tensai: chain op %d is on device %d, op 0 on device %d", j, hs[j]->device,
+                           hs[0]->device);
+        spec[j].m = &hs[j]->m;
+        spec[j].x = ops[j].x;
+        spec[j].out = ops[j].out;
+        spec[j].epi = ops[j].epilogue;
+        spec[j].resid = ops[j].resid;
+        spec[j].norm_w = ops[j].norm_w;
+        spec[j].norm_from = ops[j].norm_from;
+        spec[j].eps = ops[j].eps;
+    }
+    cudaError_t e = cudaSetDevice(hs[0]->device);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "set device");
+    TqChain *ch = nullptr;
+    int why = TQ_CHAIN_OK, bad = 0;
+    e = tq_chain_build(spec.data(), n, &ch, &why, &bad);
+    if (why != TQ_CHAIN_OK) {
+        static const char *what[] = {"",
+                                     "op count out of range",
+                                     "int8 and int4 matrices in one chain",
+                                     "a matrix without rows or columns",
+                                     "an int4 matrix without its tensor-core copy",
+                                     "a null or not 16-byte aligned input, or a null output",
+                                     "an unknown epilogue, or one the matrix cannot take (SwiGLU: int4, even "
+                                     "columns; residual: a resid pointer)",
+                                     "too many column tiles",
+                                     "a normalised input that is not the output of an earlier residual op of "
+                                     "matching width"};
+        return tq_fail(TQ_ERR_ARG, "tensai: chain op %d: %s", bad, what[why]);
+    }
+    if (e != cudaSuccess) return tq_cuda_fail(e, "chain build");
+    auto ent = std::make_shared<ChainEntry>();
+    ent->chain = ch;
+    ent->device = hs[0]->device;
+    std::lock_guard<std::mutex> lk(g_chain_mu);
+    *chain = g_next_chain++;
+    g_chains[*chain] = ent;
+    return TQ_OK;
+}
+
+static std::shared_ptr<ChainEntry> find_chain(uint64_t h, int *rc) {
+    std::lock_guard<std::mutex> lk(g_chain_mu);
+    auto it = g_chains.find(h);
+    if (it == g_chains.end()) {
+        *rc = tq_fail(TQ_ERR_HANDLE, "tensai: invalid or freed chain handle %llu", (unsigned long long)h);
+        return nullptr;
+    }
+    *rc = TQ_OK;
+    return it->second;
+}
+
+int tq_chain_run(uint64_t chain, void *stream) {
+    int rc;
+    auto c = find_chain(chain, &rc);
+    if (!c) return rc;
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "set device");
+    TqScratch scr;
+    if ((rc = scratch_for(c->device, (cudaStream_t)stream, &scr, 1))) return rc;
+    e = tq_chain_launch(c->chain, scr, (cudaStream_t)stream);
+    return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "chain launch");
+}
+
+int tq_chain_free(uint64_t chain) {
+    std::shared_ptr<ChainEntry> c;
+    {
+        std::lock_guard<std::mutex> lk(g_chain_mu);
+        auto it = g_chains.find(chain);
+        if (it == g_chains.end()) return TQ_OK;
+        c = it->second;
+        g_chains.erase(it);
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(c->device);
+    cudaDeviceSynchronize(); // no launch may still read the descriptors
+    tq_chain_destroy(c->chain);
+    cudaSetDevice(prev);
     return TQ_OK;
 }
 

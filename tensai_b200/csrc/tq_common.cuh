@@ -147,8 +147,11 @@ cudaError_t tq_launch_matvec(const TqMatrixDev &m, const float *x, float *out, i
 //   TQ_EPI_SWIGLU  int4 [gate | up] matrix of 2F columns (column c and F + c
 //                  share a code byte): out[c] = float32(silu(gate_c)) * up_c,
 //                  c < F, silu in float64 (_example/qwen/model.go:296-299).
+//   TQ_EPI_RESID   (chains only) out = resid + x W, resid may be out itself
+//                  (the residual adds of _example/qwen/model.go:276-278, 301-303).
 #define TQ_EPI_NONE 0
 #define TQ_EPI_SWIGLU 1
+#define TQ_EPI_RESID 2
 cudaError_t tq_launch_cmv_epi(const TqMatrixDev &m, const float *x, float *out, const TqScratch &scr, cudaStream_t st,
                               int epi, bool tc);
 // int4 matvec on the tensor cores (mma.sync over the K-packed copy), one row
@@ -176,3 +179,38 @@ enum { TQ_FIXED_OK = 0, TQ_FIXED_CUDA, TQ_FIXED_DEVICE, TQ_FIXED_SMS, TQ_FIXED_T
 #define TQ_FIXED_ROWS_PER_LAUNCH 4
 int tq_launch_matvec_fixed(const TqMatrixDev &m, const float *x, float *out, int M, cudaStream_t st,
                            cudaError_t *err);
+
+// A chain of dependent single-row matvecs in one persistent launch
+// (tq_chain.cu). Op j reads its input only after op j - 1 has written all of
+// its output. Every op of a chain has the same bit width; x is 16-byte aligned.
+// norm_w != null: x (the output of op norm_from, a TQ_EPI_RESID op earlier in
+// the chain) is RMS-normalised with weight norm_w and epsilon eps first.
+#define TQ_CHAIN_MAX_OPS 4096
+struct TqChainSpec {
+    const TqMatrixDev *m;
+    const float *x;
+    float *out;
+    int epi;
+    const float *resid;
+    const float *norm_w;
+    int norm_from;
+    double eps;
+};
+struct TqChain;
+enum {
+    TQ_CHAIN_OK = 0,
+    TQ_CHAIN_BAD_COUNT,  // no ops, or more than TQ_CHAIN_MAX_OPS
+    TQ_CHAIN_MIXED_BITS, // int8 and int4 ops in one chain
+    TQ_CHAIN_EMPTY,      // a matrix without rows or columns
+    TQ_CHAIN_NO_KPACK,   // an int4 matrix without its K-packed copy
+    TQ_CHAIN_X_ALIGN,    // a null or not 16-byte aligned input, or a null output
+    TQ_CHAIN_EPI,        // an unknown epilogue or one the matrix cannot take
+    TQ_CHAIN_TOO_WIDE,   // more than TQ_MAX_TILES column tiles
+    TQ_CHAIN_NORM,       // a normalised input that is not an earlier residual op's output
+};
+// Validates the ops and copies their descriptors to the current device
+// (synchronous); *why names the first problem found and *bad_op its op.
+cudaError_t tq_chain_build(const TqChainSpec *spec, int n, TqChain **out, int *why, int *bad_op);
+void tq_chain_destroy(TqChain *ch);
+int tq_chain_device(const TqChain *ch);
+cudaError_t tq_chain_launch(const TqChain *ch, const TqScratch &scr, cudaStream_t st);

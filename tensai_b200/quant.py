@@ -178,6 +178,52 @@ def matmul_dev(handle: int, x, out, stream=None) -> None:
                                          x.shape[0] if x.dim() == 2 else 1, st))
 
 
+class Chain:
+    """A chain of dependent single-row matvecs run as one launch (tq_chain_create).
+
+    ops: sequence of dicts with keys handle, x, out (CUDA float32 tensors or
+    device addresses) and optionally epilogue ("none" | "swiglu" | "resid"),
+    resid, norm_w, norm_from, eps."""
+
+    _EPI = {"none": _lib.TQ_CHAIN_EPI_NONE, "swiglu": _lib.TQ_CHAIN_EPI_SWIGLU, "resid": _lib.TQ_CHAIN_EPI_RESID}
+
+    def __init__(self, ops):
+        def addr(t):
+            if t is None:
+                return None
+            return t if isinstance(t, int) else t.data_ptr()
+
+        arr = (_lib.ChainOp * len(ops))()
+        for i, o in enumerate(ops):
+            arr[i].matrix = o["handle"]
+            arr[i].x = addr(o["x"])
+            arr[i].out = addr(o["out"])
+            arr[i].epilogue = self._EPI[o.get("epilogue", "none")]
+            arr[i].resid = addr(o.get("resid"))
+            arr[i].norm_w = addr(o.get("norm_w"))
+            arr[i].norm_from = o.get("norm_from", -1)
+            arr[i].eps = o.get("eps", 0.0)
+        h = ctypes.c_uint64()
+        self.handle = 0
+        _lib.check(_lib.load().tq_chain_create(arr, len(ops), ctypes.byref(h)))
+        self.handle = h.value
+
+    def run(self, stream=None) -> None:
+        st = ctypes.c_void_p(stream.cuda_stream if stream is not None else None)
+        _lib.check(_lib.load().tq_chain_run(self.handle, st))
+
+    def free(self) -> None:
+        if self.handle:
+            _lib.load().tq_chain_free(self.handle)
+            self.handle = 0
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.free()
+
+
 def synth_dev(out, seed: int, stream_id: int, sigma: float, stream=None) -> None:
     """Fills a float32 CUDA tensor with the seeded generator shared with the oracle."""
     st = ctypes.c_void_p(stream.cuda_stream if stream is not None else None)
