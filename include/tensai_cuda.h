@@ -137,12 +137,16 @@ TQ_EXPORT int tq_matmul_dev(uint64_t handle, const float *x, float *out, int m, 
  * 1,048,576 int4 columns) and GPUs of at most 160 SMs, else
  * TQ_ERR_UNSUPPORTED with a message naming the limit; activation rows run 4
  * per launch, any m. The first call on each device does the set-up (looks up
- * the fixed arrays' device addresses) and should come before any stream
+ * the fixed arrays' device addresses and loads every kernel this entry point
+ * can launch, so no later call loads code) and should come before any stream
  * capture. All callers on one device share the fixed scratch: calls that may
  * overlap on the device (other streams, other threads) race and corrupt each
  * other's results, so issue them in order on one stream. A bounded-wait
- * timeout inside the kernel is recorded in the fixed status word only and is
- * not reported by tq_device_status. */
+ * timeout inside the kernel sets the fixed scratch's status word:
+ * tq_device_status reports it (TQ_STATUS_TIMEOUT) and re-arms the fixed
+ * counters; results since the timeout are invalid. The set-up holds device
+ * addresses for the life of the process: after a cudaDeviceReset of a device,
+ * do not use this entry point on that device again. */
 TQ_EXPORT int tq_matmul_dev_fixed(uint64_t handle, const float *x, float *out, int m, void *stream);
 
 /* ---- chains of dependent matvecs ----------------------------------------- */
@@ -198,7 +202,7 @@ TQ_EXPORT int tq_chain_free(uint64_t chain);
  * row count: int4 single rows as 5 below, otherwise single-launch CUDA-core
  * fp32 FMA for m <= 2 and tensor-core integer MMA (weights used as stored,
  * activations split into exact int8 digit planes) for 3 <= m <= 15. 1 = CUDA-core fp32 FMA with per-warp copies;
- * 2 = single-launch tensor-core integer MMA; 3 = single-launch CUDA-core fp32
+ * 2 is retired (TQ_ERR_ARG); 3 = single-launch CUDA-core fp32
  * FMA, 2 rows per launch; 4 = tensor-core integer MMA with a digit-plane
  * launch; 5 = int4 on the tensor cores by mma.sync (codes from a K-packed
  * device copy that every int4 matrix holds, activations as exact int8 digits

@@ -45,6 +45,7 @@ struct ThreadCtx {
     size_t d_x_cap = 0, d_out_cap = 0;
     float *h_x = nullptr, *h_out = nullptr; // pinned staging
     size_t h_x_cap = 0, h_out_cap = 0;
+    unsigned *h_status = nullptr; // pinned: the stream scratch's status word after each call
 };
 thread_local std::unordered_map<int, ThreadCtx> t_ctx;
 
@@ -157,7 +158,7 @@ static cudaError_t read_status(const TqScratch &scr, cudaStream_t st, unsigned *
 //                (tq_cmv.cu) for M <= 2 and the tcgen05 matvec (tq_igemv.cu)
 //                for 3 <= M <= 15;
 //   1: CUDA-core matvec with per-warp copies (tq_matvec.cu);
-//   2: single-launch tensor-core matvec (tq_gemv.cu);
+//   2: retired (a single-launch tensor-core variant, never the fastest);
 //   3: single-launch CUDA-core matvec (tq_cmv.cu), 2 rows per launch;
 //   4: tensor-core matvec with a digit-plane launch (tq_igemv.cu);
 //   5: int4 on the tensor cores by mma.sync (tq_cmv.cu), one row per launch;
@@ -171,12 +172,11 @@ static cudaError_t launch_matvec(const TqMatrixDev &m, const float *x, float *ou
     if (M >= TQ_MM_MIN_ROWS) return tq_launch_mm(m, x, out, M, scr, st);
     switch (g_matvec_kernel.load()) {
     case 1: return tq_launch_matvec(m, x, out, M, scr, st);
-    case 2: return tq_launch_gemv(m, x, out, M, scr, st);
     case 3: return tq_launch_cmv(m, x, out, M, scr, st);
     case 4: return tq_launch_igemv(m, x, out, M, scr, st);
     case 5: return tq_launch_tmv(m, x, out, M, scr, st);
     default:
-        if (M == 1 && m.bits == 4 && m.kcodes) return tq_launch_tmv(m, x, out, M, scr, st);
+        if (M == 1 && m.bits == 4 && m.kpack) return tq_launch_tmv(m, x, out, M, scr, st);
         return M <= 2 ? tq_launch_cmv(m, x, out, M, scr, st) : tq_launch_igemv(m, x, out, M, scr, st);
     }
 }
@@ -262,10 +262,10 @@ static int check_dims(int bits, int rows, int cols) {
 }
 
 static void release_matrix(TqMatrixDev *m) {
-    for (void *p : {(void *)m->codes, (void *)m->scale, (void *)m->kcodes, (void *)m->kscale})
+    for (void *p : {(void *)m->codes, (void *)m->scale, (void *)m->kpack})
         if (p) cudaFree(p);
-    m->codes = m->kcodes = nullptr;
-    m->scale = m->kscale = nullptr;
+    m->codes = m->kpack = nullptr;
+    m->scale = nullptr;
 }
 
 // Allocates a device matrix on the calling thread's device and clears it on
@@ -280,16 +280,15 @@ static int alloc_matrix(int bits, int rows, int cols, TqMatrixDev *m, cudaStream
     const size_t cbytes = tq_code_bytes(bits, rows, cols);
     const size_t sfloats = tq_scale_floats(bits, rows, cols);
     // int4 matrices also hold a K-packed copy of codes and scales for the
-    // tensor-core matvec (filled by the quantize / upload launchers)
-    const int copies = bits == 4 ? 2 : 1;
-    uint8_t **cp[2] = {&m->codes, &m->kcodes};
-    float **sp[2] = {&m->scale, &m->kscale};
-    cudaError_t e = cudaSuccess;
-    for (int c = 0; c < copies && e == cudaSuccess; c++) {
-        e = tq_dev_malloc((void **)cp[c], cbytes);
-        if (e == cudaSuccess) e = tq_dev_malloc((void **)sp[c], sfloats * sizeof(float));
-        if (e == cudaSuccess) e = cudaMemsetAsync(*cp[c], 0, cbytes, st);
-        if (e == cudaSuccess) e = cudaMemsetAsync(*sp[c], 0, sfloats * sizeof(float), st);
+    // tensor-core matvecs (filled by the quantize / upload launchers)
+    cudaError_t e = tq_dev_malloc((void **)&m->codes, cbytes);
+    if (e == cudaSuccess) e = tq_dev_malloc((void **)&m->scale, sfloats * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->codes, 0, cbytes, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->scale, 0, sfloats * sizeof(float), st);
+    if (bits == 4) {
+        const size_t kbytes = cbytes / TQ_ITEM_BYTES * TQ_KPACK_BYTES;
+        if (e == cudaSuccess) e = tq_dev_malloc((void **)&m->kpack, kbytes);
+        if (e == cudaSuccess) e = cudaMemsetAsync(m->kpack, 0, kbytes, st);
     }
     if (e != cudaSuccess) {
         release_matrix(m);
@@ -562,18 +561,30 @@ int tq_matmul(uint64_t handle, const float *x, float *out, int m) {
     if ((rc = grow_dev(&c->d_x, &c->d_x_cap, nx)) || (rc = grow_dev(&c->d_out, &c->d_out_cap, no)) ||
         (rc = grow_host(&c->h_x, &c->h_x_cap, nx)) || (rc = grow_host(&c->h_out, &c->h_out_cap, no)))
         return rc;
+    if (!c->h_status) {
+        e = cudaMallocHost((void **)&c->h_status, sizeof(unsigned));
+        if (e != cudaSuccess) return tq_cuda_fail(e, "pinned staging allocation");
+    }
     TqScratch scr;
     if ((rc = scratch_for(p->device, c->stream, &scr, m))) return rc;
+    // One synchronization per call: x in, the launch, then out and the
+    // scratch's status word back into pinned memory.
     std::memcpy(c->h_x, x, nx * sizeof(float));
     e = cudaMemcpyAsync(c->d_x, c->h_x, nx * sizeof(float), cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess) e = launch_matvec(p->m, c->d_x, c->d_out, m, scr, c->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(c->h_out, c->d_out, no * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(c->h_status, scr.status, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return tq_cuda_fail(e, "matmul");
-    unsigned status = 0;
-    if ((e = read_status(scr, c->stream, &status)) != cudaSuccess) return tq_cuda_fail(e, "status read");
-    if (status & TQ_STATUS_TIMEOUT)
-        return tq_fail(TQ_ERR_TIMEOUT, "tensai: a kernel timed out waiting for its weight copies");
+    if (*c->h_status) { // rare: re-arm the status word before reporting
+        const unsigned status = *c->h_status;
+        e = cudaMemsetAsync(scr.status, 0, sizeof(unsigned), c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) return tq_cuda_fail(e, "status reset");
+        if (status & TQ_STATUS_TIMEOUT)
+            return tq_fail(TQ_ERR_TIMEOUT, "tensai: a kernel timed out waiting for its weight copies");
+    }
     std::memcpy(out, c->h_out, no * sizeof(float));
     return TQ_OK;
 }
@@ -617,6 +628,9 @@ int tq_device_status(unsigned *bits) {
         if (e != cudaSuccess) return tq_cuda_fail(e, "status read");
         *bits |= v;
     }
+    unsigned fixed = 0; // the allocation-free entry point's own status word
+    if ((e = tq_fixed_status(&fixed)) != cudaSuccess) return tq_cuda_fail(e, "fixed status read");
+    *bits |= fixed;
     return TQ_OK;
 }
 
@@ -657,7 +671,9 @@ int tq_chain_create(const tq_chain_op *ops, int n, uint64_t *chain) {
                                      "columns; residual: a resid pointer)",
                                      "too many column tiles",
                                      "a normalised input that is not the output of an earlier residual op of "
-                                     "matching width"};
+                                     "matching width",
+                                     "too many rows for its column count: a GPU's share of the matrix covers "
+                                     "more than 64 groups of 64 rows"};
         return tq_fail(TQ_ERR_ARG, "tensai: chain op %d: %s", bad, what[why]);
     }
     if (e != cudaSuccess) return tq_cuda_fail(e, "chain build");
@@ -712,7 +728,8 @@ int tq_chain_free(uint64_t chain) {
 }
 
 int tq_set_matvec_kernel(int which) {
-    if (which < 0 || which > 5) return tq_fail(TQ_ERR_ARG, "tensai: matvec kernel must be 0..5, got %d", which);
+    if (which < 0 || which > 5 || which == 2)
+        return tq_fail(TQ_ERR_ARG, "tensai: matvec kernel must be 0, 1, 3, 4 or 5, got %d", which);
     g_matvec_kernel.store(which);
     return TQ_OK;
 }

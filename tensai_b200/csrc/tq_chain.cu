@@ -52,13 +52,16 @@ using namespace tqi;
 
 constexpr int CW = 8;          // consumer warps
 constexpr int CWI = CW / 2;    // item streams: warps 2i and 2i + 1 take the two halves (TC: column halves) of an item
-constexpr int kChainThreads = (CW + 1) * 32; // producer warp + consumers
+constexpr int kChainThreads = (CW + 2) * 32; // producer warp, consumers, reducer warp
 constexpr int kChainSmemCap = 226 * 1024;
 constexpr int kUp = 4 * 32; // SwiGLU: entry e (gate) pairs with entry e + kUp (up)
+// Activations staged per op and CTA: the 64-row groups its slice touches, at
+// most TQ_CHAIN_MAX_GROUPS of them, 256 bytes each (int4: their digits in place).
+constexpr int XU = TQ_CHAIN_MAX_GROUPS;
 
 struct ChainOp {
-    const uint8_t *codes; // int4: the K-packed copy; int8: the tiled codes
-    const float *scale;   // int4: the K-packed scales; int8: per-column scales
+    const uint8_t *codes; // int4: the K-packed items (codes and scales); int8: the tiled codes
+    const float *scale;   // int8: per-column scales
     const float *x;       // rows floats, 16-byte aligned
     float *out;
     const float *resid;   // TQ_EPI_RESID
@@ -85,33 +88,32 @@ template <int BITS> struct ChCfg {
     static constexpr bool TC = BITS == 4;
     static constexpr int NP = BITS == 8 ? 4 : 8; // sums per lane
     static constexpr int E = NP * 32;            // sums of a tile segment
-    static constexpr int SLOT = TC ? kItem + 1024 : kItem;
-    static constexpr int XD = 4; // per-warp activation ring
-    static constexpr int XROWS = TC ? kRows : kHalf;
-    static constexpr int XSLOT = XD * XROWS * 4;
-    static constexpr int PLANES = TC ? 3 * kRows : 0;
-    static constexpr int RED = 2 * CW * E * 4;
-    static constexpr int FIXED = CW * XSLOT + CW * PLANES + RED + 2048;
+    // A ring slot holds G consecutive items of a slice, moved by ONE bulk copy:
+    // a copy has a fixed cost per SM of about 0.4 us whatever its size, so one
+    // thread issuing 8 KB copies streams about 3.2 TB/s over 148 SMs, 16 KB
+    // copies 6.2 TB/s and 32 KB copies 7.0 TB/s (measured on B200).
+    static constexpr int ITEMB = TC ? TQ_KPACK_BYTES : kItem; // int4: codes and scales of a K-packed item
+    static constexpr int G = TC ? 2 : 4;
+    static constexpr int SLOT = G * ITEMB;
+    static constexpr int XS = XU * 256;          // staged activation groups
+    static constexpr int RED = 2 * CW * E * 4;   // two deposit buffers
+    static constexpr int HAND = E * 4;           // the first segment, handed to the reducer warp
+    static constexpr int FIXED = XS + RED + HAND + 2048;
     static constexpr int R0 = (kChainSmemCap - FIXED) / SLOT;
     static constexpr int R = R0 < 24 ? R0 : 24;
     static constexpr int RING_OFF = 0;
-    static constexpr int X_OFF = R * SLOT;
-    static constexpr int PL_OFF = X_OFF + CW * XSLOT;
-    static constexpr int RED_OFF = PL_OFF + CW * PLANES;
-    static constexpr int BAR_OFF = RED_OFF + RED;
-    static constexpr int SSR_OFF = BAR_OFF + 2 * R * 8; // CW doubles
+    static constexpr int XS_OFF = R * SLOT;
+    static constexpr int RED_OFF = XS_OFF + XS;
+    static constexpr int HAND_OFF = RED_OFF + RED;
+    static constexpr int BAR_OFF = HAND_OFF + HAND;     // full[R], empty[R], hand_full, hand_empty
+    static constexpr int SSR_OFF = BAR_OFF + (2 * R + 2) * 8; // CW doubles
     static constexpr int MISC_OFF = SSR_OFF + CW * 8;
     static constexpr int SMEM = MISC_OFF + 64;
-    static_assert(R >= 8, "ring too shallow");
+    static_assert(R >= 4, "ring too shallow");
     static_assert(SMEM <= kChainSmemCap, "shared memory budget");
     static_assert(E <= CW * 32, "one entry per consumer thread");
 };
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 __device__ __forceinline__ unsigned ld_relaxed(const unsigned *p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -146,21 +148,22 @@ __device__ __forceinline__ void chain_abort(const ChainParams &p, volatile int *
     *abort = 1;
 }
 
-// Bounded wait until *cnt >= target (acquire). One thread.
+// Bounded wait until *cnt >= target, then acquire. One thread.
 __device__ void wait_count(const ChainParams &p, const unsigned *cnt, unsigned target, volatile int *abort) {
-    if (ld_acquire(cnt) >= target) return;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-        if (ld_acquire(cnt) >= target) return;
-        if (*abort || ld_relaxed(p.ctl + 1)) {
-            chain_abort(p, abort, false);
-            return;
-        }
-        if (global_ns() - t0 > kWaitNs) {
-            chain_abort(p, abort, true);
-            return;
+    if (ld_relaxed(cnt) < target) {
+        const unsigned long long t0 = global_ns();
+        while (ld_relaxed(cnt) < target) {
+            if (*abort || ld_relaxed(p.ctl + 1)) {
+                chain_abort(p, abort, false);
+                return;
+            }
+            if (global_ns() - t0 > kWaitNs) {
+                chain_abort(p, abort, true);
+                return;
+            }
         }
     }
+    fence_gpu(); // acquire: the writers' tiles before this CTA's loads
 }
 
 // Output column of sum j of lane `lane` in tile `tile` (int4: -1 beyond the pairs).
@@ -210,7 +213,7 @@ __device__ void finish_tile_warp(const ChainOp &op, unsigned *done, int tile, in
         ss = warp_sum_d(ss);
         if (lane == 0) op.ss_out[tile] = ss;
     }
-    fence_gpu(); // this lane's stores, then the warp's count
+    // the warp's stores, then one cumulative release of the tile count
     __syncwarp();
     if (lane == 0) red_release(done, 1u);
 }
@@ -269,6 +272,24 @@ template <int BITS> __device__ __forceinline__ float put_entry(const ChainOp &op
     return col >= 0 ? put<BITS>(op, col, v) : 0.f;
 }
 
+// Where a CTA's slice of op j lies: items [i0, i1) of the tile-major list,
+// tile segments, and whether its first segment (a tile shared with earlier
+// CTAs, when the slice goes on past it) is handed to the reducer warp.
+struct Slice {
+    long long i0, i1;
+    int nitems, tile0, nseg;
+    bool handoff;
+    __device__ __forceinline__ Slice(const TqSplit &split, int c, int units) {
+        i0 = split.start(c);
+        i1 = split.start(c + 1);
+        nitems = (int)(i1 - i0);
+        tile0 = (int)(i0 / units);
+        nseg = (int)((i1 - 1) / units) - tile0 + 1;
+        const long long t0 = (long long)tile0 * units;
+        handoff = nseg > 1 && split.owner(t0) != split.owner(t0 + units - 1);
+    }
+};
+
 template <int BITS>
 __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) {
     using C = ChCfg<BITS>;
@@ -277,6 +298,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
     extern __shared__ __align__(16) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
     uint64_t *empty = full + R;
+    uint64_t *hand_full = empty + R, *hand_empty = hand_full + 1;
     double *ssred = reinterpret_cast<double *>(smem + C::SSR_OFF);
     volatile int *abort = reinterpret_cast<volatile int *>(smem + C::MISC_OFF);
     int *cnt = reinterpret_cast<int *>(smem + C::MISC_OFF + 8);                    // [2] deposits per buffer
@@ -289,6 +311,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
     volatile int *lastflag = reinterpret_cast<volatile int *>(smem + C::MISC_OFF + 28);
     double *inv_s = reinterpret_cast<double *>(smem + C::MISC_OFF + 32);
     float *red = reinterpret_cast<float *>(smem + C::RED_OFF);
+    float *hand = reinterpret_cast<float *>(smem + C::HAND_OFF);
+    uint8_t *xs = smem + C::XS_OFF; // staged groups, 256 bytes each
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x;
@@ -296,8 +320,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
     if (threadIdx.x == 0) {
         for (int s = 0; s < R; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 2); // both halves consumed
+            mbar_init(&empty[s], 2 * C::G); // both halves of each item consumed
         }
+        mbar_init(hand_full, 1);
+        mbar_init(hand_empty, 1);
         *abort = 0;
         *issued = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -317,8 +343,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
                 const TqSplit split(op->items, ctas);
                 const long long i0 = split.start(c), i1 = split.start(c + 1);
                 const uint8_t *codes = op->codes;
-                const float *scale = op->scale;
-                for (long long it = i0; it < i1; it++, seq++) {
+                for (long long it = i0; it < i1; it += C::G, seq++) { // one group of up to G items per slot
                     const int s = seq % R;
                     if (seq >= R && !wait_bar(&empty[s], ((seq / R) & 1) ^ 1, abort, p.status)) {
                         stop = true;
@@ -328,10 +353,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
                         stop = true;
                         break;
                     }
+                    const uint32_t bytes = (uint32_t)(i1 - it < C::G ? i1 - it : C::G) * C::ITEMB;
                     uint8_t *dst = smem + C::RING_OFF + s * C::SLOT;
-                    mbar_arrive_expect_tx(&full[s], C::SLOT);
-                    bulk_load(dst, codes + it * kItem, kItem, &full[s]);
-                    if (TC) bulk_load(dst + kItem, scale + it * (2 * kCols), 1024, &full[s]);
+                    mbar_arrive_expect_tx(&full[s], bytes);
+                    bulk_load(dst, codes + it * C::ITEMB, bytes, &full[s]);
                     *issued = seq + 1;
                 }
             }
@@ -344,14 +369,33 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
                 while (!mbar_try_wait_hint(&full[k % R], (k / R) & 1, 100000u))
                     if (global_ns() - t0 > kWaitNs) break;
         }
+    } else if (warp == CW + 1) {
+        // ---------------- reducer: a shared first segment, off the consumers' path ----------------
+        pdl_wait(); // it may write op 0's outputs, which the previous kernel owns until here
+        int nh = 0;
+        for (int j = 0; j < p.nops; j++) {
+            const ChainOp &op = p.ops[j];
+            if (c >= op.ctas) continue;
+            const TqSplit split(op.items, op.ctas);
+            const Slice sl(split, c, op.units);
+            if (!sl.handoff) continue;
+            const bool ok = wait_bar(hand_full, nh & 1, abort, p.status);
+            float v[NP];
+#pragma unroll
+            for (int q = 0; q < NP; q++) v[q] = hand[q * 32 + lane];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(hand_empty);
+            nh++;
+            if (ok) publish_shared_warp<BITS>(op, p, p.done + j, split, c, sl.tile0, lane, v);
+        }
     } else {
         // ---------------- consumers ----------------
         const int cw = warp - 1, ct = threadIdx.x - 32;
         const int hf = cw & 1, jsub = cw >> 1;
         const uint32_t mg = 0x4B000000u;
-        float *xs = reinterpret_cast<float *>(smem + C::X_OFF + cw * C::XSLOT);
         const uint8_t *ring = smem + C::RING_OFF;
-        int seq_base = 0; // sequence number of this CTA's first item of op j
+        int seq_base = 0; // sequence number of the ring group holding this CTA's first item of op j
+        int nh = 0;       // first segments handed to the reducer so far
         unsigned prev_tiles = 0;
         for (int j = 0; j < p.nops; j++) {
             const ChainOp &op = p.ops[j];
@@ -378,52 +422,54 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
             prev_tiles = (unsigned)op.tiles;
             const int ctas = op.ctas;
             if (c >= ctas) continue;
-            const double inv = norm ? *inv_s : 1.0;
-            const TqSplit split(op.items, ctas);
-            const long long i0 = split.start(c), i1 = split.start(c + 1);
-            const int nitems = (int)(i1 - i0);
             const int units = op.units;
-            const int tile0 = (int)(i0 / units);
+            const TqSplit split(op.items, ctas);
+            const Slice sl(split, c, units);
+            const long long i0 = sl.i0;
+            const int nitems = sl.nitems, tile0 = sl.tile0, nseg = sl.nseg;
             auto seg_begin = [&](int s) { return s == 0 ? 0 : (int)((long long)(tile0 + s) * units - i0); };
-            const int nseg = (int)((i1 - 1) / units) - tile0 + 1;
             const int last_tile = tile0 + nseg - 1;
             const long long lt0 = (long long)last_tile * units;
             const int last_cf = split.owner(lt0), last_cl = split.owner(lt0 + units - 1);
             const int last_slot = split.slot(c, lt0);
 
-            // activations: ring slot t % XD holds this warp's t-th item's rows
-            // (TC: all 64 rows of its unit; else the 32 rows of its half)
-            int unit_x = (int)((i0 + jsub) % units);
-            int tx = 0;
-            const int nmine = jsub < nitems ? (nitems - 1 - jsub) / CWI + 1 : 0;
-            constexpr int XL = C::XROWS / 4; // lanes that copy 16 bytes each
-            auto issue_x = [&]() {
-                if (tx < nmine) {
-                    if (lane < XL) {
-                        const int r0 = unit_x * kRows + (TC ? 0 : hf * kHalf) + 4 * lane;
-                        const int nv = op.rows - r0;
-                        const int bytes = nv >= 4 ? 16 : nv > 0 ? 4 * nv : 0;
-                        cp_async16_cg(xs + (tx & (C::XD - 1)) * C::XROWS + 4 * lane, op.x + (bytes ? r0 : 0), bytes);
-                    }
-                    unit_x += CWI;
-                    while (unit_x >= units) unit_x -= units;
-                }
-                cp_async_commit();
-                tx++;
-            };
-            // the lane's own landed activations of item t, normalised in place
-            auto norm_x = [&](int t, int unit) {
-                if (!norm || lane >= XL) return;
-                float4 *v4 = reinterpret_cast<float4 *>(xs + (t & (C::XD - 1)) * C::XROWS + 4 * lane);
-                const int r0 = unit * kRows + (TC ? 0 : hf * kHalf) + 4 * lane;
-                float4 v = *v4;
-                float *f = reinterpret_cast<float *>(&v);
+            // ---- the slice's activations, all at once: groups u0, u0 + 1, ...
+            // (mod units) into slots 0.. (item jj's group is slot jj % units) ----
+            const int u0 = (int)(i0 % units);
+            const int ngroups = nitems < units ? nitems : units; // <= XU (checked when the chain was built)
+            for (int ci = ct; ci < ngroups * 16; ci += CW * 32) {
+                const int k = ci >> 4, ch = ci & 15;
+                int unit = u0 + k;
+                if (unit >= units) unit -= units;
+                const int r0 = unit * kRows + 4 * ch;
+                const int nv = op.rows - r0;
+                const int bytes = nv >= 4 ? 16 : nv > 0 ? 4 * nv : 0;
+                cp_async16_cg(xs + k * 256 + 16 * ch, op.x + (bytes ? r0 : 0), bytes);
+            }
+            cp_async_commit();
+            cp_async_wait<0>();
+            if (norm) { // the same chunks, RMS-normalised in place by the thread that copied them
+                const double inv = *inv_s;
+                for (int ci = ct; ci < ngroups * 16; ci += CW * 32) {
+                    const int k = ci >> 4, ch = ci & 15;
+                    int unit = u0 + k;
+                    if (unit >= units) unit -= units;
+                    const int r0 = unit * kRows + 4 * ch;
+                    float4 *v4 = reinterpret_cast<float4 *>(xs + k * 256 + 16 * ch);
+                    float4 v = *v4;
+                    float *f = reinterpret_cast<float *>(&v);
 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    if (r0 + k < op.rows) f[k] = __fmul_rn((float)__dmul_rn((double)f[k], inv), __ldg(op.norm_w + r0 + k));
-                *v4 = v;
-            };
-            for (int i = 0; i < C::XD - 1; i++) issue_x();
+                    for (int q = 0; q < 4; q++)
+                        if (r0 + q < op.rows)
+                            f[q] = __fmul_rn((float)__dmul_rn((double)f[q], inv), __ldg(op.norm_w + r0 + q));
+                    *v4 = v;
+                }
+            }
+            named_sync(1, CW * 32);
+            if constexpr (TC) { // each group's digits, once, in place
+                for (int k = cw; k < ngroups; k += CW) tmv_digits_unit(xs + k * 256, lane);
+                named_sync(1, CW * 32);
+            }
 
             uint32_t ofs[8];
 #pragma unroll
@@ -440,7 +486,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
 
             // Deposits this warp's sums of segment s (not the slice's last);
             // the last warp to deposit reduces the segment in warp order and
-            // finishes or publishes its tile.
+            // finishes its tile, or hands a shared first segment to the
+            // reducer warp.
             auto deposit = [&](int s) {
                 const int sb = 2 * seg_begin(s), se = 2 * seg_begin(s + 1); // work units
                 const int len = se - sb;
@@ -480,17 +527,20 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
                     __threadfence_block();
                     ready[b] = s + 2;
                 }
-                const int tile = tile0 + s;
-                const long long t0 = (long long)tile * units;
-                if (split.owner(t0) == split.owner(t0 + units - 1))
-                    finish_tile_warp<BITS>(op, done, tile, lane, v);
-                else
-                    publish_shared_warp<BITS>(op, p, done, split, c, tile, lane, v);
+                if (s == 0 && sl.handoff) {
+                    if (nh > 0) wait_bar(hand_empty, (nh - 1) & 1, abort, p.status); // the previous handoff was taken
+#pragma unroll
+                    for (int q = 0; q < NP; q++) hand[q * 32 + lane] = v[q];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(hand_full);
+                } else {
+                    finish_tile_warp<BITS>(op, done, tile0 + s, lane, v); // a whole tile inside the slice
+                }
             };
 
             int s = 0;
             int next_sb = nseg > 1 ? seg_begin(1) : nitems;
-            for (int jj = jsub, t_it = 0; jj < nitems; jj += CWI, t_it++) {
+            for (int jj = jsub; jj < nitems; jj += CWI) {
                 while (jj >= next_sb) {
                     flush();
                     deposit(s);
@@ -499,11 +549,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
                     s++;
                     next_sb = s + 1 < nseg ? next_sb + units : nitems;
                 }
-                const int unit = (int)((i0 + jj) % units);
-                issue_x();
-                cp_async_wait<C::XD - 1>(); // this item's activations (this lane's copies) have landed
-                norm_x(t_it, unit);
-                const int k = seq_base + jj;
+                const int gi = jj / C::G;  // the item's group within the slice
+                const int k = seq_base + gi; // and its ring sequence number
                 if (*issued <= k) {
                     const unsigned long long t0 = global_ns();
                     while (*issued <= k && !*abort)
@@ -511,30 +558,35 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
                 }
                 const int slot = k % R;
                 const bool ok = wait_bar(&full[slot], (k / R) & 1, abort, p.status);
-                __syncwarp(); // every lane's activations visible to the warp
-                const uint8_t *item = ring + slot * C::SLOT;
+                const uint8_t *item = ring + slot * C::SLOT + (jj - gi * C::G) * C::ITEMB;
+                const uint8_t *grp = xs + (jj % units) * 256;
                 if constexpr (TC) {
-                    if (ok) tmv_item(item, hf, xs + (t_it & (C::XD - 1)) * kRows, smem + C::PL_OFF + cw * C::PLANES, lane, accp);
+                    if (ok) tmv_item_pre(item, hf, grp, lane, accp);
                 } else {
-                    if (ok) half_item<BITS, 1>(item, hf, xs + (t_it & (C::XD - 1)) * kHalf, ofs, mg, lane, acc);
+                    if (ok) half_item<BITS, 1>(item, hf, reinterpret_cast<const float *>(grp) + hf * kHalf, ofs, mg, lane, acc);
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
-                __syncwarp(); // the x slot is reused XD - 1 items later
+                if (lane == 0) {
+                    // a group short of G items (a slice's last) is completed by
+                    // its first item's first half for the missing items
+                    const int geff = nitems - gi * C::G < C::G ? nitems - gi * C::G : C::G;
+                    const int n = (jj == gi * C::G && hf == 0) ? 1 + 2 * (C::G - geff) : 1;
+                    mbar_arrive_cnt(&empty[slot], n);
+                }
             }
-            cp_async_wait<0>();
             flush();
             for (; s < nseg - 1; s++) {
                 deposit(s);
 #pragma unroll
                 for (int q = 0; q < NP; q++) acc[0][q] = 0.f;
             }
+            if (sl.handoff) nh++;
             // ---- the slice's last segment, by all consumer threads ----
             {
-                const int sl = nseg - 1, b = sl & 1;
-                if (ready[b] < sl) {
+                const int sg = nseg - 1, b = sg & 1;
+                if (ready[b] < sg) {
                     const unsigned long long t0 = global_ns();
-                    while (ready[b] < sl && !*abort)
+                    while (ready[b] < sg && !*abort)
                         if (global_ns() - t0 > kWaitNs) chain_abort(p, abort, true);
                 }
                 float *rb = red + (size_t)(b * CW + cw) * E + lane;
@@ -549,20 +601,19 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
                     for (int w = 0; w < CW; w++) v += red[(size_t)(b * CW + w) * E + e];
                     return v;
                 };
-                // the tile's sum of squares over the consumer threads, in a fixed order
+                // the tile's sum of squares over the consumer threads in a fixed
+                // order, then one cumulative release of the tile count
                 auto finish_all = [&](double ss) {
                     if (op.ss_out) {
                         ss = warp_sum_d(ss);
                         if (lane == 0) ssred[cw] = ss;
                     }
-                    fence_gpu();
                     named_sync(1, CW * 32);
                     if (ct == 0) {
                         if (op.ss_out) {
                             double t = 0.0;
                             for (int w = 0; w < CW; w++) t = __dadd_rn(t, ssred[w]);
                             op.ss_out[tile] = t;
-                            fence_gpu();
                         }
                         red_release(done, 1u);
                     }
@@ -612,7 +663,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
                     }
                 }
             }
-            seq_base += nitems;
+            seq_base += (nitems + C::G - 1) / C::G;
         }
     }
     __syncthreads();
@@ -635,6 +686,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(ChainParams p) 
 
 // ---- host side ------------------------------------------------------------------
 
+// 64-row groups the busiest CTA's slice of m touches (one CTA per SM, at most
+// one per item): what the kernel stages per op.
+static int chain_groups(const TqMatrixDev &m, int sms) {
+    const long long items = (long long)m.tiles * m.units;
+    const long long ctas = items < sms ? items : sms;
+    const long long per = (items + ctas - 1) / ctas;
+    return (int)(per < m.units ? per : m.units);
+}
+
 struct TqChain {
     int device = 0;
     int bits = 0;
@@ -653,6 +713,11 @@ cudaError_t tq_chain_build(const TqChainSpec *spec, int n, TqChain **out, int *w
         *why = TQ_CHAIN_BAD_COUNT;
         return cudaErrorInvalidValue;
     }
+    int device = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess && (sms < 1 || sms > TQ_MAX_CTAS)) e = cudaErrorInvalidValue;
+    if (e != cudaSuccess) return e;
     const int bits = spec[0].m->bits;
     for (int j = 0; j < n; j++) {
         const TqChainSpec &s = spec[j];
@@ -660,12 +725,13 @@ cudaError_t tq_chain_build(const TqChainSpec *spec, int n, TqChain **out, int *w
         int bad = TQ_CHAIN_OK;
         if (m.bits != bits) bad = TQ_CHAIN_MIXED_BITS;
         else if (m.rows < 1 || m.cols < 1) bad = TQ_CHAIN_EMPTY;
-        else if (bits == 4 && (!m.kcodes || !m.kscale)) bad = TQ_CHAIN_NO_KPACK;
+        else if (bits == 4 && !m.kpack) bad = TQ_CHAIN_NO_KPACK;
         else if (!s.x || !s.out || ((uintptr_t)s.x & 15)) bad = TQ_CHAIN_X_ALIGN;
         else if (s.epi != TQ_EPI_NONE && s.epi != TQ_EPI_SWIGLU && s.epi != TQ_EPI_RESID) bad = TQ_CHAIN_EPI;
         else if (s.epi == TQ_EPI_SWIGLU && (bits != 4 || m.cols % 2)) bad = TQ_CHAIN_EPI;
         else if (s.epi == TQ_EPI_RESID && !s.resid) bad = TQ_CHAIN_EPI;
         else if (m.tiles > TQ_MAX_TILES) bad = TQ_CHAIN_TOO_WIDE;
+        else if (chain_groups(m, sms) > TQ_CHAIN_MAX_GROUPS) bad = TQ_CHAIN_TOO_DEEP;
         else if (s.norm_w) {
             const int f = s.norm_from;
             if (f < 0 || f >= j || spec[f].epi != TQ_EPI_RESID || spec[f].out != s.x || spec[f].m->cols != m.rows)
@@ -678,14 +744,7 @@ cudaError_t tq_chain_build(const TqChainSpec *spec, int n, TqChain **out, int *w
         }
     }
     TqChain *ch = new TqChain();
-    cudaError_t e = cudaGetDevice(&ch->device);
-    int sms = 0;
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ch->device);
-    if (e == cudaSuccess && (sms < 1 || sms > TQ_MAX_CTAS)) e = cudaErrorInvalidValue;
-    if (e != cudaSuccess) {
-        delete ch;
-        return e;
-    }
+    ch->device = device;
     // sums of squares: one double per column tile of every op a later op normalises
     std::vector<size_t> ss_off(n, 0);
     size_t ss_doubles = 0;
@@ -716,8 +775,8 @@ cudaError_t tq_chain_build(const TqChainSpec *spec, int n, TqChain **out, int *w
         const TqMatrixDev &m = *s.m;
         ChainOp &o = h[j];
         std::memset(&o, 0, sizeof o);
-        o.codes = bits == 4 ? m.kcodes : m.codes;
-        o.scale = bits == 4 ? m.kscale : m.scale;
+        o.codes = bits == 4 ? m.kpack : m.codes;
+        o.scale = bits == 4 ? nullptr : m.scale;
         o.x = s.x;
         o.out = s.out;
         o.resid = s.epi == TQ_EPI_RESID ? s.resid : nullptr;

@@ -290,8 +290,12 @@ __global__ void __launch_bounds__(kThreads, TC ? 1 : 2) cmv_kernel(CmvParams p) 
                 const long long it = i0 + j;
                 uint8_t *dst = smem + C::RING_OFF + s * C::SLOT;
                 mbar_arrive_expect_tx(&full[s], C::SLOT);
-                bulk_load(dst, p.codes + it * kItem, kItem, &full[s]);
-                if (BITS == 4) bulk_load(dst + kItem, p.scale + it * (2 * kCols), 1024, &full[s]);
+                if (TC) { // one K-packed item: codes then scales, contiguous
+                    bulk_load(dst, p.codes + it * TQ_KPACK_BYTES, TQ_KPACK_BYTES, &full[s]);
+                } else {
+                    bulk_load(dst, p.codes + it * kItem, kItem, &full[s]);
+                    if (BITS == 4) bulk_load(dst + kItem, p.scale + it * (2 * kCols), 1024, &full[s]);
+                }
                 *issued = j + 1;
             }
         }
@@ -685,8 +689,12 @@ __global__ void __launch_bounds__(kKThreads, TC ? 1 : 2) kcmv_kernel(CmvParams p
                 const long long it = i0 + j;
                 uint8_t *dst = smem + C::RING_OFF + s * C::SLOT;
                 mbar_arrive_expect_tx(&full[s], C::SLOT);
-                bulk_load(dst, p.codes + it * kItem, kItem, &full[s]);
-                if (BITS == 4) bulk_load(dst + kItem, p.scale + it * (2 * kCols), 1024, &full[s]);
+                if (TC) { // one K-packed item: codes then scales, contiguous
+                    bulk_load(dst, p.codes + it * TQ_KPACK_BYTES, TQ_KPACK_BYTES, &full[s]);
+                } else {
+                    bulk_load(dst, p.codes + it * kItem, kItem, &full[s]);
+                    if (BITS == 4) bulk_load(dst + kItem, p.scale + it * (2 * kCols), 1024, &full[s]);
+                }
                 *issued = j + 1;
             }
         }
@@ -810,20 +818,19 @@ cudaError_t launch_kcmv(const TqMatrixDev &mat, const float *x, float *out, cons
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    static int configured[64] = {};
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
-        e = cudaFuncSetAttribute(kcmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return e;
+    static TqDeviceOnce once;
+    e = tq_device_once(once, dev, [] {
+        cudaError_t r = cudaFuncSetAttribute(kcmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if constexpr (kHasTc) {
-            e = cudaFuncSetAttribute(kcmv_kernel<4, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
-            if (e != cudaSuccess) return e;
+            if (r == cudaSuccess)
+                r = cudaFuncSetAttribute(kcmv_kernel<4, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
         }
-        configured[dev] = 1;
-    }
+        return r;
+    });
+    if (e != cudaSuccess) return e;
     CmvParams prm = {};
-    prm.codes = tc ? mat.kcodes : mat.codes;
-    prm.scale = tc ? mat.kscale : mat.scale;
+    prm.codes = tc ? mat.kpack : mat.codes;
+    prm.scale = tc ? nullptr : mat.scale;
     prm.x = x;
     prm.out = out;
     prm.status = scr.status;
@@ -894,27 +901,23 @@ cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const
     using C = CCfg<BITS, M>;
     constexpr bool kHasTc = BITS == 4 && M == 1;
     using CT = CCfg<4, 1, true>;
-    tc = tc && kHasTc && mat.kcodes && mat.kscale;
+    tc = tc && kHasTc && mat.kpack;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    static int configured[64] = {};
-    static int sm_count[64] = {};
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
-        e = cudaFuncSetAttribute(cmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return e;
+    static TqDeviceOnce once;
+    e = tq_device_once(once, dev, [] {
+        cudaError_t r = cudaFuncSetAttribute(cmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if constexpr (kHasTc) {
-            e = cudaFuncSetAttribute(cmv_kernel<4, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
-            if (e != cudaSuccess) return e;
+            if (r == cudaSuccess)
+                r = cudaFuncSetAttribute(cmv_kernel<4, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
         }
-        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        configured[dev] = 1;
-    }
+        return r;
+    });
+    if (e != cudaSuccess) return e;
     CmvParams prm = {};
-    prm.codes = tc ? mat.kcodes : mat.codes;
-    prm.scale = tc ? mat.kscale : mat.scale;
+    prm.codes = tc ? mat.kpack : mat.codes;
+    prm.scale = tc ? nullptr : mat.scale;
     prm.x = x;
     prm.out = out;
     prm.partial = scr.partial;
@@ -928,7 +931,7 @@ cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const
     prm.items = (long long)mat.tiles * mat.units;
     prm.magic = 0x4B000000u;
     prm.epi = epi;
-    const int sms = sm_count[dev];
+    const int sms = once.sms[dev];
     if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS) return cudaErrorInvalidValue;
     if (const int k = tc ? cluster_split_tc(mat, sms) : cluster_split(mat, sms))
         return launch_kcmv<BITS, M>(mat, x, out, scr, st, k, epi, tc);
@@ -957,10 +960,10 @@ cudaError_t launch_cmv(const TqMatrixDev &mat, const float *x, float *out, const
 TQ_HD int tmv_col(int hf, int cb, int rho) { return 128 * hf + 4 * (4 * (rho & 7) + (cb & 3)) + 2 * (cb >> 2) + (rho >> 3); }
 
 // The K-packed copy of an int4 matrix (see the tensor-core variant above):
-// one thread per 4-byte word of kcodes (8 codes of one item column), then one
-// per kscale float.
+// one thread per 4-byte word of an item's K-packed codes (8 codes of one item
+// column), then one per scale float; item it occupies kpack[it * TQ_KPACK_BYTES ..].
 __global__ void repack4_kernel(const uint8_t *__restrict__ codes, const float *__restrict__ scale,
-                               uint8_t *__restrict__ kcodes, float *__restrict__ kscale, long long items) {
+                               uint8_t *__restrict__ kpack, long long items) {
     const long long words = items * (kItem / 4), stride = (long long)gridDim.x * blockDim.x;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < words; i += stride) {
         const long long it = i / (kItem / 4);
@@ -975,33 +978,34 @@ __global__ void repack4_kernel(const uint8_t *__restrict__ codes, const float *_
             const uint32_t byte = src[tq_item_offset(8 * kb + r, b)];
             w |= (hi ? byte >> 4 : byte & 15u) << (4 * r);
         }
-        reinterpret_cast<uint32_t *>(kcodes + it * kItem)[wi] = w;
+        reinterpret_cast<uint32_t *>(kpack + it * TQ_KPACK_BYTES)[wi] = w;
     }
     const long long nsc = items * 256;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nsc; i += stride) {
         const long long it = i / 256;
         const int ks = (int)(i % 256);
         const int hf = ks >> 7, tq = (ks >> 5) & 3, g = (ks >> 2) & 7, e = ks & 3;
-        kscale[i] = scale[it * 256 + tmv_col(hf, tq + 4 * (e >> 1), g + 8 * (e & 1))];
+        reinterpret_cast<float *>(kpack + it * TQ_KPACK_BYTES + kItem)[ks] =
+            scale[it * 256 + tmv_col(hf, tq + 4 * (e >> 1), g + 8 * (e & 1))];
     }
 }
 
 } // namespace
 
 cudaError_t tq_launch_repack4(const TqMatrixDev &m, cudaStream_t st) {
-    if (m.bits != 4 || !m.kcodes || !m.kscale) return cudaSuccess;
+    if (m.bits != 4 || !m.kpack) return cudaSuccess;
     const long long items = (long long)m.tiles * m.units;
     if (items == 0) return cudaSuccess;
     const long long words = items * (kItem / 4);
     const unsigned grid = (unsigned)(words / 256 < 148 * 8 ? (words + 255) / 256 : 148 * 8);
-    repack4_kernel<<<grid, 256, 0, st>>>(m.codes, m.scale, m.kcodes, m.kscale, items);
+    repack4_kernel<<<grid, 256, 0, st>>>(m.codes, m.scale, m.kpack, items);
     return cudaGetLastError();
 }
 
 // int4, one row per launch, on the tensor cores (the K-packed copy).
 cudaError_t tq_launch_tmv(const TqMatrixDev &mat, const float *x, float *out, int M, const TqScratch &scr,
                           cudaStream_t st) {
-    if (mat.bits != 4 || !mat.kcodes) return tq_launch_cmv(mat, x, out, M, scr, st);
+    if (mat.bits != 4 || !mat.kpack) return tq_launch_cmv(mat, x, out, M, scr, st);
     if (M <= 0 || mat.cols == 0) return cudaSuccess;
     if (mat.rows == 0) return cudaMemsetAsync(out, 0, sizeof(float) * (size_t)M * mat.cols, st);
     for (int m0 = 0; m0 < M; m0++) {

@@ -26,9 +26,12 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #define TQ_GROUP 64        // rows per int4 scale group (q4Group, quant4.go:12)
 #define TQ_TILE_BYTES 128  // bytes of a code row per item
 #define TQ_ITEM_BYTES (TQ_TILE_BYTES * TQ_GROUP)
+#define TQ_KPACK_BYTES (TQ_ITEM_BYTES + 1024) // a K-packed int4 item: codes, then 256 float scales
 #define TQ_MAX_TILES 8192  // rowBytes <= 1 MiB
 #define TQ_MAX_CTAS 256    // persistent matvec grid <= 256 CTAs
 #define TQ_STATUS_TIMEOUT 1u // a kernel gave up waiting on an mbarrier
@@ -50,6 +53,24 @@ struct TqScratch {
 // Two partial slots per CTA of up to 2 runs x 128 rows x 128 columns.
 static inline size_t tq_mm_partial_floats(int sms) { return (size_t)2 * sms * 2 * TQ_MM_MAX_ROWS * TQ_TILE_BYTES; }
 
+// One-time set-up of a kernel launcher on each device (kernel attributes, SM
+// count), safe when several host threads launch at once: the first caller on
+// a device runs it, concurrent callers wait for it, later calls read the
+// cached result. Devices 0..63.
+struct TqDeviceOnce {
+    std::once_flag flag[64];
+    cudaError_t err[64] = {};
+    int sms[64] = {};
+};
+template <class F> inline cudaError_t tq_device_once(TqDeviceOnce &o, int dev, F &&setup) {
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::call_once(o.flag[dev], [&] {
+        cudaError_t e = cudaDeviceGetAttribute(&o.sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        o.err[dev] = e == cudaSuccess ? setup() : e;
+    });
+    return o.err[dev];
+}
+
 struct TqMatrixDev {
     int bits;       // 8 or 4
     int rows;       // K
@@ -58,8 +79,11 @@ struct TqMatrixDev {
     int units;      // ceil(rows/64) (= scale groups for int4)
     uint8_t *codes; // tiles*units*8192 bytes, tiled (see above)
     float *scale;   // see above
-    uint8_t *kcodes; // int4: the same codes K-packed for the tensor-core matvec (tq_cmv.cu), or null
-    float *kscale;   // int4: the scales in that matvec's per-item order, or null
+    // int4: the same items K-packed for the tensor-core matvecs (tq_cmv.cu,
+    // tq_chain.cu), TQ_KPACK_BYTES each: 8 KB of codes then the item's 256
+    // scales in that kernel's order, so that one bulk copy moves an item and
+    // consecutive items are one contiguous range. Null for int8.
+    uint8_t *kpack;
 };
 
 #ifdef __CUDACC__
@@ -163,9 +187,6 @@ cudaError_t tq_launch_tmv(const TqMatrixDev &m, const float *x, float *out, int 
 cudaError_t tq_launch_repack4(const TqMatrixDev &m, cudaStream_t st);
 cudaError_t tq_launch_igemv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                             cudaStream_t st);
-// Single-launch tensor-core matvec for M <= 8 rows per launch (tq_gemv.cu).
-cudaError_t tq_launch_gemv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
-                           cudaStream_t st);
 // CUDA-core matvec for M <= 2 rows per launch (tq_cmv.cu).
 cudaError_t tq_launch_cmv(const TqMatrixDev &m, const float *x, float *out, int M, const TqScratch &scr,
                           cudaStream_t st);
@@ -179,6 +200,9 @@ enum { TQ_FIXED_OK = 0, TQ_FIXED_CUDA, TQ_FIXED_DEVICE, TQ_FIXED_SMS, TQ_FIXED_T
 #define TQ_FIXED_ROWS_PER_LAUNCH 4
 int tq_launch_matvec_fixed(const TqMatrixDev &m, const float *x, float *out, int M, cudaStream_t st,
                            cudaError_t *err);
+// Status bits of the fixed scratch on the current device (device idle); when
+// set, the fixed counters are re-armed.
+cudaError_t tq_fixed_status(unsigned *bits);
 
 // A chain of dependent single-row matvecs in one persistent launch
 // (tq_chain.cu). Op j reads its input only after op j - 1 has written all of
@@ -186,6 +210,9 @@ int tq_launch_matvec_fixed(const TqMatrixDev &m, const float *x, float *out, int
 // norm_w != null: x (the output of op norm_from, a TQ_EPI_RESID op earlier in
 // the chain) is RMS-normalised with weight norm_w and epsilon eps first.
 #define TQ_CHAIN_MAX_OPS 4096
+// 64-row groups of activations a CTA stages per op: an op whose per-CTA slice
+// (items / SMs, rounded up) covers more distinct groups is not chainable.
+#define TQ_CHAIN_MAX_GROUPS 64
 struct TqChainSpec {
     const TqMatrixDev *m;
     const float *x;
@@ -207,6 +234,7 @@ enum {
     TQ_CHAIN_EPI,        // an unknown epilogue or one the matrix cannot take
     TQ_CHAIN_TOO_WIDE,   // more than TQ_MAX_TILES column tiles
     TQ_CHAIN_NORM,       // a normalised input that is not an earlier residual op's output
+    TQ_CHAIN_TOO_DEEP,   // a per-CTA slice covering more than TQ_CHAIN_MAX_GROUPS row groups
 };
 // Validates the ops and copies their descriptors to the current device
 // (synchronous); *why names the first problem found and *bad_op its op.

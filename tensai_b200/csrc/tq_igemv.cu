@@ -664,16 +664,11 @@ cudaError_t launch_ig(const TqMatrixDev &mat, const float *x, float *out, const 
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    static int configured[64] = {};
-    static int sm_count[64] = {};
-    if (dev >= 64) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
-        e = cudaFuncSetAttribute(igemv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return e;
-        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        configured[dev] = 1;
-    }
+    static TqDeviceOnce once;
+    e = tq_device_once(once, dev, [] {
+        return cudaFuncSetAttribute(igemv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    });
+    if (e != cudaSuccess) return e;
     IgParams prm;
     prm.codes = mat.codes;
     prm.scale = mat.scale;
@@ -688,7 +683,7 @@ cudaError_t launch_ig(const TqMatrixDev &mat, const float *x, float *out, const 
     prm.units = mat.units;
     prm.tiles = mat.tiles;
     prm.items = (long long)mat.tiles * mat.units;
-    const int sms = sm_count[dev];
+    const int sms = once.sms[dev];
     if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS) return cudaErrorInvalidValue;
     if ((size_t)mat.units * (Planes<M>::BBYTES + Planes<M>::MB) > TQ_SCRATCH_PLANES_BYTES) return cudaErrorInvalidValue;
     const int ctas = (int)(prm.items < sms ? prm.items : sms);

@@ -173,44 +173,13 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// One 64-row item, item columns of half hf, into this lane's partial sums
-// accp[cb][rh] (MMA rows g + 8 rh of block cb). xr: the group's 64
-// activations; pl: this warp's 192 bytes of digit planes.
-__device__ __forceinline__ void tmv_item(const uint8_t *item, int hf, const float *xr, uint8_t *pl, int lane,
-                                         float (&accp)[8][2]) {
-    const int g = lane >> 2, t = lane & 3;
-    const float2 xv = *reinterpret_cast<const float2 *>(xr + 2 * lane); // rows 2l, 2l + 1
-    const uint32_t ax = max(__float_as_uint(xv.x) & 0x7FFFFFFFu, __float_as_uint(xv.y) & 0x7FFFFFFFu);
-    uint32_t amax;
-    asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(amax) : "r"(ax));
-    // |x| < 2^(e - 126) for the largest biased exponent e: 2^s with s = 148 - e
-    // keeps |X| <= 2^22 (s at most 126 so that 2^-s is a normal float)
-    int sh = 148 - (int)(amax >> 23);
-    sh = sh > 126 ? 126 : sh;
-    const float up = __uint_as_float((uint32_t)(127 + sh) << 23), dn = __uint_as_float((uint32_t)(127 - sh) << 23);
-    const int X0 = __float2int_rn(xv.x * up), X1 = __float2int_rn(xv.y * up);
-    int sx;
-    asm volatile("redux.sync.add.s32 %0, %1, 0xffffffff;" : "=r"(sx) : "r"(X0 + X1));
-    const uint32_t dg0 = (uint32_t)(X0 + 0x808080) ^ 0x808080u, dg1 = (uint32_t)(X1 + 0x808080) ^ 0x808080u;
-    uint16_t *pl16 = reinterpret_cast<uint16_t *>(pl);
-    pl16[lane] = (uint16_t)__byte_perm(dg0, dg1, 0x0040); // plane p, bytes 2l, 2l + 1
-    pl16[32 + lane] = (uint16_t)__byte_perm(dg0, dg1, 0x0051);
-    pl16[64 + lane] = (uint16_t)__byte_perm(dg0, dg1, 0x0062);
-    __syncwarp();
-    uint32_t be0 = 0, bo0 = 0, be1 = 0, bo1 = 0; // B: digit g at even / odd rows of the two 32-row halves
-    if (g < 3) {
-        const uint2 q0 = *reinterpret_cast<const uint2 *>(pl + g * 64 + 8 * t);
-        const uint2 q1 = *reinterpret_cast<const uint2 *>(pl + g * 64 + 32 + 8 * t);
-        be0 = __byte_perm(q0.x, q0.y, 0x6420);
-        bo0 = __byte_perm(q0.x, q0.y, 0x7531);
-        be1 = __byte_perm(q1.x, q1.y, 0x6420);
-        bo1 = __byte_perm(q1.x, q1.y, 0x7531);
-    }
-    __syncwarp(); // the planes are read before the next item writes them
-    const float K = t == 0 ? dn : t == 1 ? dn * 65536.f : 0.f;
-    // a NaN or infinity in the group has no digits: its columns become NaN,
-    // as the float products would make them
-    const float O = amax >= 0x7F800000u ? __uint_as_float(0x7FC00000u) : t == 1 ? -8.f * (float)sx * dn : 0.f;
+// The MMA part of one 64-row item, item columns of half hf, into this lane's
+// partial sums accp[cb][rh] (MMA rows g + 8 rh of block cb): B fragments be0,
+// bo0 (digit g at the even / odd rows of the first 32-row half), be1, bo1 (the
+// second half), and the lane's K and O of the group fold (see below).
+__device__ __forceinline__ void tmv_mma(const uint8_t *item, int hf, uint32_t be0, uint32_t bo0, uint32_t be1,
+                                        uint32_t bo1, float K, float O, int lane, float (&accp)[8][2]) {
+    const int g = lane >> 2;
     const uint8_t *cw = item + hf * (kItem / 2) + lane * 16;
     const float *scl = reinterpret_cast<const float *>(item + kItem) + hf * 128 + g * 4;
     float4 sc[4];
@@ -240,6 +209,99 @@ __device__ __forceinline__ void tmv_item(const uint8_t *item, int hf, const floa
         accp[cb][0] = fmaf(vg, cb < 4 ? s4.x : s4.z, accp[cb][0]);
         accp[cb][1] = fmaf(vg8, cb < 4 ? s4.y : s4.w, accp[cb][1]);
     }
+}
+
+// The group's activation digits, by one warp: lane l holds rows 2l, 2l + 1
+// (xv). X = round(x 2^s) with 2^s from the group's largest |x| (|X| <= 2^22)
+// is cut into three signed byte digits (bytes of X + 0x808080, each xor 0x80),
+// written as planes [3][64] bytes at pl. K0 = 2^-s, K1 = 2^(16-s) and
+// O1 = -8 sum(X) 2^-s are the fold constants of lanes t = 0 and 1; O1 is NaN
+// for a group holding a NaN or an infinity, which has no digits (its
+// columns become NaN).
+__device__ __forceinline__ void tmv_digits(float2 xv, uint8_t *pl, int lane, float &K0, float &K1, float &O1) {
+    const uint32_t ax = max(__float_as_uint(xv.x) & 0x7FFFFFFFu, __float_as_uint(xv.y) & 0x7FFFFFFFu);
+    uint32_t amax;
+    asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(amax) : "r"(ax));
+    // |x| < 2^(e - 126) for the largest biased exponent e: 2^s with s = 148 - e
+    // keeps |X| <= 2^22 (s at most 126 so that 2^-s is a normal float)
+    int sh = 148 - (int)(amax >> 23);
+    sh = sh > 126 ? 126 : sh;
+    const float up = __uint_as_float((uint32_t)(127 + sh) << 23), dn = __uint_as_float((uint32_t)(127 - sh) << 23);
+    const int X0 = __float2int_rn(xv.x * up), X1 = __float2int_rn(xv.y * up);
+    int sx;
+    asm volatile("redux.sync.add.s32 %0, %1, 0xffffffff;" : "=r"(sx) : "r"(X0 + X1));
+    const uint32_t dg0 = (uint32_t)(X0 + 0x808080) ^ 0x808080u, dg1 = (uint32_t)(X1 + 0x808080) ^ 0x808080u;
+    uint16_t *pl16 = reinterpret_cast<uint16_t *>(pl);
+    pl16[lane] = (uint16_t)__byte_perm(dg0, dg1, 0x0040); // plane p, bytes 2l, 2l + 1
+    pl16[32 + lane] = (uint16_t)__byte_perm(dg0, dg1, 0x0051);
+    pl16[64 + lane] = (uint16_t)__byte_perm(dg0, dg1, 0x0062);
+    K0 = dn;
+    K1 = dn * 65536.f;
+    O1 = amax >= 0x7F800000u ? __uint_as_float(0x7FC00000u) : -8.f * (float)sx * dn;
+}
+
+// The B fragments of lane (g, t) from a group's digit planes.
+__device__ __forceinline__ void tmv_bfrag(const uint8_t *pl, int lane, uint32_t &be0, uint32_t &bo0, uint32_t &be1,
+                                          uint32_t &bo1) {
+    const int g = lane >> 2, t = lane & 3;
+    be0 = bo0 = be1 = bo1 = 0;
+    if (g < 3) {
+        const uint2 q0 = *reinterpret_cast<const uint2 *>(pl + g * 64 + 8 * t);
+        const uint2 q1 = *reinterpret_cast<const uint2 *>(pl + g * 64 + 32 + 8 * t);
+        be0 = __byte_perm(q0.x, q0.y, 0x6420);
+        bo0 = __byte_perm(q0.x, q0.y, 0x7531);
+        be1 = __byte_perm(q1.x, q1.y, 0x6420);
+        bo1 = __byte_perm(q1.x, q1.y, 0x7531);
+    }
+}
+
+// Lane t's K and O of the group fold: the D fragment holds, in lane t = 0,
+// sum n*d0 and sum n*d1 (n the unsigned code) and in lane t = 1 sum n*d2, so
+// lane t adds scale * ((D_a + 256 D_b) * K_t + O_t) with K_0 = 2^-s,
+// K_1 = 2^(16-s), O_1 = -8 * sum(X) * 2^-s (the code offset 8), K and O zero
+// for t >= 2; O is NaN for every lane of a non-finite group.
+__device__ __forceinline__ void tmv_fold(int lane, float K0, float K1, float O1, float &K, float &O) {
+    const int t = lane & 3;
+    K = t == 0 ? K0 : t == 1 ? K1 : 0.f;
+    O = (t == 1 || O1 != O1) ? O1 : 0.f;
+}
+
+// One 64-row item, item columns of half hf, into this lane's partial sums
+// accp[cb][rh]. xr: the group's 64 activations; pl: this warp's 192 bytes of
+// digit planes.
+__device__ __forceinline__ void tmv_item(const uint8_t *item, int hf, const float *xr, uint8_t *pl, int lane,
+                                         float (&accp)[8][2]) {
+    float K0, K1, O1;
+    tmv_digits(*reinterpret_cast<const float2 *>(xr + 2 * lane), pl, lane, K0, K1, O1); // rows 2l, 2l + 1
+    __syncwarp();
+    uint32_t be0, bo0, be1, bo1;
+    tmv_bfrag(pl, lane, be0, bo0, be1, bo1);
+    __syncwarp(); // the planes are read before the next item writes them
+    float K, O;
+    tmv_fold(lane, K0, K1, O1, K, O);
+    tmv_mma(item, hf, be0, bo0, be1, bo1, K, O, lane, accp);
+}
+
+// A group's digits prepared once in shared memory (unit slot u: planes
+// [3][64] bytes, then float4 {K0, K1, O1, 0} at byte 192): the digits of the
+// 64 floats at u, written over them in place, by one warp.
+__device__ __forceinline__ void tmv_digits_unit(uint8_t *u, int lane) {
+    const float2 xv = *reinterpret_cast<const float2 *>(reinterpret_cast<const float *>(u) + 2 * lane);
+    __syncwarp(); // every lane has its activations before the planes overwrite them
+    float K0, K1, O1;
+    tmv_digits(xv, u, lane, K0, K1, O1);
+    if (lane == 0) *reinterpret_cast<float4 *>(u + 192) = make_float4(K0, K1, O1, 0.f);
+}
+
+// One 64-row item with its group's digits prepared in unit slot u.
+__device__ __forceinline__ void tmv_item_pre(const uint8_t *item, int hf, const uint8_t *u, int lane,
+                                             float (&accp)[8][2]) {
+    uint32_t be0, bo0, be1, bo1;
+    tmv_bfrag(u, lane, be0, bo0, be1, bo1);
+    const float4 kc = *reinterpret_cast<const float4 *>(u + 192);
+    float K, O;
+    tmv_fold(lane, kc.x, kc.y, kc.z, K, O);
+    tmv_mma(item, hf, be0, bo0, be1, bo1, K, O, lane, accp);
 }
 
 // The lane's partial sums accp (all lanes of a quad hold parts of the same

@@ -390,23 +390,23 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_kernel(QmvParams p) {
     cp_async_wait<0>();
 }
 
+// Per-device set-up of qmv_kernel<BITS, M>: its shared-memory attribute, which
+// also loads the kernel's code onto the device.
+template <int BITS, int M> TqDeviceOnce g_qmv_once;
+template <int BITS, int M> cudaError_t qmv_setup(int dev) {
+    using S = Smem<BITS, M>;
+    return tq_device_once(g_qmv_once<BITS, M>, dev, [] {
+        return cudaFuncSetAttribute(qmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total);
+    });
+}
+
 template <int BITS, int M>
 cudaError_t launch_qmv(const TqMatrixDev &mat, const float *x, float *out, const TqScratch &scr, cudaStream_t st) {
-    using S = Smem<BITS, M>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    static int configured[64] = {};
-    static int sm_count[64] = {};
-    if (dev >= 64) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
-        e = cudaFuncSetAttribute(qmv_kernel<BITS, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total);
-        if (e != cudaSuccess) return e;
-        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        configured[dev] = 1;
-    }
-    const int sms = sm_count[dev];
+    if ((e = qmv_setup<BITS, M>(dev)) != cudaSuccess) return e;
+    const int sms = g_qmv_once<BITS, M>.sms[dev];
     QmvParams prm;
     prm.codes = mat.codes;
     prm.scale = mat.scale;
@@ -423,7 +423,7 @@ cudaError_t launch_qmv(const TqMatrixDev &mat, const float *x, float *out, const
     prm.items = (long long)prm.tiles * prm.units;
     if (prm.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS) return cudaErrorInvalidValue;
     const int ctas = (int)(prm.items < sms ? prm.items : sms);
-    qmv_kernel<BITS, M><<<ctas, kThreads, S::total, st>>>(prm);
+    qmv_kernel<BITS, M><<<ctas, kThreads, Smem<BITS, M>::total, st>>>(prm);
     return cudaGetLastError();
 }
 
@@ -490,12 +490,24 @@ struct FixedScratch {
 FixedScratch g_fixed[64];
 std::mutex g_fixed_mu;
 
+// Loads and configures every kernel the fixed path can launch (int8 and int4,
+// 1..kFixedRows rows), so that no later call loads code onto the device.
+cudaError_t fixed_kernels_setup(int dev) {
+    const cudaError_t es[] = {qmv_setup<8, 1>(dev), qmv_setup<8, 2>(dev), qmv_setup<8, 3>(dev), qmv_setup<8, 4>(dev),
+                              qmv_setup<4, 1>(dev), qmv_setup<4, 2>(dev), qmv_setup<4, 3>(dev), qmv_setup<4, 4>(dev)};
+    static_assert(kFixedRows == 4, "one set-up per row count");
+    for (cudaError_t e : es)
+        if (e != cudaSuccess) return e;
+    return cudaSuccess;
+}
+
 } // namespace
 
 // Launches out = x @ W for M rows with the fixed scratch. Set-up runs once per
 // device, with that device current: the symbol addresses of the fixed arrays
-// (cudaGetSymbolAddress) and the SM count. Returns TQ_FIXED_OK or the limit
-// that was exceeded; *err holds a CUDA error for TQ_FIXED_CUDA.
+// (cudaGetSymbolAddress), the SM count, and the kernels' code and attributes.
+// Returns TQ_FIXED_OK or the limit that was exceeded; *err holds a CUDA error
+// for TQ_FIXED_CUDA.
 int tq_launch_matvec_fixed(const TqMatrixDev &mat, const float *x, float *out, int M, cudaStream_t st,
                            cudaError_t *err) {
     *err = cudaSuccess;
@@ -512,6 +524,7 @@ int tq_launch_matvec_fixed(const TqMatrixDev &mat, const float *x, float *out, i
             if ((*err = cudaGetSymbolAddress(&words, g_fixed_words)) != cudaSuccess) return TQ_FIXED_CUDA;
             if ((*err = cudaDeviceGetAttribute(&f.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
                 return TQ_FIXED_CUDA;
+            if ((*err = fixed_kernels_setup(dev)) != cudaSuccess) return TQ_FIXED_CUDA;
             f.scr.partial = static_cast<float *>(partial);
             f.scr.counters = static_cast<unsigned *>(words);
             f.scr.status = static_cast<unsigned *>(words) + kFixedTiles;
@@ -536,4 +549,21 @@ int tq_launch_matvec_fixed(const TqMatrixDev &mat, const float *x, float *out, i
         if (*err != cudaSuccess) return TQ_FIXED_CUDA;
     }
     return TQ_FIXED_OK;
+}
+
+// The fixed scratch's status bits on the current device (0 before its first
+// call), with the device idle. A timeout may have left tile counters
+// mid-count, so when the status is set the counters and the status word are
+// zeroed again (plain memsets of the fixed array; nothing is allocated).
+cudaError_t tq_fixed_status(unsigned *bits) {
+    *bits = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) return e;
+    std::lock_guard<std::mutex> lk(g_fixed_mu);
+    const FixedScratch &f = g_fixed[dev];
+    if (!f.ready) return cudaSuccess;
+    if ((e = cudaMemcpy(bits, f.scr.status, sizeof *bits, cudaMemcpyDeviceToHost)) != cudaSuccess) return e;
+    if (*bits) e = cudaMemset(f.scr.counters, 0, sizeof(unsigned) * (kFixedTiles + 32));
+    return e;
 }

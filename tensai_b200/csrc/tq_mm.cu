@@ -441,16 +441,11 @@ cudaError_t launch_mm(const TqMatrixDev &mat, const float *x, float *out, int M,
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    static int configured[64] = {};
-    static int sm_count[64] = {};
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
-        e = cudaFuncSetAttribute(mm_kernel<BITS, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return e;
-        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        configured[dev] = 1;
-    }
+    static TqDeviceOnce once;
+    e = tq_device_once(once, dev, [] {
+        return cudaFuncSetAttribute(mm_kernel<BITS, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    });
+    if (e != cudaSuccess) return e;
     MmParams prm;
     prm.codes = mat.codes;
     prm.scale = mat.scale;
@@ -466,7 +461,7 @@ cudaError_t launch_mm(const TqMatrixDev &mat, const float *x, float *out, int M,
     prm.m = M;
     prm.xvec = (mat.rows % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     prm.items = (long long)mat.tiles * mat.units;
-    const int sms = sm_count[dev];
+    const int sms = once.sms[dev];
     if (mat.tiles > TQ_MAX_TILES || sms > TQ_MAX_CTAS || !scr.mm_partial) return cudaErrorInvalidValue;
     const int ctas = (int)(prm.items < sms ? prm.items : sms);
     mm_kernel<BITS, NP><<<ctas, kThreads, C::SMEM, st>>>(prm);

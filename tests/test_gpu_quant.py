@@ -39,12 +39,10 @@ def device():
 
 
 # 0: the default choice per row count, 1: CUDA-core matvec with per-warp
-# copies, 2: single-launch tensor-core matvec (digit planes made in the
-# kernel), 3: single-launch CUDA-core matvec (2 rows per launch), 4: tensor-core
+# copies, 3: single-launch CUDA-core matvec (2 rows per launch), 4: tensor-core
 # matvec with a digit-plane launch, 5: int4 rows on the tensor cores by
-# mma.sync over the K-packed copy (int8 as 3).
-@pytest.fixture(params=[0, 1, 2, 3, 4, 5],
-                ids=["default", "cudacore", "tcgen05-1launch", "cudacore-1launch", "tcgen05", "mma-int4"])
+# mma.sync over the K-packed copy (int8 as 3). 2 is retired.
+@pytest.fixture(params=[0, 1, 3, 4, 5], ids=["default", "cudacore", "cudacore-1launch", "tcgen05", "mma-int4"])
 def kernel(request):
     L = _lib.load()
     _lib.check(L.tq_set_matvec_kernel(request.param))
@@ -267,6 +265,46 @@ def test_nan_activation_makes_every_output_nan(bits, m, kernel):
     assert qm.MatMul(x, out, m) is None
     assert np.isnan(out[0]).all()
     assert np.isfinite(out[1:]).all()
+    qm.Free()
+
+
+def _digit_kernel(kernel, bits, m):
+    """Whether (kernel, bits, rows) runs on the tensor cores with integer
+    activation digits (tq_set_matvec_kernel's table): those give NaN for a
+    64-row group holding an infinity, which has no digits."""
+    if kernel == 4:
+        return True
+    if kernel == 5:
+        return bits == 4
+    if kernel == 0:
+        return (bits == 4 and m == 1) or m >= 3
+    return False
+
+
+@pytest.mark.parametrize("m", [1, 4])
+@pytest.mark.parametrize("bits", [8, 4])
+def test_infinite_activation_makes_every_output_non_finite(bits, m, kernel):
+    """An infinite activation leaves no output of its row finite, as in the
+    reference (Inf times a nonzero code is +-Inf, times a zero code NaN). The
+    CUDA-core kernels give the reference's values: the oracle's +-Inf / NaN
+    pattern column for column. The digit kernels give NaN for every column of
+    the row. The other rows stay finite."""
+    rows, cols = 1000, 1030
+    w = O.synth((rows, cols), 6, 1, 0.02)
+    q, s = (O.quantize8 if bits == 8 else O.quantize4)(w)
+    qm = (QMatrix if bits == 8 else Q4Matrix)(rows, cols, q, s)
+    x = O.synth((m, rows), 6, 2, 1.0)
+    x[0, 321] = np.inf
+    out = np.zeros((m, cols), np.float32)
+    assert qm.MatMul(x, out, m) is None
+    assert not np.isfinite(out[0]).any()
+    assert np.isfinite(out[1:]).all()
+    if _digit_kernel(kernel, bits, m):
+        assert np.isnan(out[0]).all()
+    else:
+        want = (O.q8_matmul if bits == 8 else O.q4_matmul)(q, s, rows, cols, x[:1])[0]
+        assert np.array_equal(np.isnan(out[0]), np.isnan(want))
+        assert np.array_equal(out[0][~np.isnan(want)], want[~np.isnan(want)])
     qm.Free()
 
 

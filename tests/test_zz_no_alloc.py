@@ -1,9 +1,10 @@
 """tq_matmul_dev_fixed: the allocation-free matvec entry point, through the C ABI.
 
 Its results must match tq_matmul_dev (the CUDA-core kernel it shares, and the
-default tensor-core kernel) within the matvec tolerance (1e-5 relative L2),
-on consecutive calls that reuse the fixed scratch, and the two consecutive
-calls must agree bit for bit. The file sorts last so that it also runs after every other GPU test
+default tensor-core kernel) and the CPU oracle (the AVX2 restatement of
+quant_simd.go / quant4_simd.go) within the matvec tolerance (1e-5 relative
+L2), on consecutive calls that reuse the fixed scratch, and the two
+consecutive calls must agree bit for bit. The file sorts last so that it also runs after every other GPU test
 in one process; it passes alone in a fresh process too.
 """
 import ctypes
@@ -11,6 +12,7 @@ import ctypes
 import numpy as np
 import pytest
 
+from oracle import oracle as O
 from tensai_b200 import _lib
 from tensai_b200 import quant as Q
 
@@ -74,6 +76,8 @@ def test_fixed_matches_existing_entry(lib, bits, rows, cols, m):
         finally:
             _lib.check(lib.tq_set_matvec_kernel(0))
         default = _call(lib.tq_matmul_dev, h, x, m, cols, st)
+        q, sc = Q.download(h, bits, rows, cols)
+        want = (O.q8_matmul if bits == 8 else O.q4_matmul)(q, sc, rows, cols, x.cpu().numpy())
     finally:
         Q.free(h)
     assert np.isfinite(first).all() and np.isfinite(second).all()
@@ -82,6 +86,8 @@ def test_fixed_matches_existing_entry(lib, bits, rows, cols, m):
     assert _rel_l2(second, cuda_core) <= REL_L2
     assert _rel_l2(first, default) <= REL_L2
     assert _rel_l2(second, default) <= REL_L2
+    assert _rel_l2(first, want) <= REL_L2
+    assert _rel_l2(second, want) <= REL_L2
 
 
 def test_fixed_allocates_no_device_memory(lib):
@@ -102,6 +108,35 @@ def test_fixed_allocates_no_device_memory(lib):
     finally:
         Q.free(h)
     assert free1 == free0
+
+
+def test_fixed_first_call_of_each_kernel_allocates_nothing(lib):
+    """The set-up (first call on the device) loads every kernel the entry point
+    can launch, so the first call of each (bits, rows per launch) afterwards
+    takes no device memory either."""
+    import torch
+    st = torch.cuda.Stream()
+    cases = [(bits, m) + _case(bits, 256, 512, m, seed=40 + bits + m) for bits in (8, 4) for m in (1, 2, 3, 4)]
+    outs = [torch.empty(m, 512, device="cuda") for _, m, _, _ in cases]
+    torch.cuda.synchronize()
+    try:
+        bits, m, h, x = cases[0]
+        _lib.check(lib.tq_matmul_dev_fixed(h, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(outs[0].data_ptr()), m,
+                                           ctypes.c_void_p(st.cuda_stream)))  # set-up (a no-op if done before)
+        st.synchronize()
+        free0, _ = torch.cuda.mem_get_info()
+        for (bits, m, h, x), out in zip(cases, outs):
+            _lib.check(lib.tq_matmul_dev_fixed(h, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr()), m,
+                                               ctypes.c_void_p(st.cuda_stream)))
+        st.synchronize()
+        free1, _ = torch.cuda.mem_get_info()
+        bits_out = ctypes.c_uint(7)
+        _lib.check(lib.tq_device_status(ctypes.byref(bits_out)))  # no timeout, and the fixed word is read
+    finally:
+        for _, _, h, _ in cases:
+            Q.free(h)
+    assert free1 == free0
+    assert bits_out.value == 0
 
 
 def test_fixed_rejects_matrices_beyond_its_scratch(lib):
