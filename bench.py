@@ -10,17 +10,17 @@ L2 (126 MB).
 
   value    algorithmic GB/s over the device-timed region (CUDA events, max over
            ranks), bytes per matvec = codes + scales + x + out (each once). The
-           step is ONE launch of the chain kernel (tq_chain_run: the 64
-           dependent matvecs, weights streamed back to back).
+           step is 64 single-call matvec launches (tq_matmul_dev: the tensor-core
+           kernel cmv_kernel<4,1,true>, one launch per matvec) in one CUDA graph.
   e2e      the same bytes through the C-ABI MatVec entry point (tq_matvec) with
            host buffers, one call per matvec as the Go MatVec makes them: every
            call copies x host->device and out device->host, and each call's
            output is the next call's input
-  roofline the chain kernel's achieved GB/s: algorithmic bytes of one launch
-           over its mean device time (CUDA events on the launching stream),
-           against the measured HBM copy bandwidth
-  single_call  the same dependent workload as 64 single-call launches
-           (tq_matmul_dev, one CUDA graph per step), for comparison
+  roofline the matvec kernel's achieved GB/s: algorithmic bytes of one launch
+           over its mean device time (CUDA events on the launching stream around
+           the step's 64 launches), against the measured HBM copy bandwidth
+  chain    the same dependent workload as ONE launch of the chain kernel
+           (tq_chain_run), for comparison
   cpu_baseline  the CPU oracle (AVX2 restatement of quant4_simd.go with the
            reference's worker split) on the host cores, bounded sample
 
@@ -74,11 +74,11 @@ def load_peak():
 
 
 def load_traffic():
-    """Per-launch DRAM bytes (read + write) of the chain kernel from the
+    """Per-launch DRAM bytes (read + write) of the matvec kernel from the
     committed ncu summary of the same workload (its
     `traffic_bytes_per_launch:` line), or None."""
     import re
-    path = os.path.join(ROOT, "profiles", "chain_int4_m1_mlp_pair.md")
+    path = os.path.join(ROOT, "profiles", "tmv_int4_m1_mlp_pair.md")
     try:
         with open(path) as f:
             m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", f.read())
@@ -347,7 +347,7 @@ QWEN_PROMPT, QWEN_GEN = 2048, 512
 QWEN_BYTES_PER_TOKEN = 3_977_035_776  # int4 codes + scales streamed per token (all layers + lm head)
 
 
-def measure_qwen(rank: int, world: int, peak: float):
+def measure_qwen(rank: int, world: int, peak: float, cpu: bool = False):
     """Qwen2.5-7B-shaped int4 greedy decode, tensor parallel over the job's
     GPUs (one rank per GPU): the 2048-token prompt through the decode step,
     then 512 tokens. Decode tokens/s from the device time of the 511 later
@@ -367,15 +367,29 @@ def measure_qwen(rank: int, world: int, peak: float):
     pre_ms, dec_ms = float(t[0]), float(t[1])
     tok_s = (QWEN_GEN - 1) / (dec_ms * 1e-3)
     bound = world * peak * 1e9 / QWEN_BYTES_PER_TOKEN
-    return {"tp": world, "decode_tok_s": round(tok_s, 2), "ms_per_token": round(dec_ms / (QWEN_GEN - 1), 4),
+    rec = {"tp": world, "decode_tok_s": round(tok_s, 2), "ms_per_token": round(dec_ms / (QWEN_GEN - 1), 4),
             "prompt_ms": round(pre_ms, 1), "prompt_tok_s": round(QWEN_PROMPT / (pre_ms * 1e-3), 1),
             "roofline": {"bound": "aggregate hbm", "tok_s_bound": round(bound, 1), "frac": round(tok_s / bound, 4),
                          "bytes_per_token": QWEN_BYTES_PER_TOKEN, "peak_gbs_per_gpu": peak},
-            "first_tokens": [int(x) for x in toks[:8]],
-            "cpu_baseline_recorded": {"decode_tok_s": 2.81, "cores": 8, "kind": "port",
-                                      "sample": "511 decode steps after the 2048-token prompt, oracle restatement "
-                                                "of the -q4 loop, timed once in the build container "
-                                                "(tests/golden/qwen7b_decode_golden_2048_512.npz)"}}
+            "first_tokens": [int(x) for x in toks[:8]]}
+    golden = os.path.join(ROOT, "tests", "golden", "qwen7b_decode_golden_2048_512.npz")
+    if os.path.exists(golden):  # the oracle's greedy ids for this prompt and seed (TP does not change them)
+        g = np.load(golden)
+        if np.array_equal(g["prompt"], prompt):
+            rec["tokens_match_golden"] = bool(np.array_equal(np.asarray(toks[:len(g["tokens"])]), g["tokens"]))
+    if cpu and rank == 0:
+        # the oracle's -q4 step on this box's cores at the mean decode position
+        # of the run (prompt + half the generated tokens), a few steps timed
+        from oracle import oracle as O
+        threads = O.set_threads(0)
+        pos0, n = QWEN_PROMPT + QWEN_GEN // 2, 3
+        secs, build = O.qwen_time_steps(QWEN_7B, pos0, n)
+        rec["cpu_baseline"] = {"decode_tok_s": round(n / secs, 3), "cores": threads, "kind": "port",
+                               "sample": f"{n} decode steps at cached positions {pos0}..{pos0 + n - 1} of the 7B shape "
+                                         f"({secs:.2f} s), oracle restatement of the -q4 step (AVX2 int4 MatVec, "
+                                         "float64 attention) with filler weights; tokens/s extrapolated from the "
+                                         "per-step time at the run's mean context"}
+    return rec
 
 
 def _check_rc(L, rc):
@@ -475,18 +489,18 @@ def run_gpu(args, rank: int, world: int):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return ms, float(t.item()), clocks
 
-    g_single = capture(single_step)
-    ms_single, ms_single_max, _ = timed(g_single, args.steps)
-    del g_single
     g_chain = capture(chain_step)
-    ms, ms_max, clocks = timed(g_chain, args.steps, sample_clocks=True)
+    ms_chain, ms_chain_max, _ = timed(g_chain, args.steps)
     del g_chain
+    g_single = capture(single_step)
+    ms, ms_max, clocks = timed(g_single, args.steps, sample_clocks=True)
+    del g_single
     # the chain and the single calls compute the same bits (same split and summation order)
-    out_chain = xa.clone()
+    out_single = xa.clone()
     with torch.cuda.stream(stream):
-        single_step()
+        chain_step()
     torch.cuda.synchronize()
-    same_bits = bool(torch.equal(out_chain, xa))
+    same_bits = bool(torch.equal(out_single, xa))
 
     bytes_step = pair_bytes() * LAYERS
     value = bytes_step * world * args.steps / (ms_max * 1e-3) / 1e9
@@ -525,15 +539,15 @@ def run_gpu(args, rank: int, world: int):
         side["C4 GPT-2-small int8 greedy decode"] = measure_gpt2(world == 1 and not args.no_cpu_baseline)
     qwen = None
     if not args.no_side_configs and not args.side_config:
-        qwen = measure_qwen(rank, world, load_peak()[0])  # collective over all ranks
+        qwen = measure_qwen(rank, world, load_peak()[0], cpu=world == 1 and not args.no_cpu_baseline)  # collective
         if side is not None:
             side[f"C5 Qwen2.5-7B int4 greedy decode TP={world}"] = qwen
     if rank == 0:
         peak, peak_src = load_peak()
-        launch_ms = ms / args.steps  # one chain launch per step on this rank
-        achieved = bytes_step / (launch_ms * 1e-3) / 1e9
+        call_us = ms / (args.steps * 2 * LAYERS) * 1e3  # one launch per matvec on this rank
+        achieved = pair_bytes() / 2 / (call_us * 1e-6) / 1e9
         traffic = load_traffic()
-        single_call_us = ms_single / (args.steps * 2 * LAYERS) * 1e3
+        chain_us = ms_chain / (args.steps * 2 * LAYERS) * 1e3
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
@@ -544,22 +558,21 @@ def run_gpu(args, rank: int, world: int):
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "frac_of_8tbs": round(achieved / 8000.0, 4),
                          "traffic": traffic,
-                         "kernel": "chain_kernel<4> (64 dependent int4 M=1 matvecs in one launch; each on the "
-                                   "tensor cores by mma.sync u8 x s8 over the K-packed codes)",
-                         "launch_us_mean": round(launch_ms * 1e3, 3),
-                         "matvec_us_mean": round(launch_ms * 1e3 / (2 * LAYERS), 3),
-                         "algorithmic_bytes_per_launch": bytes_step},
+                         "kernel": "cmv_kernel<4,1,true> (int4 matvec on the tensor cores by mma.sync u8 x s8 "
+                                   "over the K-packed codes, M=1, one launch per matvec)",
+                         "call_us_mean": round(call_us, 3),
+                         "algorithmic_bytes_per_launch": pair_bytes() / 2},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": LAYERS * 4 * (K_UP + N_UP),
                     "d2h_bytes_per_step": LAYERS * 4 * (N_UP + K_UP),
                     "api": "tq_matvec (host x/out, synchronous), the MatVec drop-in, one call per matvec",
-                    "steps": e2e_steps, "same_bits_as_device_chain": e2e_same},
-            "single_call": {"value": round(bytes_step * args.steps / (ms_single_max * 1e-3) / 1e9, 3), "unit": "GB/s",
-                            "us_per_matvec": round(single_call_us, 3),
-                            "frac": round(pair_bytes() / 2 / (single_call_us * 1e-6) / 1e9 / peak, 4),
-                            "kernel": "cmv_kernel<4,1,true>, one launch per matvec (tq_matmul_dev)",
-                            "same_bits_as_chain": same_bits},
-            "gpu_launches": args.steps,
+                    "steps": e2e_steps, "same_bits_as_device_calls": e2e_same},
+            "chain": {"value": round(bytes_step * args.steps / (ms_chain_max * 1e-3) / 1e9, 3), "unit": "GB/s",
+                      "us_per_matvec": round(chain_us, 3),
+                      "frac": round(pair_bytes() / 2 / (chain_us * 1e-6) / 1e9 / peak, 4),
+                      "kernel": "chain_kernel<4>: the step's 64 dependent matvecs in one launch (tq_chain_run)",
+                      "same_bits_as_single_calls": same_bits},
+            "gpu_launches": args.steps * 2 * LAYERS,
             "clocks": clocks.summary(),
         }
         if side:

@@ -298,6 +298,15 @@ TQ_EXPORT int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, 
 /* Releases a model and its NCCL communicator (a second call is a no-op). */
 TQ_EXPORT int tq_qwen_free(uint64_t model);
 
+/* The shard of the model that rank `rank` of `world` GPUs holds, as
+ * tq_qwen_create computes it: plan[0..11] = query heads [a, b), KV heads
+ * [a, b), o_proj rows [a, b), attention output dims [a, b), MLP columns
+ * (gate/up, = down rows) [a, b), lm-head columns [a, b). The Go loader of a
+ * sharded checkpoint slices its tensors with it (loadQwen, model.go:95-177,
+ * per rank). Errors as tq_qwen_create's for configurations that do not split
+ * over world GPUs. Needs no GPU. */
+TQ_EXPORT int tq_qwen_shard_plan(const tq_qwen_config *cfg, int world, int rank, int *plan);
+
 /* Seeded uniform token ids in [0, vocab) on the host: id i =
  * mix64(key + (i+1)*0x9E3779B97F4A7C15) % vocab with the generator key of
  * (seed, stream 3). A stand-in for a tokenized prompt. */

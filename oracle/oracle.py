@@ -60,6 +60,8 @@ def lib():
         L.tqo_gpt2_generate.restype = I
         L.tqo_qwen_generate.argtypes = [P, U64, F, P, I, I, P, P, P, P]
         L.tqo_qwen_generate.restype = I
+        L.tqo_qwen_time_steps.argtypes = [P, I, I, P]
+        L.tqo_qwen_time_steps.restype = I
         L.tqo_synth_tokens.argtypes = [P, I, I, U64]
         L.tqo_synth_tokens.restype = None
         _lib = L
@@ -200,6 +202,18 @@ class QwenCfg(ctypes.Structure):
 
 
 QWEN_7B = dict(n_layer=28, n_head=28, n_kv=4, d=3584, ffn=18944, vocab=152064, ctx=2560, eps=1e-6, theta=1e6)
+
+
+def qwen_time_steps(cfg: dict, pos0: int, n_steps: int):
+    """Wall seconds of n_steps decode steps at cached positions pos0.. of a
+    Qwen2 of shape cfg (seeded filler weights and caches: the timing of a
+    long-context step without minutes of weight building), and of the build."""
+    c = QwenCfg(**cfg)
+    secs = (ctypes.c_double * 2)()
+    rc = lib().tqo_qwen_time_steps(ctypes.byref(c), int(pos0), int(n_steps), secs)
+    if rc:
+        raise ValueError("tqo_qwen_time_steps: bad configuration")
+    return float(secs[0]), float(secs[1])
 
 
 def qwen_generate(cfg: dict, seed: int, sigma: float, prompt, n_gen: int, seconds=None, prompt_logits=False):

@@ -567,3 +567,96 @@ TQO_EXPORT int tqo_qwen_generate(const tqo_qwen_cfg *c, uint64_t seed, float sig
     qwen_free(m);
     return 0;
 }
+
+/* ---- bounded timing of the decode step at a long context ------------------- */
+
+/* Fills n bytes (fill_job) with a seeded xorshift stream, in parallel chunks:
+ * the timed model's codes and its float buffers, whose values do not change
+ * the cost of a step. */
+struct fill_job {
+    uint8_t *p;
+    size_t n;
+    uint64_t seed;
+    int floats; /* fill floats in [-1, 1) instead of bytes */
+};
+#define FILL_CHUNK ((size_t)1 << 22)
+static void fill_task(void *arg, int idx) {
+    struct fill_job *j = arg;
+    const size_t a = (size_t)idx * FILL_CHUNK, b = a + FILL_CHUNK < j->n ? a + FILL_CHUNK : j->n;
+    uint64_t x = j->seed ^ (0x9E3779B97F4A7C15ull * (uint64_t)(idx + 1));
+    for (size_t i = a; i < b; i += 4) {
+        x ^= x << 13, x ^= x >> 7, x ^= x << 17;
+        if (j->floats) {
+            ((float *)j->p)[i / 4] = (float)((int32_t)(x >> 32)) * (1.0f / 2147483648.0f);
+        } else {
+            for (size_t k = 0; k < 4 && i + k < b; k++) j->p[i + k] = (uint8_t)(x >> (8 * k));
+        }
+    }
+}
+static void fill(void *p, size_t bytes, uint64_t seed, int floats) {
+    struct fill_job j = {p, bytes, seed, floats};
+    tqo_pool_run(fill_task, &j, (int)((bytes + FILL_CHUNK - 1) / FILL_CHUNK));
+}
+static void q4_timing(q4mat *m, int rows, int cols, uint64_t seed) {
+    m->rows = rows, m->cols = cols;
+    const size_t qb = (size_t)rows * (cols / 2) + 16, sf = (size_t)((rows + 63) / 64) * cols;
+    m->q = malloc(qb);
+    m->scale = malloc(sizeof(float) * sf);
+    fill(m->q, qb, seed, 0);
+    for (size_t i = 0; i < sf; i++) m->scale[i] = 0.01f;
+}
+
+/*
+ * Wall time of n_steps decode steps (step, model.go:232-307) at cached
+ * positions pos0 .. pos0 + n_steps - 1 of a Qwen2 of shape c: the bounded CPU
+ * baseline of a long-context decode, extrapolated per token by the caller.
+ * The model's codes, embeddings and caches are seeded filler (the cost of a
+ * step does not depend on their values, and building real weights of the 7B
+ * shape takes minutes). seconds[0]: the timed steps; seconds[1]: the build.
+ * Returns 0 or -1.
+ */
+TQO_EXPORT int tqo_qwen_time_steps(const tqo_qwen_cfg *c, int pos0, int n_steps, double *seconds) {
+    if (!c || !seconds || pos0 < 0 || n_steps < 1 || pos0 + n_steps > c->ctx || c->n_head % c->n_kv ||
+        c->d % c->n_head || (c->d / c->n_head) % 2 || c->ffn % 2 || c->vocab % 2)
+        return -1;
+    const double t0 = now_s();
+    qwen *m = calloc(1, sizeof(qwen));
+    m->c = *c;
+    m->hd = c->d / c->n_head;
+    m->kvd = c->n_kv * m->hd;
+    const int d = c->d, kvd = m->kvd, ffn = c->ffn;
+    m->embed = malloc(sizeof(float) * (size_t)c->vocab * d);
+    fill(m->embed, sizeof(float) * (size_t)c->vocab * d, 1, 1);
+    m->normw = ones(d);
+    q4_timing(&m->lm, d, c->vocab, 2);
+    m->b = calloc((size_t)c->n_layer, sizeof(qwblock));
+    for (int l = 0; l < c->n_layer; l++) {
+        qwblock *b = &m->b[l];
+        const uint64_t s0 = 32 + 16 * (uint64_t)l;
+        q4_timing(&b->wq, d, d, s0);
+        q4_timing(&b->wk, d, kvd, s0 + 1);
+        q4_timing(&b->wv, d, kvd, s0 + 2);
+        q4_timing(&b->wo, d, d, s0 + 3);
+        q4_timing(&b->gate, d, ffn, s0 + 4);
+        q4_timing(&b->up, d, ffn, s0 + 5);
+        q4_timing(&b->down, ffn, d, s0 + 6);
+        b->ln1 = ones(d), b->ln2 = ones(d);
+        b->bq = zeros(d), b->bk = zeros(kvd), b->bv = zeros(kvd);
+        b->kc = malloc(sizeof(float) * (size_t)c->ctx * kvd);
+        b->vc = malloc(sizeof(float) * (size_t)c->ctx * kvd);
+        fill(b->kc, sizeof(float) * (size_t)c->ctx * kvd, s0 + 7, 1);
+        fill(b->vc, sizeof(float) * (size_t)c->ctx * kvd, s0 + 8, 1);
+    }
+    float *logits = malloc(sizeof(float) * (size_t)c->vocab);
+    const double t1 = now_s();
+    int tok = 0;
+    for (int i = 0; i < n_steps; i++) {
+        qwen_step(m, tok, pos0 + i, logits);
+        tok = argmax(logits, c->vocab, NULL);
+    }
+    seconds[0] = now_s() - t1;
+    seconds[1] = t1 - t0;
+    free(logits);
+    qwen_free(m);
+    return 0;
+}

@@ -416,6 +416,40 @@ cudaError_t step(Qwen &m, int n_prompt) {
     return cudaGetLastError();
 }
 
+// How rank `rank` of `world` GPUs shards a model (the header's
+// tq_qwen_shard_plan): attention ways wa (world when it divides the KV heads,
+// else the KV heads, repeated over world / n_kv GPUs), this rank's attention
+// shard, its o_proj rows, MLP columns (= down rows) and lm-head columns.
+struct ShardPlan {
+    int wa, ashard, nq, nkv, orow0, orows, fcols, vcols, voff;
+};
+int shard_plan(const tq_qwen_config &c, int world, int rank, ShardPlan *p) {
+    if (c.n_layer < 1 || c.n_head < 1 || c.n_kv < 1 || c.d < 1 || c.ffn < 1 || c.vocab < 1 || c.ctx < 1 ||
+        c.n_head % c.n_kv || c.d % c.n_head || (c.d / c.n_head) % 2)
+        return tq_fail(TQ_ERR_ARG, "tensai: bad Qwen2 configuration");
+    if (world < 1 || rank < 0 || rank >= world)
+        return tq_fail(TQ_ERR_ARG, "tensai: bad rank %d of world %d", rank, world);
+    if (c.n_kv % world == 0)
+        p->wa = world;
+    else if (world % c.n_kv == 0)
+        p->wa = c.n_kv;
+    else
+        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: %d GPUs do not split %d KV heads", world, c.n_kv);
+    if (c.d % world || (c.d / world) % TQ_GROUP || c.ffn % world || (c.ffn / world) % TQ_GROUP || c.vocab % world ||
+        (c.vocab / world) % 2)
+        return tq_fail(TQ_ERR_UNSUPPORTED,
+                       "tensai: d/world and ffn/world must be whole 64-row groups and vocab/world even");
+    p->ashard = rank * p->wa / world;
+    p->nq = c.n_head / p->wa;
+    p->nkv = c.n_kv / p->wa;
+    p->orows = c.d / world;
+    p->orow0 = rank * p->orows;
+    p->fcols = c.ffn / world;
+    p->vcols = c.vocab / world;
+    p->voff = rank * p->vcols;
+    return TQ_OK;
+}
+
 std::shared_ptr<Qwen> find(uint64_t h, int *rc) {
     std::lock_guard<std::mutex> lk(g_q_mu);
     auto it = g_qwens.find(h);
@@ -446,10 +480,10 @@ int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sigma, int ra
                    uint64_t *model) {
     if (!cfg || !model) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
     const tq_qwen_config &c = *cfg;
-    if (c.n_layer < 1 || c.n_head < 1 || c.n_kv < 1 || c.d < 1 || c.ffn < 1 || c.vocab < 1 || c.ctx < 1 ||
-        c.n_head % c.n_kv || c.d % c.n_head || (c.d / c.n_head) % 2)
-        return tq_fail(TQ_ERR_ARG, "tensai: bad Qwen2 configuration");
-    if (world < 1 || rank < 0 || rank >= world || (world > 1 && !nccl_id))
+    ShardPlan sp;
+    int rc0 = shard_plan(c, world, rank, &sp);
+    if (rc0) return rc0;
+    if (world > 1 && !nccl_id)
         return tq_fail(TQ_ERR_ARG, "tensai: bad rank %d of world %d (world > 1 needs an NCCL id)", rank, world);
     if (c.ctx > 6144) return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: context %d exceeds 6144", c.ctx);
     auto m = std::make_shared<Qwen>();
@@ -458,28 +492,18 @@ int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sigma, int ra
     m->world = world;
     m->hd = c.d / c.n_head;
     m->group = c.n_head / c.n_kv;
-    // attention ways: world when it divides the KV heads, else the KV heads (duplicated over world/n_kv GPUs)
-    if (c.n_kv % world == 0)
-        m->wa = world;
-    else if (world % c.n_kv == 0)
-        m->wa = c.n_kv;
-    else
-        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: %d GPUs do not split %d KV heads", world, c.n_kv);
-    m->ashard = rank * m->wa / world;
-    m->nq = c.n_head / m->wa;
-    m->nkv = c.n_kv / m->wa;
+    m->wa = sp.wa;
+    m->ashard = sp.ashard;
+    m->nq = sp.nq;
+    m->nkv = sp.nkv;
     m->qd = m->nq * m->hd;
     m->kvd = m->nkv * m->hd;
-    if (c.d % world || (c.d / world) % TQ_GROUP || c.ffn % world || (c.ffn / world) % TQ_GROUP || c.vocab % world ||
-        (c.vocab / world) % 2)
-        return tq_fail(TQ_ERR_UNSUPPORTED,
-                       "tensai: d/world and ffn/world must be whole 64-row groups and vocab/world even");
-    m->orows = c.d / world;
-    m->orow0 = rank * m->orows;
+    m->orows = sp.orows;
+    m->orow0 = sp.orow0;
     m->arow = m->orow0 - m->ashard * m->qd;
-    m->fcols = c.ffn / world;
-    m->vcols = c.vocab / world;
-    m->voff = rank * m->vcols;
+    m->fcols = sp.fcols;
+    m->vcols = sp.vcols;
+    m->voff = sp.voff;
     int rc = TQ_OK;
     cudaError_t e = cudaGetDevice(&m->device);
     if (e == cudaSuccess && world > 1) {
@@ -562,6 +586,20 @@ int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen,
     unsigned status = 0;
     if ((e = tq_read_status(m->scr, m->st, &status)) != cudaSuccess) return tq_cuda_fail(e, "status read");
     if (status & TQ_STATUS_TIMEOUT) return tq_fail(TQ_ERR_TIMEOUT, "tensai: a kernel timed out during decode");
+    return TQ_OK;
+}
+
+int tq_qwen_shard_plan(const tq_qwen_config *cfg, int world, int rank, int *plan) {
+    if (!cfg || !plan) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    ShardPlan sp;
+    int rc = shard_plan(*cfg, world, rank, &sp);
+    if (rc) return rc;
+    const int hd = cfg->d / cfg->n_head;
+    const int v[12] = {sp.ashard * sp.nq,    (sp.ashard + 1) * sp.nq,    sp.ashard * sp.nkv,
+                       (sp.ashard + 1) * sp.nkv, sp.orow0,             sp.orow0 + sp.orows,
+                       sp.ashard * sp.nq * hd, (sp.ashard + 1) * sp.nq * hd, rank * sp.fcols,
+                       (rank + 1) * sp.fcols, sp.voff,               sp.voff + sp.vcols};
+    std::memcpy(plan, v, sizeof v);
     return TQ_OK;
 }
 

@@ -79,27 +79,19 @@ class QwenConfig(ctypes.Structure):
 
 
 def qwen_shard_plan(cfg: dict, world: int, rank: int) -> dict:
-    """The slices of the model that rank `rank` of `world` holds (the rule
-    tq_qwen_create applies): attention heads, o_proj rows, MLP columns
-    (gate/up) = down rows, lm-head columns. Raises ValueError when the
-    configuration does not split over `world` GPUs."""
-    nh, nkv, d, ffn, V = cfg["n_head"], cfg["n_kv"], cfg["d"], cfg["ffn"], cfg["vocab"]
-    hd = d // nh
-    if nkv % world == 0:
-        wa = world
-    elif world % nkv == 0:
-        wa = nkv
-    else:
-        raise ValueError(f"{world} GPUs do not split {nkv} KV heads")
-    if d % world or (d // world) % 64 or ffn % world or (ffn // world) % 64 or V % world or (V // world) % 2:
-        raise ValueError("d/world and ffn/world must be whole 64-row groups and vocab/world even")
-    ashard = rank * wa // world
-    nq, nk = nh // wa, nkv // wa
-    orows = d // world
-    return dict(q_heads=(ashard * nq, (ashard + 1) * nq), kv_heads=(ashard * nk, (ashard + 1) * nk),
-                o_rows=(rank * orows, (rank + 1) * orows), att_dims=(ashard * nq * hd, (ashard + 1) * nq * hd),
-                ffn=(rank * (ffn // world), (rank + 1) * (ffn // world)),
-                vocab=(rank * (V // world), (rank + 1) * (V // world)))
+    """The slices of the model that rank `rank` of `world` holds, from the
+    library (tq_qwen_shard_plan, the rule tq_qwen_create applies): attention
+    heads, o_proj rows, MLP columns (gate/up) = down rows, lm-head columns.
+    Raises ValueError when the configuration does not split over `world` GPUs."""
+    c = QwenConfig(**cfg)
+    plan = (ctypes.c_int * 12)()
+    L = _lib.load()
+    rc = L.tq_qwen_shard_plan(ctypes.byref(c), world, rank, plan)
+    if rc != _lib.TQ_OK:
+        raise ValueError(L.tq_last_error().decode())
+    v = list(plan)
+    return dict(q_heads=(v[0], v[1]), kv_heads=(v[2], v[3]), o_rows=(v[4], v[5]), att_dims=(v[6], v[7]),
+                ffn=(v[8], v[9]), vocab=(v[10], v[11]))
 
 
 def nccl_unique_id() -> bytes:

@@ -115,3 +115,20 @@ def test_tensor_parallel_tiny_qwen_matches_oracle(world):
     for r in range(world):
         assert isinstance(got[r], list), got[r]
         assert np.array_equal(got[r], want), (r, _diverge(got[r], want, margins))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_qwen7b_shape_matches_golden_tokens(world):
+    """The Qwen2.5-7B shape sharded over 2, 4 or 8 GPUs (at 8, attention
+    repeats over GPU pairs: 4 KV heads) gives the oracle's greedy ids."""
+    if _ndev() < world:
+        pytest.skip(f"needs {world} GPUs")
+    z = np.load(os.path.join(GOLDEN, "qwen7b_decode_golden_64_32.npz"))
+    n_prompt, n_gen = len(z["prompt"]), len(z["tokens"])
+    cfg = dict(QWEN_7B, ctx=n_prompt + n_gen)
+    prompt = synth_tokens(n_prompt, cfg["vocab"], int(z["seed"]))
+    assert np.array_equal(prompt, z["prompt"])
+    got = run_tp(cfg, int(z["seed"]), prompt, n_gen, world)
+    for r in range(world):
+        assert isinstance(got[r], list), got[r]
+        assert np.array_equal(got[r], z["tokens"]), (r, _diverge(got[r], z["tokens"], z["margins"]))
