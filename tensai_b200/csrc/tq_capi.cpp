@@ -669,11 +669,14 @@ int tq_chain_create(const tq_chain_op *ops, int n, uint64_t *chain) {
                                      "a null or not 16-byte aligned input, or a null output",
                                      "an unknown epilogue, or one the matrix cannot take (SwiGLU: int4, even "
                                      "columns; residual: a resid pointer)",
-                                     "too many column tiles",
+                                     "too many columns (int8: more than 8192 column tiles; int4: more than 256 "
+                                     "columns per SM)",
                                      "a normalised input that is not the output of an earlier residual op of "
                                      "matching width",
                                      "too many rows for its column count: a GPU's share of the matrix covers "
-                                     "more than 64 groups of 64 rows"};
+                                     "more than 64 groups of 64 rows",
+                                     "an input or residual that overlaps an earlier op's output without being "
+                                     "exactly that output (or an int4 output overlapping its own external input)"};
         return tq_fail(TQ_ERR_ARG, "tensai: chain op %d: %s", bad, what[why]);
     }
     if (e != cudaSuccess) return tq_cuda_fail(e, "chain build");

@@ -703,6 +703,7 @@ struct TqChain {
     void *mem = nullptr;   // device: ops, done counters, ctl words, sums of squares
     ChainOp *ops = nullptr;
     unsigned *done = nullptr, *ctl = nullptr;
+    TqChain4 *c4 = nullptr; // int4 chains
 };
 
 cudaError_t tq_chain_build(const TqChainSpec *spec, int n, TqChain **out, int *why, int *bad_op) {
@@ -719,6 +720,25 @@ cudaError_t tq_chain_build(const TqChainSpec *spec, int n, TqChain **out, int *w
     if (e == cudaSuccess && (sms < 1 || sms > TQ_MAX_CTAS)) e = cudaErrorInvalidValue;
     if (e != cudaSuccess) return e;
     const int bits = spec[0].m->bits;
+    for (int j = 0; j < n; j++)
+        if (spec[j].m->bits != bits) {
+            *why = TQ_CHAIN_MIXED_BITS;
+            *bad_op = j;
+            return cudaErrorInvalidValue;
+        }
+    if (bits == 4) {
+        TqChain4 *c4 = nullptr;
+        e = tq_chain4_build(spec, n, sms, &c4, why, bad_op);
+        if (e != cudaSuccess) return e;
+        TqChain *ch = new TqChain();
+        ch->device = device;
+        ch->bits = 4;
+        ch->nops = n;
+        ch->ctas = sms;
+        ch->c4 = c4;
+        *out = ch;
+        return cudaSuccess;
+    }
     for (int j = 0; j < n; j++) {
         const TqChainSpec &s = spec[j];
         const TqMatrixDev &m = *s.m;
@@ -812,6 +832,7 @@ cudaError_t tq_chain_build(const TqChainSpec *spec, int n, TqChain **out, int *w
 
 void tq_chain_destroy(TqChain *ch) {
     if (!ch) return;
+    tq_chain4_destroy(ch->c4);
     if (ch->mem) cudaFree(ch->mem);
     delete ch;
 }
@@ -850,5 +871,5 @@ template <int BITS> static cudaError_t launch_chain(const TqChain &ch, const TqS
 }
 
 cudaError_t tq_chain_launch(const TqChain *ch, const TqScratch &scr, cudaStream_t st) {
-    return ch->bits == 4 ? launch_chain<4>(*ch, scr, st) : launch_chain<8>(*ch, scr, st);
+    return ch->c4 ? tq_chain4_launch(ch->c4, scr.status, st) : launch_chain<8>(*ch, scr, st);
 }

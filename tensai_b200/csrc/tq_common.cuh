@@ -235,6 +235,7 @@ enum {
     TQ_CHAIN_TOO_WIDE,   // more than TQ_MAX_TILES column tiles
     TQ_CHAIN_NORM,       // a normalised input that is not an earlier residual op's output
     TQ_CHAIN_TOO_DEEP,   // a per-CTA slice covering more than TQ_CHAIN_MAX_GROUPS row groups
+    TQ_CHAIN_ALIAS,      // an input or residual overlapping an earlier op's output other than exactly
 };
 // Validates the ops and copies their descriptors to the current device
 // (synchronous); *why names the first problem found and *bad_op its op.
@@ -242,3 +243,10 @@ cudaError_t tq_chain_build(const TqChainSpec *spec, int n, TqChain **out, int *w
 void tq_chain_destroy(TqChain *ch);
 int tq_chain_device(const TqChain *ch);
 cudaError_t tq_chain_launch(const TqChain *ch, const TqScratch &scr, cudaStream_t st);
+// int4 chains (tq_chain4.cu): column-owner CTAs, at most TQ_CHAIN4_MAX_BLOCKS
+// 32-column blocks per CTA and op (cols <= 256 x SMs).
+#define TQ_CHAIN4_MAX_BLOCKS 8
+struct TqChain4;
+cudaError_t tq_chain4_build(const TqChainSpec *spec, int n, int sms, TqChain4 **out, int *why, int *bad_op);
+void tq_chain4_destroy(TqChain4 *ch);
+cudaError_t tq_chain4_launch(const TqChain4 *ch, unsigned *status, cudaStream_t st);
