@@ -90,10 +90,14 @@ constexpr int kDgW = 13;                  // digit words per 16 values
 constexpr int kQSmemCap = 226 * 1024;
 constexpr int kRedB = QW * kNP * 32 * 4;       // warp sums per block column
 constexpr int kPlB = QW * 2 * 256;             // per warp: two digit-plane buffers
-constexpr int kQR = (kQSmemCap - kRedB - kPlB - 1024) / kSlotB;
+constexpr int kXD = 4;                         // digit-word batches in flight per warp
+constexpr int kXB = 4 * 4 * kDgW * 8;          // words of a batch of 4 groups (1664 bytes)
+constexpr int kXrB = QW * kXD * kXB;           // per warp: a ring of kXD batches
+constexpr int kQR = (kQSmemCap - kRedB - kPlB - kXrB - 1024) / kSlotB;
 constexpr int kRedOff = kQR * kSlotB;
 constexpr int kPlOff = kRedOff + kRedB;
-constexpr int kBarOff = kPlOff + kPlB; // full[kQR], empty[kQR]
+constexpr int kXrOff = kPlOff + kPlB;
+constexpr int kBarOff = kXrOff + kXrB; // full[kQR], empty[kQR]
 constexpr int kMiscOff = kBarOff + 2 * kQR * 8;
 constexpr int kQSmem = kMiscOff + 128;
 static_assert(kQR >= 6, "ring too shallow");
@@ -263,53 +267,56 @@ __device__ __forceinline__ void block_group(const uint8_t *blk, int lane, const 
 }
 
 // UBT block-groups of one block (consecutive groups, stride apart in the
-// slot) into the lane's sums: every A fragment loaded, then every MMA issued,
-// then the folds, so that 4 UBT independent MMAs are in flight. Groups past
-// the slot's last (n <= k < UBT) are skipped.
+// slot) into the lane's sums, two groups at a time: both groups' A fragments
+// loaded, their 8 MMAs issued, then the folds. Groups past the slot's last
+// (n <= k < UBT) are skipped.
 template <int UBT>
 __device__ __forceinline__ void block_groups(const uint8_t *blk, size_t stride, int n, int lane,
                                              const uint32_t (&b)[UBT][4], const float (&K)[UBT][2],
                                              const float (&O)[UBT][2], float (&acc)[4]) {
     constexpr uint32_t HI = 0xF0F0F0F0u;
-    uint4 a[UBT][2];
-    float4 sc[UBT];
 #pragma unroll
-    for (int k = 0; k < UBT; k++) {
-        const uint8_t *bk = blk + (k < n ? k : 0) * stride;
-        a[k][0] = *reinterpret_cast<const uint4 *>(bk + 16 * lane);
-        a[k][1] = *reinterpret_cast<const uint4 *>(bk + 512 + 16 * lane);
-        sc[k] = *reinterpret_cast<const float4 *>(bk + 1024 + 16 * (lane >> 2));
-    }
-    int d[UBT][4][4];
+    for (int k0 = 0; k0 < UBT; k0 += 2) {
+        if (k0 >= n) break;
+        uint4 a[2][2];
+        float4 sc[2];
 #pragma unroll
-    for (int k = 0; k < UBT; k++)
+        for (int k = 0; k < 2; k++) {
+            const uint8_t *bk = blk + (k0 + k < n ? k0 + k : k0) * stride;
+            a[k][0] = *reinterpret_cast<const uint4 *>(bk + 16 * lane);
+            a[k][1] = *reinterpret_cast<const uint4 *>(bk + 512 + 16 * lane);
+            sc[k] = *reinterpret_cast<const float4 *>(bk + 1024 + 16 * (lane >> 2));
+        }
+        int d[2][4][4];
 #pragma unroll
-        for (int m = 0; m < 4; m++) d[k][m][0] = d[k][m][1] = d[k][m][2] = d[k][m][3] = 0;
+        for (int k = 0; k < 2; k++) {
 #pragma unroll
-    for (int k = 0; k < UBT; k++) {
-        mma_u8s8(d[k][0], a[k][0].x, a[k][0].y, a[k][0].z, a[k][0].w, b[k][0], b[k][1]);
-        mma_u8s8(d[k][1], a[k][0].x & HI, a[k][0].y & HI, a[k][0].z & HI, a[k][0].w & HI, b[k][0], b[k][1]);
-        mma_u8s8(d[k][2], a[k][1].x, a[k][1].y, a[k][1].z, a[k][1].w, b[k][2], b[k][3]);
-        mma_u8s8(d[k][3], a[k][1].x & HI, a[k][1].y & HI, a[k][1].z & HI, a[k][1].w & HI, b[k][2], b[k][3]);
-    }
+            for (int m = 0; m < 4; m++) d[k][m][0] = d[k][m][1] = d[k][m][2] = d[k][m][3] = 0;
+            const uint32_t *bb = b[k0 + k];
+            mma_u8s8(d[k][0], a[k][0].x, a[k][0].y, a[k][0].z, a[k][0].w, bb[0], bb[1]);
+            mma_u8s8(d[k][1], a[k][0].x & HI, a[k][0].y & HI, a[k][0].z & HI, a[k][0].w & HI, bb[0], bb[1]);
+            mma_u8s8(d[k][2], a[k][1].x, a[k][1].y, a[k][1].z, a[k][1].w, bb[2], bb[3]);
+            mma_u8s8(d[k][3], a[k][1].x & HI, a[k][1].y & HI, a[k][1].z & HI, a[k][1].w & HI, bb[2], bb[3]);
+        }
 #pragma unroll
-    for (int k = 0; k < UBT; k++) {
-        if (k >= n) break;
-        const int(&r0)[4] = d[k][0];
-        const int(&h0)[4] = d[k][1];
-        const int(&r1)[4] = d[k][2];
-        const int(&h1)[4] = d[k][3];
-        const float o = O[k][0] + O[k][1];
-        const float l0 = fmaf((float)((r0[0] - h0[0]) + ((r0[1] - h0[1]) << 8)), K[k][0],
-                              fmaf((float)((r1[0] - h1[0]) + ((r1[1] - h1[1]) << 8)), K[k][1], o));
-        const float l8 = fmaf((float)((r0[2] - h0[2]) + ((r0[3] - h0[3]) << 8)), K[k][0],
-                              fmaf((float)((r1[2] - h1[2]) + ((r1[3] - h1[3]) << 8)), K[k][1], o));
-        const float u0 = fmaf((float)((h0[0] + (h0[1] << 8)) >> 4), K[k][0], fmaf((float)((h1[0] + (h1[1] << 8)) >> 4), K[k][1], o));
-        const float u8 = fmaf((float)((h0[2] + (h0[3] << 8)) >> 4), K[k][0], fmaf((float)((h1[2] + (h1[3] << 8)) >> 4), K[k][1], o));
-        acc[0] = fmaf(l0, sc[k].x, acc[0]);
-        acc[1] = fmaf(l8, sc[k].y, acc[1]);
-        acc[2] = fmaf(u0, sc[k].z, acc[2]);
-        acc[3] = fmaf(u8, sc[k].w, acc[3]);
+        for (int k = 0; k < 2; k++) {
+            if (k0 + k >= n) break;
+            const int(&r0)[4] = d[k][0];
+            const int(&h0)[4] = d[k][1];
+            const int(&r1)[4] = d[k][2];
+            const int(&h1)[4] = d[k][3];
+            const float K0 = K[k0 + k][0], K1 = K[k0 + k][1], o = O[k0 + k][0] + O[k0 + k][1];
+            const float l0 = fmaf((float)((r0[0] - h0[0]) + ((r0[1] - h0[1]) << 8)), K0,
+                                  fmaf((float)((r1[0] - h1[0]) + ((r1[1] - h1[1]) << 8)), K1, o));
+            const float l8 = fmaf((float)((r0[2] - h0[2]) + ((r0[3] - h0[3]) << 8)), K0,
+                                  fmaf((float)((r1[2] - h1[2]) + ((r1[3] - h1[3]) << 8)), K1, o));
+            const float u0 = fmaf((float)((h0[0] + (h0[1] << 8)) >> 4), K0, fmaf((float)((h1[0] + (h1[1] << 8)) >> 4), K1, o));
+            const float u8 = fmaf((float)((h0[2] + (h0[3] << 8)) >> 4), K0, fmaf((float)((h1[2] + (h1[3] << 8)) >> 4), K1, o));
+            acc[0] = fmaf(l0, sc[k].x, acc[0]);
+            acc[1] = fmaf(l8, sc[k].y, acc[1]);
+            acc[2] = fmaf(u0, sc[k].z, acc[2]);
+            acc[3] = fmaf(u8, sc[k].w, acc[3]);
+        }
     }
 }
 
@@ -421,19 +428,41 @@ __device__ __forceinline__ void own_digit_loop(const Q4Op &op, const Q4Params &p
     }
 }
 
-// ---- digit words: B fragments read straight from the writer's words ----
+// ---- digit words: B fragments read from the writer's words ----
+//
+// Each warp copies the words of its next kXD batches into its own shared
+// ring (cp.async through L2), so the L2 latency of a batch's words is hidden
+// behind the batches before it; words of an earlier launch are copied again
+// (bounded polling) until they carry this launch's epoch.
 
-// Raw words of one 64-row group for lane (g, t): per 32-row half h its plane
+// Copies the words of groups 4 u0 .. 4 (u0 + UBT) - 1 (those below ng) to xs;
+// one cp.async group per lane.
+template <int UBT>
+__device__ __forceinline__ void dg_issue(const Q4Op &op, int u0, int ng, uint8_t *xs, int lane) {
+    constexpr int NW = UBT * 4 * kDgW; // words of a batch (an even count)
+    const int g0 = 4 * u0;
+    int nw = (ng - g0) * kDgW;
+    nw = nw < 0 ? 0 : nw > NW ? NW : nw;
+    const uint8_t *src = reinterpret_cast<const uint8_t *>(op.xd + (size_t)g0 * kDgW); // 16-byte aligned: 416 u0
+    for (int c = lane; c < NW / 2; c += 32) {
+        const int bytes = 2 * c + 2 <= nw ? 16 : 2 * c < nw ? 8 : 0;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(xs + 16 * c)),
+                     "l"(src + (bytes ? 16 * c : 0)), "r"(bytes)
+                     : "memory");
+    }
+}
+
+// Lane (g, t)'s words of unit k of a batch in xs: per 32-row half h its plane
 // word (g = 0..2: first 16 rows' plane g; g = 4..6: second 16 rows' plane
-// g - 4) and the {O, s} word of the 16-row group lane t folds.
-__device__ __forceinline__ void dg_fetch(const Q4Op &op, int u, int lane, int ng, unsigned long long (&w)[4]) {
+// g - 4) and the {O, s} word of the 16-row group lane t folds; 0 past ng.
+__device__ __forceinline__ void dg_words(const uint8_t *xs, int k, int u, int lane, int ng, unsigned long long (&w)[4]) {
     const int g = lane >> 2, t = lane & 3;
+    const unsigned long long *xw = reinterpret_cast<const unsigned long long *>(xs);
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        const int gp = 4 * u + 2 * h + (g >> 2);
-        w[h] = ((g & 3) != 3 && gp < ng) ? ld_word(op.xd + (size_t)gp * kDgW + (g & 3) * 4 + t) : 0ull;
-        const int gc = 4 * u + 2 * h + (t >> 1);
-        w[2 + h] = gc < ng ? ld_word(op.xd + (size_t)gc * kDgW + 12) : 0ull;
+        const int rp = 4 * k + 2 * h + (g >> 2), rc = 4 * k + 2 * h + (t >> 1);
+        w[h] = ((g & 3) != 3 && 4 * u - 4 * k + rp < ng) ? xw[rp * kDgW + (g & 3) * 4 + t] : 0ull;
+        w[2 + h] = 4 * u - 4 * k + rc < ng ? xw[rc * kDgW + 12] : 0ull;
     }
 }
 
@@ -470,43 +499,47 @@ __device__ __forceinline__ void dg_decode(const unsigned long long (&w)[4], int 
     }
 }
 
-// This warp's batches of UBT consecutive groups (batches cw, cw + 8, ...),
-// digit words fetched one batch ahead.
+// This warp's batches of UBT consecutive groups (batches cw, cw + 8, ...).
 template <int UBT>
 __device__ __forceinline__ void digit_loop(const Q4Op &op, const Q4Params &p, uint8_t *smem, uint64_t *full,
                                            uint64_t *empty, volatile int *issued, volatile int *abort, int cw,
                                            int lane, int nb, int slot_base, unsigned ex, float (&acc)[kNP][4]) {
     const int U = op.units, UB = op_ub(nb), ng = (op.rows + 15) / 16;
     const int nbat = (U + UBT - 1) / UBT;
+    const int nloc = cw < nbat ? (nbat - 1 - cw) / QW + 1 : 0;
     const unsigned e24 = ex & 0xFFFFFFu;
-    unsigned long long wn[UBT][4];
-    auto fetch = [&](int bt) {
+    uint8_t *xr = smem + kXrOff + cw * kXD * kXB;
 #pragma unroll
-        for (int k = 0; k < UBT; k++) dg_fetch(op, bt * UBT + k, lane, ng, wn[k]);
-    };
-    if (cw < nbat) fetch(cw);
-    for (int bt = cw; bt < nbat; bt += QW) {
-        unsigned long long wc[UBT][4];
-#pragma unroll
-        for (int k = 0; k < UBT; k++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) wc[k][i] = wn[k][i];
-        if (bt + QW < nbat) fetch(bt + QW);
-        const int u0 = bt * UBT;
-        // every word of the batch from this launch (bounded polling)
+    for (int i = 0; i < kXD; i++) {
+        if (i < nloc) dg_issue<UBT>(op, (cw + QW * i) * UBT, ng, xr + i * kXB, lane);
+        cp_async_commit();
+    }
+    for (int i = 0; i < nloc; i++) {
+        const int u0 = (cw + QW * i) * UBT;
+        uint8_t *xs = xr + (i % kXD) * kXB;
+        cp_async_wait<kXD - 1>();
+        __syncwarp();
+        unsigned long long w[UBT][4];
         bool ok = true;
 #pragma unroll
-        for (int k = 0; k < UBT; k++) ok = ok && dg_ok(wc[k], u0 + k, lane, ng, e24);
-        if (!__all_sync(0xffffffffu, ok)) {
+        for (int k = 0; k < UBT; k++) {
+            dg_words(xs, k, u0 + k, lane, ng, w[k]);
+            ok = ok && dg_ok(w[k], u0 + k, lane, ng, e24);
+        }
+        if (!__all_sync(0xffffffffu, ok)) { // copied before the writers were done: again (bounded)
             const unsigned long long t0 = global_ns();
             for (unsigned it = 1;; it++) {
-                __nanosleep(32);
-#pragma unroll
-                for (int k = 0; k < UBT; k++)
-                    if (!dg_ok(wc[k], u0 + k, lane, ng, e24)) dg_fetch(op, u0 + k, lane, ng, wc[k]);
+                __nanosleep(64);
+                dg_issue<UBT>(op, u0, ng, xs, lane);
+                cp_async_commit();
+                cp_async_wait<0>();
+                __syncwarp();
                 ok = true;
 #pragma unroll
-                for (int k = 0; k < UBT; k++) ok = ok && dg_ok(wc[k], u0 + k, lane, ng, e24);
+                for (int k = 0; k < UBT; k++) {
+                    dg_words(xs, k, u0 + k, lane, ng, w[k]);
+                    ok = ok && dg_ok(w[k], u0 + k, lane, ng, e24);
+                }
                 if (__all_sync(0xffffffffu, ok)) break;
                 if (poll_stop(p, abort, it, t0, lane)) break;
             }
@@ -514,14 +547,18 @@ __device__ __forceinline__ void digit_loop(const Q4Op &op, const Q4Params &p, ui
         uint32_t b[UBT][4];
         float K[UBT][2], O[UBT][2];
 #pragma unroll
-        for (int k = 0; k < UBT; k++) dg_decode(wc[k], u0 + k, lane, ng, b[k], K[k], O[k]);
+        for (int k = 0; k < UBT; k++) dg_decode(w[k], u0 + k, lane, ng, b[k], K[k], O[k]);
+        __syncwarp(); // every lane has read xs before it is refilled
+        if (i + kXD < nloc) dg_issue<UBT>(op, (cw + QW * (i + kXD)) * UBT, ng, xs, lane);
+        cp_async_commit();
         const int k = slot_base + u0 / UB, ub = u0 % UB;
         if (slot_ready(p, full, issued, k, abort)) {
             const uint8_t *slot = smem + (size_t)(k % kQR) * kSlotB;
-            const int nu = U - u0 < UBT ? U - u0 : UBT; // groups past K carry zero digits: multiply them anyway
-#pragma unroll 1
-            for (int q = 0; q < nb; q++)
-                block_groups<UBT>(slot + ((size_t)ub * nb + q) * kBlkB, (size_t)nb * kBlkB, nu, lane, b, K, O, acc[q]);
+            const int nu = U - u0 < UBT ? U - u0 : UBT;
+#pragma unroll
+            for (int q = 0; q < kNP; q++)
+                if (q < nb)
+                    block_groups<UBT>(slot + ((size_t)ub * nb + q) * kBlkB, (size_t)nb * kBlkB, nu, lane, b, K, O, acc[q]);
         }
         __syncwarp();
         if (lane == 0) {
@@ -530,6 +567,8 @@ __device__ __forceinline__ void digit_loop(const Q4Op &op, const Q4Params &p, ui
             mbar_arrive_cnt(&empty[k % kQR], nu + (ub == 0 ? kSlotBlks - nus : 0));
         }
     }
+    cp_async_wait<0>(); // no copy lands in the ring after the warp moves on
+    __syncwarp();
 }
 
 __global__ void __launch_bounds__(kQThreads, 1) chain4_kernel(Q4Params p) {
@@ -613,13 +652,37 @@ __global__ void __launch_bounds__(kQThreads, 1) chain4_kernel(Q4Params p) {
             // CTA order (own digits: before the digits; digit words: the sums
             // are scaled at the end, so the wait overlaps the groups)
             auto norm_inv = [&]() {
-                if (cw == 0) {
-                    double s = 0.0;
-                    for (int cc = lane; cc < C; cc += 32) {
-                        const float hi = wait_word(p, op.nss + 2 * cc, ex, abort);
-                        const float lo = wait_word(p, op.nss + 2 * cc + 1, ex, abort);
-                        s = __dadd_rn(s, __hiloint2double((int)__float_as_uint(hi), (int)__float_as_uint(lo)));
+                if (cw == 0) { // all of a lane's words in flight at once, then bounded polling of stale ones
+                    constexpr int MC = TQ_MAX_CTAS / 32;
+                    unsigned long long w[MC][2];
+                    bool ok = true;
+#pragma unroll
+                    for (int i = 0; i < MC; i++) {
+                        const int cc = lane + 32 * i;
+                        w[i][0] = w[i][1] = 0;
+                        if (cc < C) ld_word2(op.nss + 2 * cc, w[i][0], w[i][1]);
                     }
+#pragma unroll
+                    for (int i = 0; i < MC; i++) ok = ok && (lane + 32 * i >= C || (word_is(w[i][0], ex) && word_is(w[i][1], ex)));
+                    if (!__all_sync(0xffffffffu, ok)) {
+                        const unsigned long long t0 = global_ns();
+                        for (unsigned it = 1;; it++) {
+                            __nanosleep(32);
+                            ok = true;
+#pragma unroll
+                            for (int i = 0; i < MC; i++) {
+                                const int cc = lane + 32 * i;
+                                if (cc < C && !(word_is(w[i][0], ex) && word_is(w[i][1], ex))) ld_word2(op.nss + 2 * cc, w[i][0], w[i][1]);
+                                ok = ok && (cc >= C || (word_is(w[i][0], ex) && word_is(w[i][1], ex)));
+                            }
+                            if (__all_sync(0xffffffffu, ok)) break;
+                            if (poll_stop(p, abort, it, t0, lane)) break;
+                        }
+                    }
+                    double s = 0.0;
+#pragma unroll
+                    for (int i = 0; i < MC; i++)
+                        if (lane + 32 * i < C) s = __dadd_rn(s, __hiloint2double((int)(unsigned)w[i][0], (int)(unsigned)w[i][1]));
                     s = warp_sum_d(s);
                     if (lane == 0) *inv_s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s, (double)op.rows), op.eps)));
                 }
