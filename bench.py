@@ -495,12 +495,13 @@ def run_gpu(args, rank: int, world: int):
     g_single = capture(single_step)
     ms, ms_max, clocks = timed(g_single, args.steps, sample_clocks=True)
     del g_single
-    # the chain and the single calls compute the same bits (same split and summation order)
+    # the chain (column-owner CTAs) adds each column in its own fixed order: the
+    # single calls' final activations agree with it to the matvec bar
     out_single = xa.clone()
     with torch.cuda.stream(stream):
         chain_step()
     torch.cuda.synchronize()
-    same_bits = bool(torch.equal(out_single, xa))
+    chain_rel = float((xa.double() - out_single.double()).norm() / out_single.double().norm().clamp_min(1e-30))
 
     bytes_step = pair_bytes() * LAYERS
     value = bytes_step * world * args.steps / (ms_max * 1e-3) / 1e9
@@ -529,7 +530,7 @@ def run_gpu(args, rank: int, world: int):
     if world > 1:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_value = bytes_step * world * e2e_steps / float(e2e_t.item()) / 1e9
-    e2e_same = bool(np.array_equal(hxa, xa.cpu().numpy()))
+    e2e_same = bool(np.array_equal(hxa, out_single.cpu().numpy()))
 
     side = None
     if rank == 0 and args.side_config:
@@ -570,8 +571,9 @@ def run_gpu(args, rank: int, world: int):
             "chain": {"value": round(bytes_step * args.steps / (ms_chain_max * 1e-3) / 1e9, 3), "unit": "GB/s",
                       "us_per_matvec": round(chain_us, 3),
                       "frac": round(pair_bytes() / 2 / (chain_us * 1e-6) / 1e9 / peak, 4),
-                      "kernel": "chain_kernel<4>: the step's 64 dependent matvecs in one launch (tq_chain_run)",
-                      "same_bits_as_single_calls": same_bits},
+                      "kernel": "chain4_kernel: the step's 64 dependent matvecs in one launch (tq_chain_run), "
+                                "column-owner CTAs",
+                      "rel_l2_vs_single_calls_after_64": chain_rel},
             "gpu_launches": args.steps * 2 * LAYERS,
             "clocks": clocks.summary(),
         }

@@ -39,14 +39,21 @@ std::unordered_map<uint64_t, std::shared_ptr<ChainEntry>> g_chains;
 uint64_t g_next_chain = 1;
 
 // Per-thread, per-device context for the host-pointer entry points.
+// The output block d_blk / h_blk is [status word, 3 pad words | out]: the
+// call's kernels report into its first word, which travels back with out.
 struct ThreadCtx {
     cudaStream_t stream = nullptr;
-    float *d_x = nullptr, *d_out = nullptr;
-    size_t d_x_cap = 0, d_out_cap = 0;
-    float *h_x = nullptr, *h_out = nullptr; // pinned staging
-    size_t h_x_cap = 0, h_out_cap = 0;
-    unsigned *h_status = nullptr; // pinned: the stream scratch's status word after each call
+    float *d_x = nullptr, *d_blk = nullptr;
+    size_t d_x_cap = 0, d_blk_cap = 0;
+    float *h_x = nullptr, *h_blk = nullptr; // pinned staging
+    size_t h_x_cap = 0, h_blk_cap = 0;
+    // Single-row calls replayed as one graph (x in, the matvec, status and
+    // out back) per (matrix handle, kernel selection); built on a matrix's
+    // second call, dropped when the staging buffers move.
+    std::unordered_map<uint64_t, cudaGraphExec_t> graphs;
 };
+constexpr size_t kBlkHead = 4; // floats before out in the output block
+constexpr size_t kMaxGraphs = 64;
 thread_local std::unordered_map<int, ThreadCtx> t_ctx;
 
 // Matvec scratch, one per (device, stream): kernels on one stream run in
@@ -213,6 +220,12 @@ static int ensure_stream(ThreadCtx *c) {
         if (e != cudaSuccess) return tq_cuda_fail(e, "stream create");
     }
     return TQ_OK;
+}
+
+static void drop_graphs(ThreadCtx *c) {
+    for (auto &kv : c->graphs)
+        if (kv.second) cudaGraphExecDestroy(kv.second);
+    c->graphs.clear();
 }
 
 static int grow_dev(float **p, size_t *cap, size_t floats) {
@@ -558,34 +571,55 @@ int tq_matmul(uint64_t handle, const float *x, float *out, int m) {
     ThreadCtx *c = ctx_for(p->device);
     if ((rc = ensure_stream(c))) return rc;
     const size_t nx = (size_t)m * p->m.rows, no = (size_t)m * p->m.cols;
-    if ((rc = grow_dev(&c->d_x, &c->d_x_cap, nx)) || (rc = grow_dev(&c->d_out, &c->d_out_cap, no)) ||
-        (rc = grow_host(&c->h_x, &c->h_x_cap, nx)) || (rc = grow_host(&c->h_out, &c->h_out_cap, no)))
+    const float *old_x = c->d_x, *old_blk = c->d_blk, *old_hx = c->h_x, *old_hb = c->h_blk;
+    if ((rc = grow_dev(&c->d_x, &c->d_x_cap, nx)) || (rc = grow_dev(&c->d_blk, &c->d_blk_cap, kBlkHead + no)) ||
+        (rc = grow_host(&c->h_x, &c->h_x_cap, nx)) || (rc = grow_host(&c->h_blk, &c->h_blk_cap, kBlkHead + no)))
         return rc;
-    if (!c->h_status) {
-        e = cudaMallocHost((void **)&c->h_status, sizeof(unsigned));
-        if (e != cudaSuccess) return tq_cuda_fail(e, "pinned staging allocation");
-    }
+    if (c->d_blk != old_blk && (e = cudaMemsetAsync(c->d_blk, 0, kBlkHead * sizeof(float), c->stream)) != cudaSuccess)
+        return tq_cuda_fail(e, "status word reset");
+    if (c->d_x != old_x || c->d_blk != old_blk || c->h_x != old_hx || c->h_blk != old_hb) drop_graphs(c);
     TqScratch scr;
     if ((rc = scratch_for(p->device, c->stream, &scr, m))) return rc;
-    // One synchronization per call: x in, the launch, then out and the
-    // scratch's status word back into pinned memory.
+    scr.status = reinterpret_cast<unsigned *>(c->d_blk); // this call's status word travels back with out
+    // x in, the launch, then status and out back in one copy; one synchronization.
+    auto enqueue = [&]() {
+        cudaError_t r = cudaMemcpyAsync(c->d_x, c->h_x, nx * sizeof(float), cudaMemcpyHostToDevice, c->stream);
+        if (r == cudaSuccess) r = launch_matvec(p->m, c->d_x, c->d_blk + kBlkHead, m, scr, c->stream);
+        if (r == cudaSuccess)
+            r = cudaMemcpyAsync(c->h_blk, c->d_blk, (kBlkHead + no) * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
+        return r;
+    };
+    const uint64_t key = handle * 8 + (uint64_t)g_matvec_kernel.load();
+    auto it = m == 1 ? c->graphs.find(key) : c->graphs.end();
+    const bool known = it != c->graphs.end(), cached = known && it->second; // null: capture failed once
     std::memcpy(c->h_x, x, nx * sizeof(float));
-    e = cudaMemcpyAsync(c->d_x, c->h_x, nx * sizeof(float), cudaMemcpyHostToDevice, c->stream);
-    if (e == cudaSuccess) e = launch_matvec(p->m, c->d_x, c->d_out, m, scr, c->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(c->h_out, c->d_out, no * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(c->h_status, scr.status, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    e = cached ? cudaGraphLaunch(it->second, c->stream) : enqueue();
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return tq_cuda_fail(e, "matmul");
-    if (*c->h_status) { // rare: re-arm the status word before reporting
-        const unsigned status = *c->h_status;
-        e = cudaMemsetAsync(scr.status, 0, sizeof(unsigned), c->stream);
+    const unsigned status = *reinterpret_cast<const unsigned *>(c->h_blk);
+    if (status) { // rare: re-arm the status word before reporting
+        e = cudaMemsetAsync(c->d_blk, 0, sizeof(unsigned), c->stream);
         if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
         if (e != cudaSuccess) return tq_cuda_fail(e, "status reset");
         if (status & TQ_STATUS_TIMEOUT)
             return tq_fail(TQ_ERR_TIMEOUT, "tensai: a kernel timed out waiting for its weight copies");
     }
-    std::memcpy(out, c->h_out, no * sizeof(float));
+    std::memcpy(out, c->h_blk + kBlkHead, no * sizeof(float));
+    if (m == 1 && !known) { // the next call on this matrix replays the same work as one graph
+        if (c->graphs.size() >= kMaxGraphs) drop_graphs(c);
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t ge = nullptr;
+        cudaError_t r = cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal);
+        if (r == cudaSuccess) {
+            const cudaError_t q = enqueue();
+            r = cudaStreamEndCapture(c->stream, &g);
+            if (q != cudaSuccess) r = q;
+        }
+        if (r == cudaSuccess) r = cudaGraphInstantiate(&ge, g, 0);
+        if (g) cudaGraphDestroy(g);
+        if (r != cudaSuccess) cudaGetLastError(); // the call itself succeeded: stay on plain launches
+        c->graphs[key] = r == cudaSuccess ? ge : nullptr;
+    }
     return TQ_OK;
 }
 

@@ -248,6 +248,32 @@ def test_results_are_bit_reproducible(kernel, bits, rows, cols):
     assert same_bits(outs[0], outs[1]) and same_bits(outs[0], outs[2])
 
 
+def test_host_matvec_replays_follow_new_inputs_and_regrown_staging(kernel):
+    """Host-pointer MatVec calls replay a captured graph from a matrix's second
+    call on: alternating a small and a larger matrix (the larger one regrows
+    the staging buffers and drops the graphs) with fresh inputs every call,
+    every result must be the oracle's for that call's input, and a repeated
+    input must give the first call's bits."""
+    mats = []
+    for bits, rows, cols, seed in ((4, 256, 512, 41), (8, 1024, 3000, 42), (4, 4096, 11008, 43)):
+        w = O.synth((rows, cols), seed, 1, 0.02)
+        q, sc = (O.quantize8 if bits == 8 else O.quantize4)(w)
+        mats.append((bits, rows, cols, q, sc, (QMatrix if bits == 8 else Q4Matrix)(rows, cols, q, sc)))
+    first = {}
+    for it in range(4):
+        for i, (bits, rows, cols, q, sc, qm) in enumerate(mats):
+            x = O.synth((rows,), 50 + it % 2, i, 1.0)
+            out = np.zeros(cols, np.float32)
+            assert qm.MatVec(x, out) is None
+            want = (O.q8_matmul if bits == 8 else O.q4_matmul)(q, sc, rows, cols, x)[0]
+            assert rel_l2(out, want) <= REL_L2, (it, i)
+            key = (i, it % 2)
+            if key in first:
+                assert same_bits(out, first[key]), (it, i)
+            else:
+                first[key] = out
+
+
 @pytest.mark.parametrize("m", [1, 4])
 @pytest.mark.parametrize("bits", [8, 4])
 def test_nan_activation_makes_every_output_nan(bits, m, kernel):
