@@ -343,6 +343,58 @@ def measure_gpt2(cpu: bool):
     return rec
 
 
+def measure_quant_load(cpu: bool):
+    """Quantize-on-load of every Qwen2.5-7B int4 matrix (per layer q|k|v
+    3584x4608, o 3584x3584, gate|up 3584x37888, down 18944x3584; the lm head
+    3584x152064) from device-resident BF16 Linear weights [out, in]
+    (tq_quantize4_linear_dev: the loader's transpose and widening fused into
+    QuantizeMatrix4). Wall time of the 197 calls with a final synchronize,
+    allocation of the handles included. With cpu=True also the oracle's
+    QuantizeMatrix4 on the host for one layer's four matrices, extrapolated
+    to the model by parameters."""
+    import torch
+    from tensai_b200 import quant as Q
+    d, kv, f, v = 3584, 512, 18944, 152064
+    shapes = [(d + 2 * kv, d), (d, d), (2 * f, d), (d, f)] * 28 + [(v, d)]  # [out, in]
+    params = sum(a * b for a, b in shapes)
+    buf = torch.empty(max(a * b for a, b in shapes), device="cuda", dtype=torch.bfloat16)
+    buf.normal_(0.0, 0.02)
+    torch.cuda.synchronize()
+    hs = [Q.quantize_linear_dev(buf[: a * b].view(a, b), 4) for a, b in shapes[:4]]  # warm-up (kernel set-up)
+    torch.cuda.synchronize()
+    for h in hs:
+        Q.free(h)
+    t0 = time.perf_counter()
+    hs = [Q.quantize_linear_dev(buf[: a * b].view(a, b), 4) for a, b in shapes]
+    torch.cuda.synchronize()
+    secs = time.perf_counter() - t0
+    for h in hs:
+        Q.free(h)
+    del buf
+    torch.cuda.empty_cache()
+    rec = {"seconds": round(secs, 4), "params": params, "bf16_GB_read": round(2 * params / 1e9, 3),
+           "GB/s_of_bf16": round(2 * params / secs / 1e9, 1),
+           "what": "197 int4 matrices of the 7B shape from device BF16 [out, in] weights: transpose, widening and "
+                   "QuantizeMatrix4 in one kernel, plus the K-packed copy; handle allocation included"}
+    if cpu:
+        from oracle import oracle as O
+        threads = O.set_threads(0)
+        sample = shapes[:4]
+        t = 0.0
+        for a, b in sample:
+            w = O.synth((b, a), 5, a, 0.02)  # the transposed f32 matrix the loader quantizes
+            t1 = time.perf_counter()
+            O.quantize4(w)
+            t += time.perf_counter() - t1
+        sp = sum(a * b for a, b in sample)
+        rec["cpu_baseline"] = {"seconds": round(t * params / sp, 2), "cores": threads, "kind": "port",
+                               "sample": f"one layer's four matrices ({sp} parameters, {t:.2f} s) through the oracle's "
+                                         "QuantizeMatrix4 on all host threads (the reference's runs on one), "
+                                         "extrapolated to the model by parameters; the BF16 widening and "
+                                         "transpose not counted"}
+    return rec
+
+
 QWEN_PROMPT, QWEN_GEN = 2048, 512
 QWEN_BYTES_PER_TOKEN = 3_977_035_776  # int4 codes + scales streamed per token (all layers + lm head)
 
@@ -538,6 +590,7 @@ def run_gpu(args, rank: int, world: int):
     elif rank == 0 and not args.no_side_configs:
         side = measure_side_configs(L, Q, torch, stream, load_peak()[0], cpu=world == 1 and not args.no_cpu_baseline)
         side["C4 GPT-2-small int8 greedy decode"] = measure_gpt2(world == 1 and not args.no_cpu_baseline)
+        side["F2 Qwen2.5-7B int4 quantize-on-load from BF16"] = measure_quant_load(world == 1 and not args.no_cpu_baseline)
     qwen = None
     if not args.no_side_configs and not args.side_config:
         qwen = measure_qwen(rank, world, load_peak()[0], cpu=world == 1 and not args.no_cpu_baseline)  # collective

@@ -90,6 +90,23 @@ TQ_EXPORT int tq_quantize4(const float *w, int rows, int cols, uint8_t *q, float
 TQ_EXPORT int tq_quantize8_dev(const float *w, int rows, int cols, void *stream, uint64_t *handle);
 TQ_EXPORT int tq_quantize4_dev(const float *w, int rows, int cols, void *stream, uint64_t *handle);
 
+/* Quantize-on-load from a checkpoint tensor: w is a DEVICE Linear weight
+ * [out_features][in_features], row-major, of element type dtype (BF16: the
+ * upper half of an f32, widened by a 16-bit shift as safetensors.go:187-190;
+ * F16: IEEE half, widened exactly; F32). The new handle holds the matrix the
+ * loader builds with Matrix().T() (_example/qwen/model.go:126-140),
+ * rows = in_features and cols = out_features, quantized bit for bit as
+ * QuantizeMatrix / QuantizeMatrix4 quantize that transpose; the transpose and
+ * the widening are fused into the quantizer (no f32 copy is made). int4 with
+ * odd out_features -> TQ_ERR_ARG as tq_quantize4. Asynchronous on stream. */
+#define TQ_LINEAR_F32 0
+#define TQ_LINEAR_F16 1
+#define TQ_LINEAR_BF16 2
+TQ_EXPORT int tq_quantize8_linear_dev(const void *w, int dtype, int out_features, int in_features, void *stream,
+                                      uint64_t *handle);
+TQ_EXPORT int tq_quantize4_linear_dev(const void *w, int dtype, int out_features, int in_features, void *stream,
+                                      uint64_t *handle);
+
 /* bits (8 or 4), rows, cols of a handle. Any output pointer may be NULL. */
 TQ_EXPORT int tq_matrix_info(uint64_t handle, int *bits, int *rows, int *cols);
 

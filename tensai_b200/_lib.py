@@ -43,6 +43,8 @@ SIGNATURES = {
     "tq_quantize4": (I, [P, I, I, P, P]),
     "tq_quantize8_dev": (I, [P, I, I, P, PU64]),
     "tq_quantize4_dev": (I, [P, I, I, P, PU64]),
+    "tq_quantize8_linear_dev": (I, [P, I, I, I, P, PU64]),
+    "tq_quantize4_linear_dev": (I, [P, I, I, I, P, PU64]),
     "tq_matrix_info": (I, [U64, PI, PI, PI]),
     "tq_download": (I, [U64, P, P]),
     "tq_free": (I, [U64]),
@@ -70,6 +72,9 @@ SIGNATURES = {
 
 ABI_VERSION = 1
 
+TQ_LINEAR_F32 = 0
+TQ_LINEAR_F16 = 1
+TQ_LINEAR_BF16 = 2
 TQ_CHAIN_EPI_NONE = 0
 TQ_CHAIN_EPI_SWIGLU = 1
 TQ_CHAIN_EPI_RESID = 2

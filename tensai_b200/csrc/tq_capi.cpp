@@ -448,6 +448,36 @@ int tq_quantize4_dev(const float *w, int rows, int cols, void *stream, uint64_t 
     return quantize_dev(4, w, rows, cols, stream, handle);
 }
 
+static int quantize_linear_dev(int bits, const void *w, int dtype, int out_features, int in_features, void *stream,
+                               uint64_t *handle) {
+    if (!handle || (!w && out_features && in_features)) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    if (dtype != TQ_LINEAR_F32 && dtype != TQ_LINEAR_F16 && dtype != TQ_LINEAR_BF16)
+        return tq_fail(TQ_ERR_ARG, "tensai: unknown Linear weight type %d", dtype);
+    const int rows = in_features, cols = out_features; // the transpose the loader quantizes
+    int rc = check_dims(bits, rows, cols);
+    if (rc) return rc;
+    if ((rc = set_thread_device())) return rc;
+    TqMatrixDev m;
+    if ((rc = alloc_matrix(bits, rows, cols, &m, (cudaStream_t)stream))) return rc;
+    cudaError_t e = tq_launch_quantize_linear(m, w, dtype, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        release_matrix(&m);
+        return tq_cuda_fail(e, "quantize launch");
+    }
+    *handle = register_handle(t_device, m);
+    return TQ_OK;
+}
+
+int tq_quantize8_linear_dev(const void *w, int dtype, int out_features, int in_features, void *stream,
+                            uint64_t *handle) {
+    return quantize_linear_dev(8, w, dtype, out_features, in_features, stream, handle);
+}
+
+int tq_quantize4_linear_dev(const void *w, int dtype, int out_features, int in_features, void *stream,
+                            uint64_t *handle) {
+    return quantize_linear_dev(4, w, dtype, out_features, in_features, stream, handle);
+}
+
 static int quantize_host(int bits, const float *w, int rows, int cols, void *q, float *scale) {
     if (!q || !scale || (!w && rows && cols)) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
     int rc = check_dims(bits, rows, cols);

@@ -158,6 +158,9 @@ static inline size_t tq_scale_floats(int bits, int rows, int cols) {
 // launch; none synchronizes.
 cudaError_t tq_launch_synth(float *out, size_t n, uint64_t seed, uint64_t stream, float sigma, cudaStream_t st);
 cudaError_t tq_launch_quantize(const TqMatrixDev &m, const float *w, cudaStream_t st);
+// Quantizes the transpose of a Linear weight [m.cols][m.rows] of element type
+// dtype (TQ_LINEAR_*): W[i][j] = w[j][i] widened to f32 exactly.
+cudaError_t tq_launch_quantize_linear(const TqMatrixDev &m, const void *w, int dtype, cudaStream_t st);
 // Reference layout (rows x rowBytes codes, reference Scale) <-> device layout,
 // both sides in device memory.
 cudaError_t tq_launch_to_tiled(const TqMatrixDev &m, const uint8_t *ref_q, const float *ref_scale, cudaStream_t st);

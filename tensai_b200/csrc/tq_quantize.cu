@@ -7,6 +7,8 @@
 // exact half-way points): __fdiv_rn for maxAbs/127 and 1/s, __fmul_rn for
 // w*inv, __fadd_rn/__fsub_rn for the +/-0.5, and __float2int_rz for Go's
 // truncating int8()/int() conversion.
+#include <cuda_fp16.h>
+#include "../../include/tensai_cuda.h"
 #include "tq_common.cuh"
 
 // ---------------------------------------------------------------------------
@@ -73,13 +75,35 @@ __device__ __forceinline__ int tq_round_away(float w, float inv) {
     return __float2int_rz(v);
 }
 
-__global__ void __launch_bounds__(256) tq_quantize8_kernel(TqMatrixDev m, const float *__restrict__ w) {
+// Where the kernels read W[i][j] (K = m.rows, N = m.cols): a row-major f32
+// [K][N] matrix, or a [N][K] Linear weight ([out][in], the checkpoint layout)
+// read transposed and widened to f32 exactly (BF16: bits << 16 as
+// safetensors.go:187-190; F16: IEEE widening), which is the loader's
+// Matrix().T() (_example/qwen/model.go:126-140) fused into the quantizer.
+struct SrcRowMajor {
+    const float *w;
+    int cols;
+    __device__ __forceinline__ float operator()(int i, int j) const { return w[(size_t)i * cols + j]; }
+};
+struct SrcLinear {
+    const void *w;
+    int rows, dtype;
+    __device__ __forceinline__ float operator()(int i, int j) const {
+        const size_t k = (size_t)j * rows + i;
+        if (dtype == TQ_LINEAR_BF16) return __uint_as_float((uint32_t)static_cast<const uint16_t *>(w)[k] << 16);
+        if (dtype == TQ_LINEAR_F16) return __half2float(static_cast<const __half *>(w)[k]);
+        return static_cast<const float *>(w)[k];
+    }
+};
+
+template <class Src>
+__global__ void __launch_bounds__(256) tq_quantize8_kernel(TqMatrixDev m, Src w) {
     __shared__ float red[8][33];
     const int j = blockIdx.x * 32 + threadIdx.x;
     const bool valid = j < m.cols;
     float maxAbs = 0.f;
     if (valid)
-        for (int i = threadIdx.y; i < m.rows; i += 8) maxAbs = tq_absmax_step(maxAbs, w[(size_t)i * m.cols + j]);
+        for (int i = threadIdx.y; i < m.rows; i += 8) maxAbs = tq_absmax_step(maxAbs, w(i, j));
     red[threadIdx.y][threadIdx.x] = maxAbs;
     __syncthreads();
     maxAbs = red[0][threadIdx.x];
@@ -90,7 +114,7 @@ __global__ void __launch_bounds__(256) tq_quantize8_kernel(TqMatrixDev m, const 
     if (!valid || s == 0) return; // codes stay 0 (quant.go:57-59); buffer is pre-zeroed
     const float inv = __fdiv_rn(1.0f, s);
     for (int i = threadIdx.y; i < m.rows; i += 8)
-        m.codes[tq_code_offset(m.units, i, j)] = (uint8_t)(int8_t)tq_round_away(w[(size_t)i * m.cols + j], inv);
+        m.codes[tq_code_offset(m.units, i, j)] = (uint8_t)(int8_t)tq_round_away(w(i, j), inv);
 }
 
 // ---------------------------------------------------------------------------
@@ -106,7 +130,8 @@ __device__ __forceinline__ uint32_t tq_nibble(float w, float s, float inv) {
     return (uint32_t)(n + 8);
 }
 
-__global__ void __launch_bounds__(128) tq_quantize4_kernel(TqMatrixDev m, const float *__restrict__ w) {
+template <class Src>
+__global__ void __launch_bounds__(128) tq_quantize4_kernel(TqMatrixDev m, Src w) {
     const int half = m.cols / 2;
     const int p = blockIdx.x * 128 + threadIdx.x;
     const int g = blockIdx.y;
@@ -115,8 +140,8 @@ __global__ void __launch_bounds__(128) tq_quantize4_kernel(TqMatrixDev m, const 
     const int rhi = min(rlo + TQ_GROUP, m.rows);
     float mlo = 0.f, mhi = 0.f;
     for (int i = rlo; i < rhi; i++) {
-        mlo = tq_absmax_step(mlo, w[(size_t)i * m.cols + p]);
-        mhi = tq_absmax_step(mhi, w[(size_t)i * m.cols + half + p]);
+        mlo = tq_absmax_step(mlo, w(i, p));
+        mhi = tq_absmax_step(mhi, w(i, half + p));
     }
     const float slo = __fdiv_rn(mlo, 7.0f), shi = __fdiv_rn(mhi, 7.0f);
     m.scale[tq_scale4_offset(m.units, g, 0, p)] = slo;
@@ -124,13 +149,13 @@ __global__ void __launch_bounds__(128) tq_quantize4_kernel(TqMatrixDev m, const 
     const float ilo = slo == 0 ? 0.f : __fdiv_rn(1.0f, slo);
     const float ihi = shi == 0 ? 0.f : __fdiv_rn(1.0f, shi);
     for (int i = rlo; i < rhi; i++) {
-        uint32_t lo = tq_nibble(w[(size_t)i * m.cols + p], slo, ilo);
-        uint32_t hi = tq_nibble(w[(size_t)i * m.cols + half + p], shi, ihi);
+        uint32_t lo = tq_nibble(w(i, p), slo, ilo);
+        uint32_t hi = tq_nibble(w(i, half + p), shi, ihi);
         m.codes[tq_code_offset(m.units, i, p)] = (uint8_t)(lo | (hi << 4));
     }
 }
 
-cudaError_t tq_launch_quantize(const TqMatrixDev &m, const float *w, cudaStream_t st) {
+template <class Src> static cudaError_t launch_quantize(const TqMatrixDev &m, Src w, cudaStream_t st) {
     if (m.rows == 0 || m.cols == 0) return cudaSuccess;
     if (m.bits == 8) {
         dim3 grid((m.cols + 31) / 32), block(32, 8);
@@ -145,6 +170,14 @@ cudaError_t tq_launch_quantize(const TqMatrixDev &m, const float *w, cudaStream_
         return tq_launch_repack4(m, st); // the tensor-core matvec's K-packed copy
     }
     return cudaGetLastError();
+}
+
+cudaError_t tq_launch_quantize(const TqMatrixDev &m, const float *w, cudaStream_t st) {
+    return launch_quantize(m, SrcRowMajor{w, m.cols}, st);
+}
+
+cudaError_t tq_launch_quantize_linear(const TqMatrixDev &m, const void *w, int dtype, cudaStream_t st) {
+    return launch_quantize(m, SrcLinear{w, m.rows, dtype}, st);
 }
 
 // ---------------------------------------------------------------------------

@@ -171,6 +171,23 @@ def quantize_dev(w, bits: int, stream=None) -> int:
     return h.value
 
 
+def quantize_linear_dev(w, bits: int, stream=None) -> int:
+    """Quantizes a checkpoint Linear weight, a CUDA tensor [out, in] of
+    float32, float16 or bfloat16, into a resident handle of the matrix the
+    loader makes with Matrix().T() (_example/qwen/model.go:126-140):
+    rows = in, cols = out."""
+    import torch
+    kinds = {torch.float32: _lib.TQ_LINEAR_F32, torch.float16: _lib.TQ_LINEAR_F16, torch.bfloat16: _lib.TQ_LINEAR_BF16}
+    if w.dtype not in kinds or w.dim() != 2 or not w.is_contiguous():
+        raise ValueError("tensai: a contiguous 2-D float32, float16 or bfloat16 Linear weight is required")
+    L = _lib.load()
+    h = ctypes.c_uint64()
+    fn = L.tq_quantize8_linear_dev if bits == 8 else L.tq_quantize4_linear_dev
+    st = ctypes.c_void_p(stream.cuda_stream if stream is not None else None)
+    _lib.check(fn(ctypes.c_void_p(w.data_ptr()), kinds[w.dtype], w.shape[0], w.shape[1], st, ctypes.byref(h)))
+    return h.value
+
+
 def matmul_dev(handle: int, x, out, stream=None) -> None:
     """out[m, cols] = x[m, rows] @ W on the device (CUDA tensors, float32)."""
     st = ctypes.c_void_p(stream.cuda_stream if stream is not None else None)

@@ -248,6 +248,37 @@ def test_results_are_bit_reproducible(kernel, bits, rows, cols):
     assert same_bits(outs[0], outs[1]) and same_bits(outs[0], outs[2])
 
 
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("out_f,in_f", [(130, 200), (10, 33), (4608, 3584), (2, 1)])
+def test_quantize_linear_weight_bit_exact(dtype, bits, out_f, in_f):
+    """Quantize-on-load: a checkpoint Linear weight [out, in] in its own dtype
+    quantizes, transposed and widened inside the kernel, to exactly the codes
+    and scales QuantizeMatrix / QuantizeMatrix4 give for Matrix().T()
+    (_example/qwen/model.go:126-140; BF16 widening safetensors.go:187-190)."""
+    import torch
+    dt = getattr(torch, dtype)
+    w32 = O.synth((out_f, in_f), 61, out_f * 7 + in_f, 0.05)
+    w = torch.from_numpy(w32).cuda().to(dt)
+    h = Q.quantize_linear_dev(w, bits)
+    torch.cuda.synchronize()
+    wt = np.ascontiguousarray(w.float().cpu().numpy().T)  # the loader's f32 transpose, widened exactly
+    q, s = Q.download(h, bits, in_f, out_f)
+    qo, so = (O.quantize8 if bits == 8 else O.quantize4)(wt)
+    assert np.array_equal(q, qo) and same_bits(s, so)
+    Q.free(h)
+
+
+def test_quantize_linear_weight_rejects_odd_int4_width_and_unknown_type():
+    import torch
+    L = _lib.load()
+    w = torch.zeros((3, 64), device="cuda")
+    h = ctypes.c_uint64()
+    assert L.tq_quantize4_linear_dev(ctypes.c_void_p(w.data_ptr()), _lib.TQ_LINEAR_F32, 3, 64, None, ctypes.byref(h)) == _lib.TQ_ERR_ARG
+    assert "even column count" in L.tq_last_error().decode()
+    assert L.tq_quantize8_linear_dev(ctypes.c_void_p(w.data_ptr()), 7, 3, 64, None, ctypes.byref(h)) == _lib.TQ_ERR_ARG
+
+
 def test_host_matvec_replays_follow_new_inputs_and_regrown_staging(kernel):
     """Host-pointer MatVec calls replay a captured graph from a matrix's second
     call on: alternating a small and a larger matrix (the larger one regrows
