@@ -413,10 +413,26 @@ def measure_qwen(rank: int, world: int, peak: float, cpu: bool = False):
     with Qwen(QWEN_7B, 1, 0.02, rank, world, nid) as m:
         toks = m.generate(prompt, QWEN_GEN)
         pre_ms, dec_ms = m.last_times_ms
-    t = torch.tensor([pre_ms, dec_ms], device="cuda", dtype=torch.float64)
+        # the same run with the prompt in 64-row chunks on the tf32 matmul
+        # (tq_qwen_set_prefill); every rank takes the same branch
+        btoks, bpre_ms, bwhy = None, 0.0, ""
+        try:
+            m.set_prefill(64)
+            ok = 1
+        except Exception as e:  # a shard layout the batched prefill does not take
+            ok, bwhy = 0, str(e)
+        flag = torch.tensor([ok], device="cuda", dtype=torch.int32)
+        if world > 1:
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if int(flag.item()):
+            btoks = m.generate(prompt, QWEN_GEN)
+            bpre_ms = m.last_times_ms[0]
+        elif not bwhy:
+            bwhy = "another rank's shard layout does not take the batched prefill"
+    t = torch.tensor([pre_ms, dec_ms, bpre_ms], device="cuda", dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    pre_ms, dec_ms = float(t[0]), float(t[1])
+    pre_ms, dec_ms, bpre_ms = float(t[0]), float(t[1]), float(t[2])
     tok_s = (QWEN_GEN - 1) / (dec_ms * 1e-3)
     bound = world * peak * 1e9 / QWEN_BYTES_PER_TOKEN
     rec = {"tp": world, "decode_tok_s": round(tok_s, 2), "ms_per_token": round(dec_ms / (QWEN_GEN - 1), 4),
@@ -424,6 +440,14 @@ def measure_qwen(rank: int, world: int, peak: float, cpu: bool = False):
             "roofline": {"bound": "aggregate hbm", "tok_s_bound": round(bound, 1), "frac": round(tok_s / bound, 4),
                          "bytes_per_token": QWEN_BYTES_PER_TOKEN, "peak_gbs_per_gpu": peak},
             "first_tokens": [int(x) for x in toks[:8]]}
+    if btoks is not None:
+        same = np.asarray(btoks) == np.asarray(toks)
+        rec["batched_prefill"] = {"rows": 64, "prompt_ms": round(bpre_ms, 1),
+                                  "prompt_tok_s": round(QWEN_PROMPT / (bpre_ms * 1e-3), 1),
+                                  "ids_equal_to_token_by_token": int(same.sum()), "of": len(same),
+                                  "first_equal_in_a_row": int(np.argmin(same)) if not same.all() else len(same)}
+    else:
+        rec["batched_prefill"] = {"unavailable": bwhy}
     golden = os.path.join(ROOT, "tests", "golden", "qwen7b_decode_golden_2048_512.npz")
     if os.path.exists(golden):  # the oracle's greedy ids for this prompt and seed (TP does not change them)
         g = np.load(golden)

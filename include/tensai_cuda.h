@@ -313,6 +313,18 @@ TQ_EXPORT int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, 
                                float *times_ms);
 
 /* Releases a model and its NCCL communicator (a second call is a no-op). */
+/* How tq_qwen_generate processes the prompt. rows = 0 (the default) feeds it
+ * token by token through the decode step, as the reference does
+ * (_example/qwen/main.go:229-231): the parity mode. rows in 16..64 runs it in
+ * chunks of that many prompt positions, each layer's matvecs as rows-row
+ * matmuls on the tf32 tensor-core kernel (2e-3 relative L2 per matmul against
+ * the float32 products), RoPE, caches and attention row by row with the
+ * step's numerics; the generated ids may then differ from the parity mode's.
+ * TQ_ERR_UNSUPPORTED when a GPU's shard repeats the attention (more GPUs
+ * than KV heads) or the context exceeds the batched attention's shared
+ * memory. */
+TQ_EXPORT int tq_qwen_set_prefill(uint64_t model, int rows);
+
 TQ_EXPORT int tq_qwen_free(uint64_t model);
 
 /* The shard of the model that rank `rank` of `world` GPUs holds, as

@@ -61,6 +61,7 @@ SIGNATURES = {
     "tq_nccl_unique_id": (I, [P]),
     "tq_qwen_create": (I, [P, U64, F, I, I, P, PU64]),
     "tq_qwen_generate": (I, [U64, P, I, I, P, P]),
+    "tq_qwen_set_prefill": (I, [U64, I]),
     "tq_qwen_free": (I, [U64]),
     "tq_qwen_shard_plan": (I, [P, I, I, P]),
     "tq_chain_create": (I, [P, I, PU64]),

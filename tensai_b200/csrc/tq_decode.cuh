@@ -121,21 +121,42 @@ __global__ void set_state_kernel(int *state, int token, int pos, int generated) 
 // `scale`, softmax in float64, p = float32(score / sum), out += p * v in
 // float32 over positions in order (_example/gpt2/model.go:195-227;
 // _example/qwen/model.go:262-293). Decode: pos from the state; prefill: the
-// row index. Shared memory: ctx doubles + ctx floats.
+// row index plus pos0 (the chunk's first position). Shared memory: ctx
+// doubles + ctx floats.
 __global__ void attention_kernel(const float *q, int qstride, const float *kc, const float *vc, int kvstride,
                                  float *out, int outstride, const int *state, int hd, int group, double scale,
-                                 int prefill, int ctx) {
+                                 int prefill, int ctx, int pos0 = 0) {
     step_entry();
     extern __shared__ double sc[];
     __shared__ double sh[32];
     const int h = blockIdx.x, r = blockIdx.y, kvh = h / group;
-    const int pos = prefill ? r : state[1];
+    const int pos = prefill ? pos0 + r : state[1];
     const float *qr = q + (size_t)r * qstride + h * hd;
     double mx = -INFINITY;
+    const bool vec = (hd & 31) == 0 && ((uintptr_t)qr & 15) == 0 && ((uintptr_t)(kc + kvh * hd) & 15) == 0 &&
+                     (kvstride & 3) == 0;
     for (int t = threadIdx.x; t <= pos; t += blockDim.x) {
         const float *kt = kc + (size_t)t * kvstride + kvh * hd;
         double s = 0;
-        for (int i = 0; i < hd; i++) s = __dadd_rn(s, __dmul_rn((double)qr[i], (double)kt[i]));
+        if (vec) { // 8 float4 loads in flight, then the products in dimension order
+            for (int i0 = 0; i0 < hd; i0 += 32) {
+                float4 kv[8], qv[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    kv[u] = *reinterpret_cast<const float4 *>(kt + i0 + 4 * u);
+                    qv[u] = *reinterpret_cast<const float4 *>(qr + i0 + 4 * u);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    s = __dadd_rn(s, __dmul_rn((double)qv[u].x, (double)kv[u].x));
+                    s = __dadd_rn(s, __dmul_rn((double)qv[u].y, (double)kv[u].y));
+                    s = __dadd_rn(s, __dmul_rn((double)qv[u].z, (double)kv[u].z));
+                    s = __dadd_rn(s, __dmul_rn((double)qv[u].w, (double)kv[u].w));
+                }
+            }
+        } else {
+            for (int i = 0; i < hd; i++) s = __dadd_rn(s, __dmul_rn((double)qr[i], (double)kt[i]));
+        }
         s = __dmul_rn(s, scale);
         sc[t] = s;
         mx = fmax(mx, s);
@@ -153,7 +174,15 @@ __global__ void attention_kernel(const float *q, int qstride, const float *kc, c
     __syncthreads();
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         float acc = 0.f;
-        for (int t = 0; t <= pos; t++) acc = __fadd_rn(acc, __fmul_rn(p[t], vc[(size_t)t * kvstride + kvh * hd + i]));
+        const float *v = vc + kvh * hd + i;
+        for (int t0 = 0; t0 <= pos; t0 += 8) { // 8 loads in flight, then the sum over positions in order
+            float vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) vv[u] = t0 + u <= pos ? v[(size_t)(t0 + u) * kvstride] : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (t0 + u <= pos) acc = __fadd_rn(acc, __fmul_rn(p[t0 + u], vv[u]));
+        }
         out[(size_t)r * outstride + h * hd + i] = acc;
     }
 }

@@ -348,7 +348,7 @@ cudaError_t prefill(Gpt2 &m, const int *prompt, int T) {
         TRY(sgemm(m.XN, bl.attn.w, m.QKV, T, 3 * d, d, m.st));
         qkv_post_kernel<<<T, kThreads, 0, m.st>>>(m.QKV, bl.attnB, bl.kc, bl.vc, m.state, d, 1);
         attention_kernel<<<dim3(m.c.n_head, T), kThreads, attn_smem(m), m.st>>>(
-            m.QKV, 3 * d, bl.kc, bl.vc, d, m.ATT, d, m.state, hd, 1, 0.125 /* 1/sqrt(64) */, 1, m.c.ctx);
+            m.QKV, 3 * d, bl.kc, bl.vc, d, m.ATT, d, m.state, hd, 1, 0.125 /* 1/sqrt(64) */, 1, m.c.ctx, 0);
         TRY(cudaGetLastError());
         TRY(sgemm(m.ATT, bl.proj.w, m.Y, T, d, d, m.st));
         residual_kernel<<<grid_for((size_t)T * d), kThreads, 0, m.st>>>(m.X, m.Y, bl.projB, d, (size_t)T * d);

@@ -129,10 +129,14 @@ __global__ void embed_norm_kernel(const float *embed, const int *state, float *x
 
 // rmsnorm (model.go:182-193): sum of squares in float64, out = float32(v *
 // inv) * w. With y: first the residual add x += y (model.go:276-278 /
-// 301-303), then the norm of the new x, in one launch.
+// 301-303), then the norm of the new x, in one launch. Block b takes row b
+// of [gridDim.x][n] x, y and out (one row in the decode step).
 __global__ void rmsnorm_kernel(float *x, const float *y, const float *w, float *out, int n, double eps) {
     step_entry();
     __shared__ double sh[32];
+    x += (size_t)blockIdx.x * n;
+    out += (size_t)blockIdx.x * n;
+    if (y) y += (size_t)blockIdx.x * n;
     constexpr int B = kNormBatch;
     const int bd = blockDim.x;
     double ss = 0;
@@ -169,6 +173,175 @@ __global__ void rmsnorm_kernel(float *x, const float *y, const float *w, float *
             const int i = i0 + u * bd;
             if (i < n) out[i] = __fmul_rn((float)__dmul_rn((double)a[u], inv), c[u]);
         }
+    }
+}
+
+// ---- batched prefill (rows of a prompt chunk at once) ----
+
+// Row r of a chunk: x[r] = embed[prompt[pos0 + r]] (model.go:239-240) and
+// a[r] = rmsnorm(x[r]) * w, one block per row.
+__global__ void embed_rows_kernel(const float *embed, const int *prompt, int pos0, float *x, const float *w, float *a,
+                                  int d, double eps) {
+    __shared__ double sh[32];
+    const int r = blockIdx.x;
+    const float *row = embed + (size_t)prompt[pos0 + r] * d;
+    float *xr = x + (size_t)r * d, *ar = a + (size_t)r * d;
+    double ss = 0;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float v = row[i];
+        xr[i] = v;
+        ss = __dadd_rn(ss, __dmul_rn((double)v, (double)v));
+    }
+    ss = block_reduce_d(ss, sh, 0);
+    const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)d), eps)));
+    for (int i = threadIdx.x; i < d; i += blockDim.x) ar[i] = __fmul_rn((float)__dmul_rn((double)row[i], inv), w[i]);
+}
+
+// Row r of a chunk's fused q|k|v (position pos0 + r): the biases added, q and
+// k rotated (model.go:244-250, 219-229: half-split pairs, float64), q in place,
+// k and the biased v stored in the caches at the row's position.
+__global__ void rope_rows_kernel(float *qkv, int qkvc, int nq, int nkv, int hd, int pos0, double theta,
+                                 const float *qbias, const float *kbias, const float *vbias, float *kc, float *vc) {
+    __shared__ double cs[kAttMaxHd];
+    const int r = blockIdx.x, pos = pos0 + r, half = hd / 2, kvd = nkv * hd;
+    rope_table(cs, pos, hd, theta);
+    __syncthreads();
+    float *q = qkv + (size_t)r * qkvc, *k = q + nq * hd, *v = k + kvd;
+    for (int e = threadIdx.x; e < nq * half; e += blockDim.x) {
+        const int h = e / half, i = e % half, j = h * hd + i;
+        float r0, r1;
+        rope_pair(cs, i, __fadd_rn(q[j], qbias[j]), __fadd_rn(q[j + half], qbias[j + half]), r0, r1);
+        q[j] = r0;
+        q[j + half] = r1;
+    }
+    float *kd = kc + (size_t)pos * kvd, *vd = vc + (size_t)pos * kvd;
+    for (int e = threadIdx.x; e < nkv * half; e += blockDim.x) {
+        const int h = e / half, i = e % half, j = h * hd + i;
+        float r0, r1;
+        rope_pair(cs, i, __fadd_rn(k[j], kbias[j]), __fadd_rn(k[j + half], kbias[j + half]), r0, r1);
+        kd[j] = r0;
+        kd[j + half] = r1;
+    }
+    for (int j = threadIdx.x; j < kvd; j += blockDim.x) vd[j] = __fadd_rn(v[j], vbias[j]);
+}
+
+// Causal attention of a prompt chunk's rows (model.go:262-293 per row):
+// block (head h, rows r0 .. r0 + kPfRows - 1 of the chunk, positions pos0 +
+// r) stages 64-position tiles of the head's cached k, then v, in shared
+// memory with coalesced loads and uses each tile for all its rows, instead
+// of every row reading the whole cache. Scores s_t = (q . k_t, float64
+// products added in dimension order) * scale stay in shared memory; the
+// softmax is float64 (max, then sum exp(s - max) per row over two warps),
+// p_t = float32(exp(s_t - max) / sum) as the Go code forms it, and out = the
+// sum over positions in order of p_t * v_t in float32.
+constexpr int kPfRows = 4;   // query rows per block
+constexpr int kPfTile = 64;  // cached positions per shared tile
+constexpr int kPfThreads = 256;
+__global__ void __launch_bounds__(kPfThreads) prefill_attention_kernel(const float *qkv, int qkvc, const float *kc,
+                                                                      const float *vc, int kvd, float *out, int outc,
+                                                                      int hd, int group, double scale, int pos0,
+                                                                      int rows, int ctx) {
+    extern __shared__ __align__(16) double pfd[];
+    double *sc = pfd;                                               // [kPfRows][ctx]: scores, then p
+    float *qs = reinterpret_cast<float *>(sc + (size_t)kPfRows * ctx); // [kPfRows][hd]
+    const int TS = hd + 1;                                          // tile row stride: conflict-free rows
+    float *ts = qs + kPfRows * hd;                                  // [kPfTile][TS]: k, then v
+    const int h = blockIdx.x, kvh = h / group, r0 = blockIdx.y * kPfRows;
+    const int nr = min(kPfRows, rows - r0);
+    const int tmax = pos0 + r0 + nr - 1; // the block's last position
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < kPfRows * hd; e += kPfThreads)
+        qs[e] = e / hd < nr ? qkv[(size_t)(r0 + e / hd) * qkvc + h * hd + e % hd] : 0.f;
+    auto load_tile = [&](const float *cache, int k0, int nk) { // coalesced 16-byte loads, padded rows
+        for (int e = threadIdx.x; e < nk * hd / 4; e += kPfThreads) {
+            const int t = e / (hd / 4), i = 4 * (e % (hd / 4));
+            const float4 v = *reinterpret_cast<const float4 *>(cache + (size_t)(k0 + t) * kvd + kvh * hd + i);
+            float *d = ts + t * TS + i;
+            d[0] = v.x;
+            d[1] = v.y;
+            d[2] = v.z;
+            d[3] = v.w;
+        }
+    };
+    // ---- scores: thread (position t of the tile, row rb) ----
+    const int tt = threadIdx.x % kPfTile, rb = threadIdx.x / kPfTile;
+    for (int k0 = 0; k0 <= tmax; k0 += kPfTile) {
+        const int nk = min(kPfTile, tmax - k0 + 1);
+        __syncthreads(); // the previous tile is no longer read
+        load_tile(kc, k0, nk);
+        __syncthreads();
+        if (tt < nk && rb < nr && k0 + tt <= pos0 + r0 + rb) {
+            const float *kt = ts + tt * TS, *qr = qs + rb * hd;
+            double acc = 0;
+            for (int i = 0; i < hd; i++) acc = __dadd_rn(acc, __dmul_rn((double)qr[i], (double)kt[i]));
+            sc[(size_t)rb * ctx + k0 + tt] = __dmul_rn(acc, scale);
+        }
+    }
+    __syncthreads();
+    // ---- softmax per row, in shared memory: warps 2r and 2r + 1 take row r ----
+    {
+        const int r = warp >> 1, half = warp & 1;
+        __shared__ double red[kPfThreads / 32][2];
+        double mx = -INFINITY, sum = 0;
+        const int pos = pos0 + r0 + r;
+        double *srow = sc + (size_t)r * ctx;
+        if (r < nr)
+            for (int t = half * 32 + lane; t <= pos; t += 64) mx = fmax(mx, srow[t]);
+        mx = warp_max_d(mx);
+        if (lane == 0) red[warp][0] = mx;
+        __syncthreads();
+        mx = fmax(red[2 * r][0], red[2 * r + 1][0]);
+        if (r < nr)
+            for (int t = half * 32 + lane; t <= pos; t += 64) sum = __dadd_rn(sum, exp(__dsub_rn(srow[t], mx)));
+        sum = warp_sum_d(sum);
+        if (lane == 0) red[warp][1] = sum;
+        __syncthreads();
+        sum = __dadd_rn(red[2 * r][1], red[2 * r + 1][1]);
+        if (r < nr)
+            for (int t = half * 32 + lane; t <= pos; t += 64)
+                srow[t] = (double)(float)__ddiv_rn(exp(__dsub_rn(srow[t], mx)), sum);
+    }
+    // ---- out = sum over positions in order of p_t v_t: thread (dimension, rows rsl, rsl + nsl, ..) ----
+    const int dsl = threadIdx.x % hd, rsl = threadIdx.x / hd, nsl = kPfThreads / hd;
+    float acc[kPfRows];
+#pragma unroll
+    for (int k = 0; k < kPfRows; k++) acc[k] = 0.f;
+    for (int k0 = 0; k0 <= tmax; k0 += kPfTile) {
+        const int nk = min(kPfTile, tmax - k0 + 1);
+        __syncthreads();
+        load_tile(vc, k0, nk);
+        __syncthreads();
+        if (rsl < nsl) {
+            for (int t = 0; t < nk; t++) {
+                const float v = ts[t * TS + dsl];
+#pragma unroll
+                for (int k = 0; k < kPfRows; k++) {
+                    const int r = rsl + k * nsl;
+                    if (k * nsl < kPfRows && r < nr && k0 + t <= pos0 + r0 + r)
+                        acc[k] = __fadd_rn(acc[k], __fmul_rn((float)sc[(size_t)r * ctx + k0 + t], v));
+                }
+            }
+        }
+    }
+    if (rsl < nsl)
+#pragma unroll
+        for (int k = 0; k < kPfRows; k++) {
+            const int r = rsl + k * nsl;
+            if (k * nsl < kPfRows && r < nr) out[(size_t)(r0 + r) * outc + h * hd + dsl] = acc[k];
+        }
+}
+
+inline size_t prefill_attention_smem(int hd, int ctx) {
+    return sizeof(double) * (size_t)kPfRows * ctx + sizeof(float) * ((size_t)kPfRows * hd + (size_t)kPfTile * (hd + 1));
+}
+
+// h[r][c] = float32(silu(gate)) * up of the fused [gate | up] rows (model.go:296-299).
+__global__ void swiglu_rows_kernel(const float *gu, float *h, int f, int rows) {
+    const size_t total = (size_t)rows * f;
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = e / f, c = e % f;
+        const double g = (double)gu[r * 2 * f + c];
+        h[e] = __fmul_rn((float)__ddiv_rn(g, __dadd_rn(1.0, exp(-g))), gu[r * 2 * f + f + c]);
     }
 }
 
@@ -232,6 +405,8 @@ struct Qwen {
     cudaGraphExec_t graph = nullptr;
     int graph_prompt = -1; // the prompt length baked into the graph (advance_kernel)
     std::vector<void *> allocs;
+    int prefill_rows = 0; // tq_qwen_set_prefill: 0 = token by token (the reference's), else rows per chunk
+    float *px = nullptr, *pa = nullptr, *pqkv = nullptr, *patt = nullptr, *py = nullptr, *pgu = nullptr, *ph = nullptr;
 };
 
 std::mutex g_q_mu;
@@ -416,6 +591,61 @@ cudaError_t step(Qwen &m, int n_prompt) {
     return cudaGetLastError();
 }
 
+// The prompt in chunks of m.prefill_rows rows: each layer's matvecs as M-row
+// matmuls (tq_launch_matmul: the tf32 tensor-core kernel from 16 rows), RoPE
+// and the KV caches per row, the causal attention of each row over the
+// cached positions, the same norms and epilogues as the step; then the last
+// row's logits give the first generated token, and the state ends as the
+// token-by-token prompt leaves it (the prompt's last position, one token
+// generated).
+cudaError_t prefill(Qwen &m, int n_prompt) {
+    const int d = m.c.d, R = m.prefill_rows, qkvc = m.qd + 2 * m.kvd;
+    const double scale = 1.0 / sqrt((double)m.hd);
+    const size_t pf_smem = prefill_attention_smem(m.hd, m.c.ctx);
+    for (int c0 = 0; c0 < n_prompt; c0 += R) {
+        const int rows = n_prompt - c0 < R ? n_prompt - c0 : R;
+        embed_rows_kernel<<<rows, 1024, 0, m.st>>>(m.embed, m.prompt, c0, m.px, m.ones, m.pa, d, m.c.eps);
+        TRY(cudaGetLastError());
+        for (size_t l = 0; l < m.L.size(); l++) {
+            Layer &ly = m.L[l];
+            if (l > 0) { // x += the previous layer's down_proj, then the norm
+                rmsnorm_kernel<<<rows, 1024, 0, m.st>>>(m.px, m.py, m.ones, m.pa, d, m.c.eps);
+                TRY(cudaGetLastError());
+            }
+            TRY(tq_launch_matmul(ly.qkv, m.pa, m.pqkv, rows, m.scr, m.st));
+            rope_rows_kernel<<<rows, 256, 0, m.st>>>(m.pqkv, qkvc, m.nq, m.nkv, m.hd, c0, m.c.theta, m.zeros,
+                                                     m.zeros + m.qd, m.zeros + m.qd + m.kvd, ly.kc, ly.vc);
+            prefill_attention_kernel<<<dim3(m.nq, (rows + kPfRows - 1) / kPfRows), kPfThreads, pf_smem, m.st>>>(
+                m.pqkv, qkvc, ly.kc, ly.vc, m.kvd, m.patt, m.qd, m.hd, m.group, scale, c0, rows, m.c.ctx);
+            TRY(cudaGetLastError());
+            TRY(tq_launch_matmul(ly.o, m.patt, m.py, rows, m.scr, m.st));
+            if (m.world > 1)
+                TRY(nccl_err(g_nccl.allReduce(m.py, m.py, (size_t)rows * d, ncclFloat32, ncclSum, m.comm, m.st)));
+            rmsnorm_kernel<<<rows, 1024, 0, m.st>>>(m.px, m.py, m.ones, m.pa, d, m.c.eps); // x += o_proj, then norm
+            TRY(cudaGetLastError());
+            TRY(tq_launch_matmul(ly.gu, m.pa, m.pgu, rows, m.scr, m.st));
+            swiglu_rows_kernel<<<grid_for((size_t)rows * m.fcols), kThreads, 0, m.st>>>(m.pgu, m.ph, m.fcols, rows);
+            TRY(cudaGetLastError());
+            TRY(tq_launch_matmul(ly.down, m.ph, m.py, rows, m.scr, m.st));
+            if (m.world > 1)
+                TRY(nccl_err(g_nccl.allReduce(m.py, m.py, (size_t)rows * d, ncclFloat32, ncclSum, m.comm, m.st)));
+        }
+    }
+    // the prompt's last row: its final residual add and norm, the lm head, the pick
+    const int last = (n_prompt - 1) % R;
+    set_state_kernel<<<1, 1, 0, m.st>>>(m.state, 0, n_prompt - 1, 0);
+    rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.px + (size_t)last * d, m.py + (size_t)last * d, m.ones, m.a, d, m.c.eps);
+    TRY(cudaGetLastError());
+    TRY(tq_launch_matmul(m.lm, m.a, m.logits, 1, m.scr, m.st));
+    TRY(greedy_pick(m.logits, m.vcols, m.voff, m.part, m.cand, m.state, m.tokens, -1, 0, m.st));
+    if (m.world > 1)
+        TRY(nccl_err(g_nccl.allGather(m.cand, m.cands, 2, ncclInt32, m.comm, m.st)));
+    else
+        TRY(cudaMemcpyAsync(m.cands, m.cand, sizeof(int) * 2, cudaMemcpyDeviceToDevice, m.st));
+    advance_kernel<<<1, 32, 0, m.st>>>(m.cands, m.world, m.state, m.tokens, m.prompt, n_prompt);
+    return cudaGetLastError();
+}
+
 // How rank `rank` of `world` GPUs shards a model (the header's
 // tq_qwen_shard_plan): attention ways wa (world when it divides the KV heads,
 // else the KV heads, repeated over world / n_kv GPUs), this rank's attention
@@ -570,7 +800,11 @@ int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen,
         m->graph_prompt = n_prompt;
     }
     if (e == cudaSuccess) e = cudaEventRecord(ev[0], m->st);
-    for (int i = 0; i < n_prompt && e == cudaSuccess; i++) e = cudaGraphLaunch(m->graph, m->st);
+    if (m->prefill_rows > 0) {
+        if (e == cudaSuccess) e = prefill(*m, n_prompt);
+    } else {
+        for (int i = 0; i < n_prompt && e == cudaSuccess; i++) e = cudaGraphLaunch(m->graph, m->st);
+    }
     if (e == cudaSuccess) e = cudaEventRecord(ev[1], m->st);
     for (int i = 1; i < n_gen && e == cudaSuccess; i++) e = cudaGraphLaunch(m->graph, m->st);
     if (e == cudaSuccess) e = cudaEventRecord(ev[2], m->st);
@@ -600,6 +834,45 @@ int tq_qwen_shard_plan(const tq_qwen_config *cfg, int world, int rank, int *plan
                        sp.ashard * sp.nq * hd, (sp.ashard + 1) * sp.nq * hd, rank * sp.fcols,
                        (rank + 1) * sp.fcols, sp.voff,               sp.voff + sp.vcols};
     std::memcpy(plan, v, sizeof v);
+    return TQ_OK;
+}
+
+int tq_qwen_set_prefill(uint64_t model, int rows) {
+    int rc = TQ_OK;
+    auto m = find(model, &rc);
+    if (!m) return rc;
+    if (rows != 0 && (rows < TQ_MM_MIN_ROWS || rows > TQ_MM_MAX_ROWS))
+        return tq_fail(TQ_ERR_ARG, "tensai: prefill rows must be 0 or %d..%d, got %d", TQ_MM_MIN_ROWS, TQ_MM_MAX_ROWS,
+                       rows);
+    if (rows == 0) {
+        m->prefill_rows = 0;
+        return TQ_OK;
+    }
+    if (m->arow != 0 || m->orows != m->qd)
+        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: batched prefill needs each GPU's attention heads to be its own "
+                                           "(this shard repeats the attention: more GPUs than KV heads)");
+    if (m->hd % 4 || m->hd > kAttMaxHd || kPfThreads % m->hd)
+        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: batched prefill attention takes head sizes dividing %d",
+                       kPfThreads);
+    const size_t smem = prefill_attention_smem(m->hd, m->c.ctx);
+    if (smem > 227 * 1024)
+        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: batched prefill attention keeps %d rows of scores per block in "
+                                           "shared memory: a context of %d positions is too long", kPfRows, m->c.ctx);
+    cudaError_t e = cudaSetDevice(m->device);
+    if (e == cudaSuccess && smem > 48 * 1024)
+        e = cudaFuncSetAttribute(prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "prefill set-up");
+    if (rows > m->prefill_rows) {
+        const int d = m->c.d, qkvc = m->qd + 2 * m->kvd;
+        const std::pair<float **, size_t> bufs[] = {
+            {&m->px, (size_t)d}, {&m->pa, (size_t)d}, {&m->pqkv, (size_t)qkvc}, {&m->patt, (size_t)m->qd},
+            {&m->py, (size_t)d}, {&m->pgu, 2 * (size_t)m->fcols}, {&m->ph, (size_t)m->fcols}};
+        for (const auto &b : bufs)
+            if ((e = dalloc(*m, (void **)b.first, sizeof(float) * rows * b.second)) != cudaSuccess)
+                return tq_cuda_fail(e, "prefill buffers");
+        if ((rc = tq_scratch_for(m->device, m->st, &m->scr, rows)) != TQ_OK) return rc; // the matmul's partials
+    }
+    m->prefill_rows = rows;
     return TQ_OK;
 }
 

@@ -132,6 +132,12 @@ class Qwen:
         self.last_times_ms = (t[0], t[1])
         return out
 
+    def set_prefill(self, rows: int) -> None:
+        """0: the prompt token by token through the decode step (the reference's
+        way, the parity mode); 16..64: in chunks of that many rows on the tf32
+        tensor-core matmul (tq_qwen_set_prefill)."""
+        _lib.check(_lib.load().tq_qwen_set_prefill(self.handle, rows))
+
     def free(self) -> None:
         if self.handle:
             _lib.load().tq_qwen_free(self.handle)

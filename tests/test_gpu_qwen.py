@@ -72,6 +72,50 @@ def test_qwen7b_shape_matches_golden_tokens(path):
     assert np.array_equal(got, z["tokens"]), _diverge(got, z["tokens"], z["margins"])
 
 
+@pytest.mark.parametrize("rows,seed", [(16, 1), (64, 2)])
+def test_batched_prefill_tiny_qwen(rows, seed):
+    """The prompt in chunks of `rows` positions (tq_qwen_set_prefill): 40
+    prompt tokens (with rows=16 two full chunks and a ragged one of 8, which
+    runs on the matvec kernels), each layer's matvecs as tf32 matmuls. The
+    generated ids are the oracle's token-by-token ids here (the parity mode
+    is checked alongside), and switching back restores the parity mode."""
+    prompt = synth_tokens(40, TINY["vocab"], seed)
+    want, margins = O.qwen_generate(TINY, seed, 0.02, prompt, 20)
+    with Qwen(TINY, seed) as m:
+        m.set_prefill(rows)
+        got = m.generate(prompt, 20)
+        m.set_prefill(0)
+        ref = m.generate(prompt, 20)
+    assert np.array_equal(ref, want), _diverge(ref, want, margins)
+    assert np.array_equal(got, want), _diverge(got, want, margins)
+
+
+def test_batched_prefill_rejects_bad_rows():
+    with Qwen(TINY, 1) as m:
+        for rows in (8, 65, -1):
+            with pytest.raises(_lib.TensaiError) as e:
+                m.set_prefill(rows)
+            assert e.value.code == _lib.TQ_ERR_ARG
+
+
+def test_qwen7b_shape_batched_prefill_agreement():
+    """The 7B shape with its 64-token prompt as one 64-row chunk: the tf32
+    matmuls change the prompt's hidden states slightly, so agreement with the
+    golden token-by-token ids is reported (printed) rather than required
+    beyond the first generated id."""
+    z = np.load(os.path.join(GOLDEN, "qwen7b_decode_golden_64_32.npz"))
+    n_prompt, n_gen = len(z["prompt"]), len(z["tokens"])
+    cfg = dict(QWEN_7B, ctx=n_prompt + n_gen)
+    with Qwen(cfg, int(z["seed"]), float(z["sigma"])) as m:
+        m.set_prefill(64)
+        got = m.generate(z["prompt"], n_gen)
+    same = np.asarray(got) == np.asarray(z["tokens"])
+    lead = int(np.argmin(same)) if not same.all() else len(same)
+    print(f"batched prefill, 7B shape: {int(same.sum())}/{n_gen} ids equal to the token-by-token golden, "
+          f"first {lead} in a row")
+    assert got[0] == z["tokens"][0], _diverge(got, z["tokens"], z["margins"])
+
+
 def _tp_worker(rank, world, port, q, cfg, seed, prompt, n):
     import torch
     import torch.distributed as dist
