@@ -243,15 +243,16 @@ __global__ void __launch_bounds__(kPfThreads) prefill_attention_kernel(const flo
                                                                       int rows, int ctx) {
     extern __shared__ __align__(16) double pfd[];
     double *sc = pfd;                                               // [kPfRows][ctx]: scores, then p
-    float *qs = reinterpret_cast<float *>(sc + (size_t)kPfRows * ctx); // [kPfRows][hd]
+    double *qs = sc + (size_t)kPfRows * ctx;                        // [kPfRows][hd], widened once
     const int TS = hd + 1;                                          // tile row stride: conflict-free rows
-    float *ts = qs + kPfRows * hd;                                  // [kPfTile][TS]: k, then v
+    float *ts = reinterpret_cast<float *>(qs + kPfRows * hd);      // [kPfTile][TS]: k, then v
+    float *ps = ts + kPfTile * TS;                                  // [kPfRows][kPfTile]: the tile's p
     const int h = blockIdx.x, kvh = h / group, r0 = blockIdx.y * kPfRows;
     const int nr = min(kPfRows, rows - r0);
     const int tmax = pos0 + r0 + nr - 1; // the block's last position
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < kPfRows * hd; e += kPfThreads)
-        qs[e] = e / hd < nr ? qkv[(size_t)(r0 + e / hd) * qkvc + h * hd + e % hd] : 0.f;
+        qs[e] = e / hd < nr ? (double)qkv[(size_t)(r0 + e / hd) * qkvc + h * hd + e % hd] : 0.0;
     auto load_tile = [&](const float *cache, int k0, int nk) { // coalesced 16-byte loads, padded rows
         for (int e = threadIdx.x; e < nk * hd / 4; e += kPfThreads) {
             const int t = e / (hd / 4), i = 4 * (e % (hd / 4));
@@ -271,9 +272,10 @@ __global__ void __launch_bounds__(kPfThreads) prefill_attention_kernel(const flo
         load_tile(kc, k0, nk);
         __syncthreads();
         if (tt < nk && rb < nr && k0 + tt <= pos0 + r0 + rb) {
-            const float *kt = ts + tt * TS, *qr = qs + rb * hd;
+            const float *kt = ts + tt * TS;
+            const double *qr = qs + rb * hd;
             double acc = 0;
-            for (int i = 0; i < hd; i++) acc = __dadd_rn(acc, __dmul_rn((double)qr[i], (double)kt[i]));
+            for (int i = 0; i < hd; i++) acc = __dadd_rn(acc, __dmul_rn(qr[i], (double)kt[i]));
             sc[(size_t)rb * ctx + k0 + tt] = __dmul_rn(acc, scale);
         }
     }
@@ -310,16 +312,21 @@ __global__ void __launch_bounds__(kPfThreads) prefill_attention_kernel(const flo
         const int nk = min(kPfTile, tmax - k0 + 1);
         __syncthreads();
         load_tile(vc, k0, nk);
+        for (int e = threadIdx.x; e < kPfRows * kPfTile; e += kPfThreads) { // the tile's p, as float, once
+            const int r = e / kPfTile, t = e % kPfTile;
+            ps[e] = (r < nr && t < nk && k0 + t <= pos0 + r0 + r) ? (float)sc[(size_t)r * ctx + k0 + t] : 0.f;
+        }
         __syncthreads();
         if (rsl < nsl) {
-            for (int t = 0; t < nk; t++) {
-                const float v = ts[t * TS + dsl];
 #pragma unroll
-                for (int k = 0; k < kPfRows; k++) {
-                    const int r = rsl + k * nsl;
-                    if (k * nsl < kPfRows && r < nr && k0 + t <= pos0 + r0 + r)
-                        acc[k] = __fadd_rn(acc[k], __fmul_rn((float)sc[(size_t)r * ctx + k0 + t], v));
-                }
+            for (int k = 0; k < kPfRows; k++) {
+                const int r = rsl + k * nsl;
+                if (k * nsl >= kPfRows || r >= nr) break;
+                const int lim = min(nk, pos0 + r0 + r - k0 + 1); // this row's positions in the tile
+                const float *pr = ps + r * kPfTile;
+                float a = acc[k];
+                for (int t = 0; t < lim; t++) a = __fadd_rn(a, __fmul_rn(pr[t], ts[t * TS + dsl]));
+                acc[k] = a;
             }
         }
     }
@@ -332,7 +339,8 @@ __global__ void __launch_bounds__(kPfThreads) prefill_attention_kernel(const flo
 }
 
 inline size_t prefill_attention_smem(int hd, int ctx) {
-    return sizeof(double) * (size_t)kPfRows * ctx + sizeof(float) * ((size_t)kPfRows * hd + (size_t)kPfTile * (hd + 1));
+    return sizeof(double) * ((size_t)kPfRows * ctx + (size_t)kPfRows * hd) +
+           sizeof(float) * ((size_t)kPfTile * (hd + 1) + (size_t)kPfRows * kPfTile);
 }
 
 // h[r][c] = float32(silu(gate)) * up of the fused [gate | up] rows (model.go:296-299).
