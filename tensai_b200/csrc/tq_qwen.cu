@@ -240,7 +240,7 @@ constexpr int kPfThreads = 256;
 __global__ void __launch_bounds__(kPfThreads) prefill_attention_kernel(const float *qkv, int qkvc, const float *kc,
                                                                       const float *vc, int kvd, float *out, int outc,
                                                                       int hd, int group, double scale, int pos0,
-                                                                      int rows, int ctx) {
+                                                                      int rows, int ctx /* scores row stride: >= the last position + 1 */) {
     extern __shared__ __align__(16) double pfd[];
     double *sc = pfd;                                               // [kPfRows][ctx]: scores, then p
     double *qs = sc + (size_t)kPfRows * ctx;                        // [kPfRows][hd], widened once
@@ -609,7 +609,9 @@ cudaError_t step(Qwen &m, int n_prompt) {
 cudaError_t prefill(Qwen &m, int n_prompt) {
     const int d = m.c.d, R = m.prefill_rows, qkvc = m.qd + 2 * m.kvd;
     const double scale = 1.0 / sqrt((double)m.hd);
-    const size_t pf_smem = prefill_attention_smem(m.hd, m.c.ctx);
+    // rows of scores are as long as the prompt (not the context), so that two
+    // blocks fit per SM for prompts up to about 2,600 positions
+    const size_t pf_smem = prefill_attention_smem(m.hd, n_prompt);
     for (int c0 = 0; c0 < n_prompt; c0 += R) {
         const int rows = n_prompt - c0 < R ? n_prompt - c0 : R;
         embed_rows_kernel<<<rows, 1024, 0, m.st>>>(m.embed, m.prompt, c0, m.px, m.ones, m.pa, d, m.c.eps);
@@ -624,7 +626,7 @@ cudaError_t prefill(Qwen &m, int n_prompt) {
             rope_rows_kernel<<<rows, 256, 0, m.st>>>(m.pqkv, qkvc, m.nq, m.nkv, m.hd, c0, m.c.theta, m.zeros,
                                                      m.zeros + m.qd, m.zeros + m.qd + m.kvd, ly.kc, ly.vc);
             prefill_attention_kernel<<<dim3(m.nq, (rows + kPfRows - 1) / kPfRows), kPfThreads, pf_smem, m.st>>>(
-                m.pqkv, qkvc, ly.kc, ly.vc, m.kvd, m.patt, m.qd, m.hd, m.group, scale, c0, rows, m.c.ctx);
+                m.pqkv, qkvc, ly.kc, ly.vc, m.kvd, m.patt, m.qd, m.hd, m.group, scale, c0, rows, n_prompt);
             TRY(cudaGetLastError());
             TRY(tq_launch_matmul(ly.o, m.patt, m.py, rows, m.scr, m.st));
             if (m.world > 1)
