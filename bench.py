@@ -411,6 +411,7 @@ def measure_qwen(rank: int, world: int, peak: float, cpu: bool = False):
     prompt = synth_tokens(QWEN_PROMPT, QWEN_7B["vocab"], 1)
     nid = broadcast_nccl_id(dist) if world > 1 else None
     with Qwen(QWEN_7B, 1, 0.02, rank, world, nid) as m:
+        exchange = m.exchange
         toks = m.generate(prompt, QWEN_GEN)
         pre_ms, dec_ms = m.last_times_ms
         # the same run with the prompt in 64-row chunks on the tf32 matmul
@@ -435,7 +436,7 @@ def measure_qwen(rank: int, world: int, peak: float, cpu: bool = False):
     pre_ms, dec_ms, bpre_ms = float(t[0]), float(t[1]), float(t[2])
     tok_s = (QWEN_GEN - 1) / (dec_ms * 1e-3)
     bound = world * peak * 1e9 / QWEN_BYTES_PER_TOKEN
-    rec = {"tp": world, "decode_tok_s": round(tok_s, 2), "ms_per_token": round(dec_ms / (QWEN_GEN - 1), 4),
+    rec = {"tp": world, "exchange": exchange, "decode_tok_s": round(tok_s, 2), "ms_per_token": round(dec_ms / (QWEN_GEN - 1), 4),
             "prompt_ms": round(pre_ms, 1), "prompt_tok_s": round(QWEN_PROMPT / (pre_ms * 1e-3), 1),
             "roofline": {"bound": "aggregate hbm", "tok_s_bound": round(bound, 1), "frac": round(tok_s / bound, 4),
                          "bytes_per_token": QWEN_BYTES_PER_TOKEN, "peak_gbs_per_gpu": peak},

@@ -312,7 +312,6 @@ TQ_EXPORT int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sig
 TQ_EXPORT int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen, int *tokens,
                                float *times_ms);
 
-/* Releases a model and its NCCL communicator (a second call is a no-op). */
 /* How tq_qwen_generate processes the prompt. rows = 0 (the default) feeds it
  * token by token through the decode step, as the reference does
  * (_example/qwen/main.go:229-231): the parity mode. rows in 16..64 runs it in
@@ -325,6 +324,23 @@ TQ_EXPORT int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, 
  * memory. */
 TQ_EXPORT int tq_qwen_set_prefill(uint64_t model, int rows);
 
+/* How the ranks of a tensor-parallel model exchange partial sums in the
+ * decode step: *kind = TQ_EXCHANGE_NONE (world 1), TQ_EXCHANGE_NCCL (NCCL
+ * all-reduce and all-gather) or TQ_EXCHANGE_PEER (one kernel per exchange
+ * that stores this rank's partial into every peer's memory over NVLink,
+ * sums all ranks' partials in rank order and applies the residual add and
+ * RMSNorm after it; the candidates of the lm head likewise). tq_qwen_create
+ * picks PEER when every rank can map every other rank's memory (CUDA IPC,
+ * at most 8 GPUs) unless the environment variable TENSAI_QWEN_EXCHANGE is
+ * "nccl" on a rank. A peer that does not arrive within 2 s fails
+ * tq_qwen_generate with TQ_ERR_TIMEOUT. The batched prefill's all-reduces
+ * use NCCL either way. */
+#define TQ_EXCHANGE_NONE 0
+#define TQ_EXCHANGE_NCCL 1
+#define TQ_EXCHANGE_PEER 2
+TQ_EXPORT int tq_qwen_exchange(uint64_t model, int *kind);
+
+/* Releases a model and its NCCL communicator (a second call is a no-op). */
 TQ_EXPORT int tq_qwen_free(uint64_t model);
 
 /* The shard of the model that rank `rank` of `world` GPUs holds, as

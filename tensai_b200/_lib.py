@@ -62,6 +62,7 @@ SIGNATURES = {
     "tq_qwen_create": (I, [P, U64, F, I, I, P, PU64]),
     "tq_qwen_generate": (I, [U64, P, I, I, P, P]),
     "tq_qwen_set_prefill": (I, [U64, I]),
+    "tq_qwen_exchange": (I, [U64, ctypes.POINTER(ctypes.c_int)]),
     "tq_qwen_free": (I, [U64]),
     "tq_qwen_shard_plan": (I, [P, I, I, P]),
     "tq_chain_create": (I, [P, I, PU64]),
@@ -76,6 +77,9 @@ ABI_VERSION = 1
 TQ_LINEAR_F32 = 0
 TQ_LINEAR_F16 = 1
 TQ_LINEAR_BF16 = 2
+TQ_EXCHANGE_NONE = 0
+TQ_EXCHANGE_NCCL = 1
+TQ_EXCHANGE_PEER = 2
 TQ_CHAIN_EPI_NONE = 0
 TQ_CHAIN_EPI_SWIGLU = 1
 TQ_CHAIN_EPI_RESID = 2

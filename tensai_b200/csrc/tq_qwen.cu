@@ -28,6 +28,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -42,10 +43,13 @@
 #define TQ_DECODE_PDL 0
 #include "tq_decode.cuh"
 #include "tq_internal.h"
+#include "tq_ptx.cuh"
 
 namespace {
 
 using namespace tqd_qwen;
+using tqp::global_ns;
+using tqp::kWaitNs;
 
 // ---- NCCL, resolved at run time -----------------------------------------------
 struct Nccl {
@@ -388,6 +392,185 @@ __global__ void copy_cols_kernel(const float *in, int in_cols, int in_col0, floa
     }
 }
 
+// ---- one-shot exchange over NVLink peer memory -----------------------------------
+// Each rank owns a slot area of [2 parities][world][cap] 8-byte words in its
+// own HBM, mapped into every other rank by CUDA IPC. Exchange call e (1, 2, …
+// counted per rank in ctl[0]; every rank makes the same calls) stores the
+// rank's words (e << 32 | payload) into slot[e & 1][rank] of every peer, then
+// waits in its own area for the words of epoch e from every peer. A 64-bit
+// store arrives whole, so the epoch half vouches for the payload half: no
+// fence or flag round trip. Two parities suffice: a rank stores into parity
+// (e + 2) & 1 only after it has every peer's words of call e + 1, which a peer
+// sends only after it has finished reading call e.
+// Every wait is bounded (kWaitNs): a wait that runs out sets TQ_STATUS_TIMEOUT
+// and ctl[1], after which later calls wait no more (their sums are garbage;
+// the status fails the generate call).
+constexpr int kArMaxWorld = 8;
+constexpr int kArBatch = 8; // words loaded per thread before the first check
+struct ArLink {
+    unsigned long long *slot[kArMaxWorld]; // rank r's slot area as mapped here (own included)
+    unsigned *ctl;                         // [0] calls done, [1] a wait ran out
+    int world, rank, cap;
+};
+
+__device__ __forceinline__ void st_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ bool ar_is(unsigned long long w, unsigned e) { return (unsigned)(w >> 32) == e; }
+
+// One thread: bounded wait for the word at p to carry epoch e.
+__device__ __noinline__ unsigned long long ar_wait(const unsigned long long *p, unsigned e, volatile int *abort,
+                                                   unsigned *ctl, unsigned *status) {
+    unsigned long long v = ld_sys_u64(p);
+    if (ar_is(v, e) || *abort) return v;
+    const unsigned long long t0 = global_ns();
+    for (unsigned it = 1;; it++) {
+        __nanosleep(32);
+        v = ld_sys_u64(p);
+        if (ar_is(v, e) || *abort) return v;
+        if ((it & 63) == 0 && global_ns() - t0 > kWaitNs) {
+            atomicOr(status, TQ_STATUS_TIMEOUT);
+            *abort = 1;
+            ctl[1] = 1;
+            return v;
+        }
+    }
+}
+
+// x += the sum over ranks of y (rank order, so every rank holds the same
+// bits), then out = RMSNorm(x) * w: the o_proj / down_proj all-reduce fused
+// with the residual add and norm after it (rmsnorm_kernel's numerics). One
+// block; peers' words are staged in dynamic shared memory ((world-1) x n floats).
+__global__ void __launch_bounds__(1024) ar_rmsnorm_kernel(ArLink L, float *x, const float *y, const float *w,
+                                                          float *out, int n, double eps, unsigned *status) {
+    step_entry();
+    extern __shared__ float recv[]; // [world-1][n], peers in the order rank+1, rank+2, …
+    __shared__ double sh[32];
+    __shared__ unsigned long long *slot[kArMaxWorld];
+    __shared__ unsigned s_e;
+    __shared__ volatile int abort;
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int r = 0; r < kArMaxWorld; r++) slot[r] = L.slot[r]; // constant indexes: no local copy
+    }
+    if (threadIdx.x == 0) {
+        s_e = L.ctl[0] + 1;
+        abort = L.ctl[1] != 0;
+    }
+    __syncthreads();
+    const unsigned e = s_e;
+    const int bd = blockDim.x, np = L.world - 1;
+    const size_t par = (size_t)(e & 1) * L.world * L.cap;
+    for (int i = threadIdx.x; i < n; i += bd) {
+        const unsigned long long wd = ((unsigned long long)e << 32) | __float_as_uint(y[i]);
+        for (int k = 1; k <= np; k++) {
+            const int r = L.rank + k < L.world ? L.rank + k : L.rank + k - L.world;
+            st_sys_u64(slot[r] + par + (size_t)L.rank * L.cap + i, wd);
+        }
+    }
+    const unsigned long long *mine = slot[L.rank] + par;
+    const int total = np * n;
+    for (int f0 = threadIdx.x; f0 < total; f0 += kArBatch * bd) {
+        unsigned long long v[kArBatch];
+#pragma unroll
+        for (int u = 0; u < kArBatch; u++) {
+            const int f = f0 + u * bd;
+            if (f < total) {
+                const int k = f / n, i = f - k * n;
+                const int r = L.rank + 1 + k < L.world ? L.rank + 1 + k : L.rank + 1 + k - L.world;
+                v[u] = ld_sys_u64(mine + (size_t)r * L.cap + i);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kArBatch; u++) {
+            const int f = f0 + u * bd;
+            if (f < total) {
+                const int k = f / n, i = f - k * n;
+                const int r = L.rank + 1 + k < L.world ? L.rank + 1 + k : L.rank + 1 + k - L.world;
+                if (!ar_is(v[u], e)) v[u] = ar_wait(mine + (size_t)r * L.cap + i, e, &abort, L.ctl, status);
+                recv[f] = __uint_as_float((unsigned)v[u]);
+            }
+        }
+    }
+    __syncthreads();
+    double ss = 0;
+    for (int i = threadIdx.x; i < n; i += bd) {
+        float s = 0.f;
+        for (int r = 0; r < L.world; r++) {
+            const int k = r > L.rank ? r - L.rank - 1 : r + L.world - L.rank - 1;
+            const float t = r == L.rank ? y[i] : recv[(size_t)k * n + i];
+            s = r == 0 ? t : __fadd_rn(s, t);
+        }
+        const float xv = __fadd_rn(x[i], s);
+        x[i] = xv;
+        ss = __dadd_rn(ss, __dmul_rn((double)xv, (double)xv));
+    }
+    ss = block_reduce_d(ss, sh, 0);
+    const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)n), eps)));
+    for (int i = threadIdx.x; i < n; i += bd) out[i] = __fmul_rn((float)__dmul_rn((double)x[i], inv), w[i]);
+    if (threadIdx.x == 0) L.ctl[0] = e; // every thread read s_e before block_reduce_d's barriers
+}
+
+// The lm-head candidates (value, id) of every rank gathered over the same
+// slots, then advance_kernel's pick: one launch for the gather and the step's
+// last kernel.
+__global__ void ar_advance_kernel(ArLink L, const int *cand, int *cands, int *state, int *tokens, const int *prompt,
+                                  int n_prompt, unsigned *status) {
+    step_entry();
+    __shared__ unsigned long long *slot[kArMaxWorld];
+    __shared__ unsigned s_e;
+    __shared__ volatile int abort;
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int r = 0; r < kArMaxWorld; r++) slot[r] = L.slot[r]; // constant indexes: no local copy
+    }
+    if (threadIdx.x == 0) {
+        s_e = L.ctl[0] + 1;
+        abort = L.ctl[1] != 0;
+    }
+    __syncthreads();
+    const unsigned e = s_e;
+    const size_t par = (size_t)(e & 1) * L.world * L.cap;
+    const int t = threadIdx.x;
+    if (t < 2) {
+        const unsigned long long wd = ((unsigned long long)e << 32) | (unsigned)cand[t];
+        for (int r = 0; r < L.world; r++)
+            if (r != L.rank) st_sys_u64(slot[r] + par + (size_t)L.rank * L.cap + t, wd);
+        cands[2 * L.rank + t] = cand[t];
+    }
+    if (t < 2 * L.world && t / 2 != L.rank) {
+        const unsigned long long *p = slot[L.rank] + par + (size_t)(t / 2) * L.cap + (t & 1);
+        unsigned long long v = ld_sys_u64(p);
+        if (!ar_is(v, e)) v = ar_wait(p, e, &abort, L.ctl, status);
+        cands[t] = (int)(unsigned)v;
+    }
+    __syncthreads();
+    if (t != 0) return;
+    __threadfence_block();
+    const int pos = state[1];
+    if (pos + 1 < n_prompt) {
+        state[0] = prompt[pos + 1];
+    } else {
+        float best = __int_as_float(cands[0]);
+        int idx = cands[1];
+        for (int k = 1; k < L.world; k++) {
+            const float v = __int_as_float(cands[2 * k]);
+            const int i = cands[2 * k + 1];
+            if (v > best || (v == best && i < idx)) best = v, idx = i;
+        }
+        tokens[state[2]] = idx;
+        state[0] = idx;
+        state[2] += 1;
+    }
+    state[1] = pos + 1;
+    L.ctl[0] = e;
+}
+
 // ---- engine -------------------------------------------------------------------
 struct Layer {
     TqMatrixDev qkv{}, o{}, gu{}, down{};
@@ -415,6 +598,11 @@ struct Qwen {
     std::vector<void *> allocs;
     int prefill_rows = 0; // tq_qwen_set_prefill: 0 = token by token (the reference's), else rows per chunk
     float *px = nullptr, *pa = nullptr, *pqkv = nullptr, *patt = nullptr, *py = nullptr, *pgu = nullptr, *ph = nullptr;
+    // the decode step's exchange: over peer memory (ar_on) or NCCL
+    bool ar_on = false;
+    ArLink ar{};
+    unsigned long long *ar_area = nullptr; // this rank's slot area (exported by IPC)
+    size_t ar_smem = 0;                    // ar_rmsnorm_kernel's dynamic shared memory
 };
 
 std::mutex g_q_mu;
@@ -442,6 +630,12 @@ void destroy(Qwen &m) {
     if (m.st) cudaStreamSynchronize(m.st);
     if (m.graph) cudaGraphExecDestroy(m.graph); // before the communicator it holds
     m.graph = nullptr;
+    for (int r = 0; r < kArMaxWorld; r++)
+        if (r != m.rank && m.ar.slot[r]) cudaIpcCloseMemHandle(m.ar.slot[r]);
+    if (m.ar_area) cudaFree(m.ar_area);
+    m.ar = ArLink{};
+    m.ar_area = nullptr;
+    m.ar_on = false;
     if (m.comm) g_nccl.commDestroy(m.comm);
     m.comm = nullptr;
     for (Layer &l : m.L)
@@ -553,6 +747,80 @@ cudaError_t build(Qwen &m, uint64_t seed, float sigma, int *rc) {
 
 cudaError_t nccl_err(ncclResult_t r) { return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown; }
 
+// Each rank's value of v gathered over NCCL (host ints, a few bytes each).
+cudaError_t gather_host(Qwen &m, const void *v, size_t bytes, void *all) {
+    void *dv = nullptr;
+    cudaError_t e = cudaMalloc(&dv, bytes * (m.world + 1));
+    if (e != cudaSuccess) return e;
+    char *mine = (char *)dv + bytes * m.world;
+    e = cudaMemcpyAsync(mine, v, bytes, cudaMemcpyHostToDevice, m.st);
+    if (e == cudaSuccess) e = nccl_err(g_nccl.allGather(mine, dv, bytes, ncclInt8, m.comm, m.st));
+    if (e == cudaSuccess) e = cudaMemcpyAsync(all, dv, bytes * m.world, cudaMemcpyDeviceToHost, m.st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m.st);
+    cudaFree(dv);
+    return e;
+}
+
+// Sets up the decode step's exchange over peer memory (world > 1): the slot
+// area, its IPC handle gathered over NCCL, every peer's area opened here. All
+// ranks take the same steps and agree (a rank that cannot, or whose
+// TENSAI_QWEN_EXCHANGE is "nccl", makes every rank keep the NCCL
+// all-reduce). Errors of the agreement itself fail the model build.
+cudaError_t ar_setup(Qwen &m) {
+    const char *env = getenv("TENSAI_QWEN_EXCHANGE");
+    const int cap = ((m.c.d > 2 ? m.c.d : 2) + 31) & ~31;
+    const size_t smem = sizeof(float) * (size_t)(m.world - 1) * m.c.d;
+    int ok = m.world <= kArMaxWorld && smem <= 200 * 1024 && !(env && !strcmp(env, "nccl"));
+    const size_t bytes = sizeof(unsigned long long) * 2 * m.world * cap;
+    if (ok) ok = cudaMalloc((void **)&m.ar_area, bytes) == cudaSuccess;
+    if (ok) ok = cudaMemsetAsync(m.ar_area, 0, bytes, m.st) == cudaSuccess;
+    if (ok && smem > 48 * 1024)
+        ok = cudaFuncSetAttribute(ar_rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+             cudaSuccess;
+    struct Rec {
+        cudaIpcMemHandle_t h;
+        int ok, pad[15];
+    } rec{};
+    if (ok) ok = cudaIpcGetMemHandle(&rec.h, m.ar_area) == cudaSuccess;
+    if (ok) ok = cudaStreamSynchronize(m.st) == cudaSuccess; // zeroed before any peer can see it
+    rec.ok = ok;
+    cudaGetLastError(); // a failed optional step above leaves no sticky error
+    std::vector<Rec> all(m.world);
+    TRY(gather_host(m, &rec, sizeof rec, all.data()));
+    for (const Rec &r : all) ok = ok && r.ok;
+    for (int r = 0; r < m.world && ok; r++) {
+        if (r == m.rank) {
+            m.ar.slot[r] = m.ar_area;
+            continue;
+        }
+        void *p = nullptr;
+        ok = cudaIpcOpenMemHandle(&p, all[r].h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        if (ok) m.ar.slot[r] = (unsigned long long *)p;
+    }
+    cudaGetLastError();
+    std::vector<int> okv(m.world);
+    TRY(gather_host(m, &ok, sizeof ok, okv.data()));
+    for (int v : okv) ok = ok && v;
+    if (ok) {
+        unsigned *ctl = nullptr;
+        TRY(dalloc(m, (void **)&ctl, sizeof(unsigned) * 2));
+        TRY(cudaMemsetAsync(ctl, 0, sizeof(unsigned) * 2, m.st));
+        m.ar.ctl = ctl;
+        m.ar.world = m.world;
+        m.ar.rank = m.rank;
+        m.ar.cap = cap;
+        m.ar_smem = smem;
+        m.ar_on = true;
+        return cudaStreamSynchronize(m.st);
+    }
+    for (int r = 0; r < kArMaxWorld; r++)
+        if (r != m.rank && m.ar.slot[r]) cudaIpcCloseMemHandle(m.ar.slot[r]);
+    if (m.ar_area) cudaFree(m.ar_area);
+    m.ar = ArLink{};
+    m.ar_area = nullptr;
+    return cudaSuccess;
+}
+
 // One step (model.go:232-307) for the state's token at the state's position.
 // The gate|up matvec ends with SiLU(gate) * up; the attention's scores pass
 // applies RoPE and fills the caches. A residual add and the RMSNorm after it
@@ -570,27 +838,35 @@ cudaError_t step(Qwen &m, int n_prompt) {
     rope.qbias = m.zeros;
     rope.kbias = m.zeros + m.qd;
     rope.vbias = m.zeros + m.qd + m.kvd;
-    const float *pending = nullptr; // residual still to be added to x (the previous down_proj output)
+    // x += the all-reduced y (an o_proj or down_proj output), then a = RMSNorm(x)
+    auto add_norm = [&]() -> cudaError_t {
+        if (m.ar_on)
+            return step_launch(ar_rmsnorm_kernel, dim3(1), dim3(1024), m.ar_smem, m.st, m.ar, m.x, m.y, m.ones, m.a,
+                               d, m.c.eps, m.scr.status);
+        if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
+        return step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, m.y, m.ones, m.a, d, m.c.eps);
+    };
+    bool pending = false; // the previous down_proj output is still to be added to x
     for (Layer &ly : m.L) {
-        if (pending)
-            TRY(step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, pending, m.ones, m.a, d, m.c.eps));
+        if (pending) TRY(add_norm());
         TRY(tq_launch_matmul(ly.qkv, m.a, m.qkv, 1, m.scr, m.st));
         rope.kc = ly.kc;
         rope.vc = ly.vc;
         TRY(decode_attention(m.qkv, ly.kc, ly.vc, m.kvd, m.att, m.state, m.nq, m.hd, m.group,
                              1.0 / sqrt((double)m.hd), m.att_scr, m.st, rope));
         TRY(tq_launch_matmul(ly.o, m.att + m.arow, m.y, 1, m.scr, m.st));
-        if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
-        TRY(step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, m.y, m.ones, m.a, d, m.c.eps)); // x += o_proj, then norm
+        TRY(add_norm()); // x += o_proj, then norm
         TRY(tq_launch_cmv_epi(ly.gu, m.a, m.h, m.scr, m.st, TQ_EPI_SWIGLU, tq_matvec_uses_tmv()));
         TRY(tq_launch_matmul(ly.down, m.h, m.y, 1, m.scr, m.st));
-        if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
-        pending = m.y;
+        pending = true;
         TRY(cudaGetLastError());
     }
-    if (pending) TRY(step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, pending, m.ones, m.a, d, m.c.eps));
+    if (pending) TRY(add_norm());
     TRY(tq_launch_matmul(m.lm, m.a, m.logits, 1, m.scr, m.st));
     TRY(greedy_pick(m.logits, m.vcols, m.voff, m.part, m.cand, m.state, m.tokens, -1, 0, m.st));
+    if (m.ar_on)
+        return step_launch(ar_advance_kernel, dim3(1), dim3(32), 0, m.st, m.ar, m.cand, m.cands, m.state, m.tokens,
+                           m.prompt, n_prompt, m.scr.status);
     if (m.world > 1)
         TRY(nccl_err(g_nccl.allGather(m.cand, m.cands, 2, ncclInt32, m.comm, m.st)));
     else
@@ -754,6 +1030,7 @@ int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sigma, int ra
         if (r != ncclSuccess) return tq_fail(TQ_ERR_CUDA, "tensai: ncclCommInitRank: %s", g_nccl.errorString(r));
     }
     if (e == cudaSuccess) e = build(*m, seed, sigma, &rc);
+    if (e == cudaSuccess && rc == TQ_OK && world > 1) e = ar_setup(*m);
     if (e != cudaSuccess || rc != TQ_OK) {
         destroy(*m);
         return rc != TQ_OK ? rc : tq_cuda_fail(e, "Qwen2 model build");
@@ -830,6 +1107,15 @@ int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen,
     unsigned status = 0;
     if ((e = tq_read_status(m->scr, m->st, &status)) != cudaSuccess) return tq_cuda_fail(e, "status read");
     if (status & TQ_STATUS_TIMEOUT) return tq_fail(TQ_ERR_TIMEOUT, "tensai: a kernel timed out during decode");
+    return TQ_OK;
+}
+
+int tq_qwen_exchange(uint64_t model, int *kind) {
+    if (!kind) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    int rc = TQ_OK;
+    auto m = find(model, &rc);
+    if (!m) return rc;
+    *kind = m->world == 1 ? TQ_EXCHANGE_NONE : m->ar_on ? TQ_EXCHANGE_PEER : TQ_EXCHANGE_NCCL;
     return TQ_OK;
 }
 

@@ -138,6 +138,14 @@ class Qwen:
         tensor-core matmul (tq_qwen_set_prefill)."""
         _lib.check(_lib.load().tq_qwen_set_prefill(self.handle, rows))
 
+    @property
+    def exchange(self) -> str:
+        """"none" (one GPU), "nccl" or "peer": how the decode step's partial
+        sums meet (tq_qwen_exchange)."""
+        k = ctypes.c_int()
+        _lib.check(_lib.load().tq_qwen_exchange(self.handle, ctypes.byref(k)))
+        return {_lib.TQ_EXCHANGE_NONE: "none", _lib.TQ_EXCHANGE_NCCL: "nccl", _lib.TQ_EXCHANGE_PEER: "peer"}[k.value]
+
     def free(self) -> None:
         if self.handle:
             _lib.load().tq_qwen_free(self.handle)

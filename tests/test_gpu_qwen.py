@@ -116,31 +116,45 @@ def test_qwen7b_shape_batched_prefill_agreement():
     assert got[0] == z["tokens"][0], _diverge(got, z["tokens"], z["margins"])
 
 
-def _tp_worker(rank, world, port, q, cfg, seed, prompt, n):
+def _tp_worker(rank, world, port, q, cfg, seed, prompt, n, env, idle_rank, done):
     import torch
     import torch.distributed as dist
 
     from tensai_b200.decode import broadcast_nccl_id
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), **env)
     torch.cuda.set_device(rank)
     _lib.check(_lib.load().tq_set_device(rank))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         nid = broadcast_nccl_id(dist)
         with Qwen(cfg, seed, 0.02, rank, world, nid) as m:
-            q.put((rank, m.generate(prompt, n).tolist()))
+            if rank == idle_rank:  # joins the model but never the generate call
+                q.put((rank, (m.exchange, "idle")))
+                done.wait(60)
+            else:
+                kind = m.exchange
+                try:
+                    ids = m.generate(prompt, n).tolist()
+                except Exception as e:
+                    ids = repr(e)
+                finally:
+                    done.set()
+                q.put((rank, (kind, ids)))
     except Exception as e:  # reported to the parent
-        q.put((rank, repr(e)))
+        q.put((rank, (None, repr(e))))
     finally:
         dist.destroy_process_group()
 
 
-def run_tp(cfg, seed, prompt, n, world):
+def run_tp(cfg, seed, prompt, n, world, env=None, idle_rank=-1):
+    """{rank: (exchange, ids or an error's repr)} of a world-GPU generate."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
+    done = ctx.Event()
     port = free_port()
-    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q, cfg, seed, prompt, n)) for r in range(world)]
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q, cfg, seed, prompt, n, env or {}, idle_rank,
+                                                  done)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=600) for _ in procs)
@@ -157,8 +171,38 @@ def test_tensor_parallel_tiny_qwen_matches_oracle(world):
     want, margins = O.qwen_generate(TINY_TP, 3, 0.02, prompt, 40)
     got = run_tp(TINY_TP, 3, prompt, 40, world)
     for r in range(world):
-        assert isinstance(got[r], list), got[r]
-        assert np.array_equal(got[r], want), (r, _diverge(got[r], want, margins))
+        kind, ids = got[r]
+        assert isinstance(ids, list), ids
+        assert kind == "peer"
+        assert np.array_equal(ids, want), (r, _diverge(ids, want, margins))
+
+
+def test_tensor_parallel_nccl_exchange_matches_oracle():
+    """TENSAI_QWEN_EXCHANGE=nccl keeps NCCL's all-reduce in the step: same ids."""
+    if _ndev() < 2:
+        pytest.skip("needs 2 GPUs")
+    prompt = synth_tokens(24, TINY_TP["vocab"], 3)
+    want, margins = O.qwen_generate(TINY_TP, 3, 0.02, prompt, 40)
+    got = run_tp(TINY_TP, 3, prompt, 40, 2, env={"TENSAI_QWEN_EXCHANGE": "nccl"})
+    for r in range(2):
+        kind, ids = got[r]
+        assert isinstance(ids, list), ids
+        assert kind == "nccl"
+        assert np.array_equal(ids, want), (r, _diverge(ids, want, margins))
+
+
+def test_tensor_parallel_peer_exchange_times_out():
+    """A rank that never joins generate: the other's exchange waits give up
+    after 2 s and generate fails with TQ_ERR_TIMEOUT (nothing hangs; the idle
+    rank keeps its memory mapped until the other has returned)."""
+    if _ndev() < 2:
+        pytest.skip("needs 2 GPUs")
+    prompt = synth_tokens(4, TINY_TP["vocab"], 3)
+    got = run_tp(TINY_TP, 3, prompt, 3, 2, env={"NCCL_NVLS_ENABLE": "0"}, idle_rank=1)
+    assert got[1] == ("peer", "idle")
+    kind, err = got[0]
+    assert kind == "peer"
+    assert isinstance(err, str) and "timed out" in err, err
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
@@ -174,5 +218,7 @@ def test_tensor_parallel_qwen7b_shape_matches_golden_tokens(world):
     assert np.array_equal(prompt, z["prompt"])
     got = run_tp(cfg, int(z["seed"]), prompt, n_gen, world)
     for r in range(world):
-        assert isinstance(got[r], list), got[r]
-        assert np.array_equal(got[r], z["tokens"]), (r, _diverge(got[r], z["tokens"], z["margins"]))
+        kind, ids = got[r]
+        assert isinstance(ids, list), ids
+        assert kind == "peer"
+        assert np.array_equal(ids, z["tokens"]), (r, _diverge(ids, z["tokens"], z["margins"]))
