@@ -191,24 +191,36 @@ inline size_t attention_smem(int ctx) { return (sizeof(double) + sizeof(float)) 
 
 // ---- split-K decode attention -------------------------------------------------------
 // The attention of the decode step's single query row, spread over chunks of
-// kAttChunk cached positions so that long contexts use every SM. Two passes:
-//   scores:   per (head, chunk), one thread per position: s_t = (q . k_t, the
+// cached positions so that long contexts use every SM. A block serves one KV
+// head and all `group` query heads that share it (grouped-query attention),
+// so each cached k and v row is read once per step, not once per query head.
+// Two passes:
+//   scores:   per KV head and chunk of kAttSChunk positions, one warp per
+//             query head and one lane per position: s_t = (q . k_t, the
 //             float64 products added in dimension order) * scale, then the
-//             chunk's max m_b and sum l_b = sum exp(s_t - m_b). With RoPE
-//             (Qwen2) the pass first rotates this step's q head (and, in the
-//             chunk holding the position, its k head) from the fused row with
-//             the step's cos/sin table, and the first head of each KV group
-//             stores the rotated k and the biased v in the caches;
-//   weights:  per (head, chunk): the softmax's global max M and sum L =
-//             sum_b l_b exp(m_b - M), p_t = float32(exp(s_t - M) / L) as the
-//             Go code forms it, and the chunk's float32 sums p_t * v_t over
-//             its positions in order (in sub-chunks added in order); the last
-//             chunk of a head to finish adds the chunk sums in chunk order.
-// Scratch (per engine): scores [heads][ctx] doubles, stats [heads][chunks][2]
-// doubles, partials [heads][chunks][hd] floats, arrival counters [heads].
-constexpr int kAttChunk = 128;
+//             head's chunk max m_b and sum l_b = sum exp(s_t - m_b). The
+//             chunk's k rows are staged in shared memory by coalesced 16-byte
+//             copies. A float32 x float32 product is exact in float64, so
+//             fma(q, k, acc) rounds once exactly as acc + q*k does. With RoPE
+//             (Qwen2) the pass first rotates the group's q heads (and, in the
+//             chunk holding the position, the KV head's k) from the fused row
+//             with the step's cos/sin table, and stores the rotated k and the
+//             biased v in the caches;
+//   weights:  per KV head and chunk of kAttChunk positions: each head's
+//             softmax max M and sum L = sum_b l_b exp(m_b - M) over the score
+//             chunks, p_t = float32(exp(s_t - M) / L) as the Go code forms
+//             it, and for every head the float32 sums p_t * v_t over the
+//             chunk's positions in order (in sub-chunks added in order), each
+//             v row read once for all heads; the last chunk of a KV head to
+//             finish adds the chunk sums in chunk order.
+// Scratch (per engine): scores [heads][ctx] doubles, stats [heads][score
+// chunks][2] doubles, partials [heads][chunks][hd] floats, arrival counters
+// [heads].
+constexpr int kAttChunk = 128;    // positions per value-pass block
+constexpr int kAttSChunk = 32;    // positions per scores block (a lane each)
 constexpr int kAttMaxHd = 256;
-constexpr int kAttWThreads = 512;
+constexpr int kAttMaxGroup = 16;  // query heads per KV head (a warp each in the scores pass)
+constexpr int kAttWThreads = 512; // value pass
 
 // RoPE of the scores pass (Qwen2, model.go:219-229: half-split pairs (i, i +
 // hd/2)); cs == nullptr for none (GPT-2, whose q, k and v are stored already).
@@ -238,68 +250,102 @@ __device__ __forceinline__ void rope_pair(const double *cs, int i, float a, floa
     r1 = (float)__dadd_rn(__dmul_rn(bd, c), __dmul_rn(ad, s));
 }
 
-__global__ void __launch_bounds__(kAttChunk) att_scores_kernel(const float *q, const float *kc, int kvstride,
-                                                               const int *state, int hd, int group, double scale,
-                                                               double *scores, double *stats, int ctx, int nchunks,
-                                                               AttRope rope) {
+// Shared memory of the scores pass: the chunk's k rows (stride hd + 4 floats:
+// 16-byte rows whose float4 reads by 8 lanes fall in distinct banks) and the
+// group's q heads.
+inline size_t att_scores_smem(int hd, int group) {
+    return sizeof(float) * ((size_t)kAttSChunk * (hd + 4) + (size_t)group * hd);
+}
+// Shared memory of the value pass: p [group][chunk] and the sub-chunk sums
+// [sub-chunks][group][hd].
+inline size_t att_weighted_smem(int hd, int group) {
+    return sizeof(float) * ((size_t)group * kAttChunk + (size_t)(kAttWThreads / hd) * group * hd);
+}
+
+__device__ __forceinline__ void att_cp16(float *dst, const float *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+
+// Block (KV head, score chunk) of 32 x group threads.
+__global__ void __launch_bounds__(32 * kAttMaxGroup) att_scores_kernel(const float *q, const float *kc, int kvstride,
+                                                                       const int *state, int hd, int group,
+                                                                       double scale, double *scores, double *stats,
+                                                                       int ctx, int nschunks, AttRope rope) {
     step_entry_wait();
-    __shared__ __align__(16) float qs[kAttMaxHd];
+    extern __shared__ __align__(16) float att_sm[];
     __shared__ __align__(16) float kp[kAttMaxHd];
-    __shared__ double sh[32];
-    const int h = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttChunk;
-    const int kvh = h / group, half = hd / 2;
+    const int kvh = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttSChunk;
     if (t0 > pos) return;
-    const bool here = pos < t0 + kAttChunk; // this chunk holds the step's own position
+    const int tid = threadIdx.x, bd = blockDim.x, ld = hd + 4, f4 = hd / 4, half = hd / 2;
+    float *ks = att_sm;                       // [kAttSChunk][ld]
+    float *qs = ks + (size_t)kAttSChunk * ld; // [group][hd]
+    const int nrows = min(kAttSChunk, pos + 1 - t0);
+    const bool own = rope.cs && pos < t0 + kAttSChunk; // this chunk holds the step's own (new) k row
+    {   // the chunk's cached k rows, in flight while q is prepared (the new
+        // row comes from kp instead)
+        const float *src = kc + (size_t)kvh * hd;
+        for (int f = tid; f < nrows * f4; f += bd) {
+            const int r = f / f4, c4 = f - r * f4;
+            if (!(own && t0 + r == pos))
+                att_cp16(ks + (size_t)r * ld + 4 * c4, src + (size_t)(t0 + r) * kvstride + 4 * c4);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     if (rope.cs) {
-        for (int i = threadIdx.x; i < half; i += blockDim.x) {
-            const int j = h * hd + i;
-            rope_pair(rope.cs, i, __fadd_rn(q[j], rope.qbias[j]), __fadd_rn(q[j + half], rope.qbias[j + half]), qs[i],
-                      qs[i + half]);
-            if (here) {
+        for (int e = tid; e < group * half; e += bd) {
+            const int j = e / half, i = e - j * half, hq = (kvh * group + j) * hd;
+            rope_pair(rope.cs, i, __fadd_rn(q[hq + i], rope.qbias[hq + i]),
+                      __fadd_rn(q[hq + i + half], rope.qbias[hq + i + half]), qs[j * hd + i], qs[j * hd + i + half]);
+        }
+        if (own) { // this position's k and v: into the caches and the staged rows (this block alone reads them)
+            for (int i = tid; i < half; i += bd) {
                 const int kj = kvh * hd + i;
                 rope_pair(rope.cs, i, __fadd_rn(rope.k[kj], rope.kbias[kj]),
                           __fadd_rn(rope.k[kj + half], rope.kbias[kj + half]), kp[i], kp[i + half]);
             }
-        }
-        if (here && h % group == 0) { // the KV group's first head stores this position's k and v
             __syncthreads();
             float *kd = rope.kc + (size_t)pos * kvstride + kvh * hd;
             float *vd = rope.vc + (size_t)pos * kvstride + kvh * hd;
-            for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+            float *kr = ks + (size_t)(pos - t0) * ld;
+            for (int i = tid; i < hd; i += bd) {
                 kd[i] = kp[i];
+                kr[i] = kp[i];
                 vd[i] = __fadd_rn(rope.v[kvh * hd + i], rope.vbias[kvh * hd + i]);
             }
         }
     } else {
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) qs[i] = q[h * hd + i];
+        for (int e = tid; e < group * hd; e += bd) qs[e] = q[(size_t)kvh * group * hd + e];
     }
-    __syncthreads();
-    const int t = t0 + threadIdx.x;
-    double s = -INFINITY;
-    if (t <= pos) {
-        const float *kt = (rope.cs && t == pos) ? kp : kc + (size_t)t * kvstride + kvh * hd;
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads(); // q and the k rows
+    const int j = tid >> 5, r = tid & 31, h = kvh * group + j;
+    double sv = -INFINITY;
+    if (r < nrows) {
+        const float *kt = ks + (size_t)r * ld, *qr = qs + (size_t)j * hd;
         double acc = 0;
-        for (int i0 = 0; i0 < hd; i0 += 32) { // 8 loads in flight, then the products in order
+        for (int i0 = 0; i0 < hd; i0 += 32) { // products added in dimension order
             float4 kv[8];
 #pragma unroll
             for (int u = 0; u < 8; u++) kv[u] = *reinterpret_cast<const float4 *>(kt + i0 + 4 * u);
 #pragma unroll
             for (int u = 0; u < 8; u++) {
-                const float4 qv = *reinterpret_cast<const float4 *>(qs + i0 + 4 * u);
-                acc = __dadd_rn(acc, __dmul_rn((double)qv.x, (double)kv[u].x));
-                acc = __dadd_rn(acc, __dmul_rn((double)qv.y, (double)kv[u].y));
-                acc = __dadd_rn(acc, __dmul_rn((double)qv.z, (double)kv[u].z));
-                acc = __dadd_rn(acc, __dmul_rn((double)qv.w, (double)kv[u].w));
+                const float4 qv = *reinterpret_cast<const float4 *>(qr + i0 + 4 * u);
+                acc = __fma_rn((double)qv.x, (double)kv[u].x, acc);
+                acc = __fma_rn((double)qv.y, (double)kv[u].y, acc);
+                acc = __fma_rn((double)qv.z, (double)kv[u].z, acc);
+                acc = __fma_rn((double)qv.w, (double)kv[u].w, acc);
             }
         }
-        s = __dmul_rn(acc, scale);
-        scores[(size_t)h * ctx + t] = s;
+        sv = __dmul_rn(acc, scale);
+        scores[(size_t)h * ctx + t0 + r] = sv;
     }
-    const double mx = block_reduce_d(s, sh, 1);
-    const double l = block_reduce_d(t <= pos ? exp(__dsub_rn(s, mx)) : 0.0, sh, 0);
-    if (threadIdx.x == 0) {
-        stats[((size_t)h * nchunks + b) * 2] = mx;
-        stats[((size_t)h * nchunks + b) * 2 + 1] = l;
+    const double mx = warp_max_d(sv);
+    const double l = warp_sum_d(r < nrows ? exp(__dsub_rn(sv, mx)) : 0.0);
+    if (r == 0) {
+        const size_t o = ((size_t)h * nschunks + b) * 2;
+        stats[o] = mx;
+        stats[o + 1] = l;
     }
 }
 
@@ -317,59 +363,94 @@ __global__ void __launch_bounds__(kAttWThreads) att_weighted_kernel(const float 
                                                                     int hd, int group, const double *scores,
                                                                     const double *stats, float *partial,
                                                                     unsigned *count, float *out, int ctx,
-                                                                    int nchunks) {
+                                                                    int nchunks, int nschunks) {
     step_entry_wait();
-    __shared__ float ps[kAttChunk];
-    __shared__ float sub[kAttWThreads];
-    __shared__ double ml[2];
+    extern __shared__ __align__(16) float att_sm[];
+    __shared__ double ml[kAttMaxGroup][2];
     __shared__ int last;
-    const int h = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttChunk, kvh = h / group;
+    const int kvh = blockIdx.x, b = blockIdx.y, pos = state[1], t0 = b * kAttChunk;
     if (t0 > pos) return;
-    const int t1 = min(t0 + kAttChunk, pos + 1), nb = pos / kAttChunk + 1;
-    if (threadIdx.x < 32) { // the softmax's max and sum over the chunks' stats
-        const int lane = threadIdx.x;
-        const double *st = stats + (size_t)h * nchunks * 2;
-        double M = -INFINITY;
-        for (int c = lane; c < nb; c += 32) M = fmax(M, st[2 * c]);
-        M = warp_max_d(M);
-        double L = 0;
-        for (int c = lane; c < nb; c += 32) L = __dadd_rn(L, __dmul_rn(st[2 * c + 1], exp(__dsub_rn(st[2 * c], M))));
-        L = warp_sum_d(L);
-        if (lane == 0) ml[0] = M, ml[1] = L;
-    }
-    __syncthreads();
-    for (int t = t0 + threadIdx.x; t < t1; t += blockDim.x)
-        ps[t - t0] = (float)__ddiv_rn(exp(__dsub_rn(scores[(size_t)h * ctx + t], ml[0])), ml[1]);
-    __syncthreads();
-    // nsub sub-chunks of sz positions, each summed in order by hd threads
-    const int nsub = blockDim.x / hd, sz = kAttChunk / nsub;
-    const int sc = threadIdx.x / hd, i = threadIdx.x % hd;
-    const int ta = t0 + sc * sz, tb = min(ta + sz, t1);
-    float acc = 0.f;
-    const float *v = vc + kvh * hd + i;
-    for (int tt = ta; tt < tb; tt += 32) {
-        float vv[32];
+    const int tid = threadIdx.x, bd = blockDim.x;
+    const int t1 = min(t0 + kAttChunk, pos + 1), nb = pos / kAttChunk + 1, nbs = pos / kAttSChunk + 1;
+    float *ps = att_sm;                              // [group][kAttChunk]
+    float *sub = att_sm + (size_t)group * kAttChunk; // [nsub][group][hd]
+    // sub-chunk sq of sz positions, dimension i: the first 32 values and the
+    // thread's scores are loaded before the softmax statistics
+    const int nsub = bd / hd, sz = kAttChunk / nsub, sq = tid / hd, i = tid - sq * hd;
+    const int ta = t0 + sq * sz, tb = min(ta + sz, t1);
+    const float *v = vc + (size_t)kvh * hd + i;
+    float vv[32];
+    auto load_v = [&](int tt) {
 #pragma unroll
         for (int u = 0; u < 32; u++) vv[u] = tt + u < tb ? v[(size_t)(tt + u) * kvstride] : 0.f;
+    };
+    load_v(ta);
+    constexpr int kPs = kAttMaxGroup * kAttChunk / kAttWThreads; // p entries per thread
+    const int nit = group * kAttChunk;
+    double my_s[kPs];
 #pragma unroll
-        for (int u = 0; u < 32; u++)
-            if (tt + u < tb) acc = __fadd_rn(acc, __fmul_rn(ps[tt + u - t0], vv[u]));
+    for (int k = 0; k < kPs; k++) {
+        const int it = tid + k * bd, j = it / kAttChunk, r = it - j * kAttChunk;
+        my_s[k] = it < nit && t0 + r < t1 ? scores[(size_t)(kvh * group + j) * ctx + t0 + r] : 0.0;
     }
-    sub[threadIdx.x] = acc;
+    const int warp = tid >> 5, lane = tid & 31;
+    if (warp < group) { // head `warp`: the softmax's max and sum over the score chunks' stats
+        const double *st = stats + (size_t)(kvh * group + warp) * nschunks * 2;
+        double M = -INFINITY;
+        for (int c = lane; c < nbs; c += 32) M = fmax(M, st[2 * c]);
+        M = warp_max_d(M);
+        double L = 0;
+        for (int c = lane; c < nbs; c += 32) L = __dadd_rn(L, __dmul_rn(st[2 * c + 1], exp(__dsub_rn(st[2 * c], M))));
+        L = warp_sum_d(L);
+        if (lane == 0) ml[warp][0] = M, ml[warp][1] = L;
+    }
     __syncthreads();
-    if (threadIdx.x < hd) {
+#pragma unroll
+    for (int k = 0; k < kPs; k++) {
+        const int it = tid + k * bd, j = it / kAttChunk, r = it - j * kAttChunk;
+        if (it < nit && t0 + r < t1) ps[it] = (float)__ddiv_rn(exp(__dsub_rn(my_s[k], ml[j][0])), ml[j][1]);
+    }
+    __syncthreads();
+    // per head, the sub-chunk's positions in order; the running sums live in sub
+    for (int tt = ta; tt < tb; tt += 32) {
+        if (tt != ta) load_v(tt);
+        for (int j = 0; j < group; j++) {
+            float *sj = sub + ((size_t)sq * group + j) * hd + i;
+            float a = tt == ta ? 0.f : *sj;
+            const float *pj = ps + (size_t)j * kAttChunk + (tt - t0);
+#pragma unroll
+            for (int u = 0; u < 32; u++)
+                if (tt + u < tb) a = __fadd_rn(a, __fmul_rn(pj[u], vv[u]));
+            *sj = a;
+        }
+    }
+    if (ta >= tb) // an empty sub-chunk adds zeros
+        for (int j = 0; j < group; j++) sub[((size_t)sq * group + j) * hd + i] = 0.f;
+    __syncthreads();
+    const int ne = group * hd;
+    for (int e = tid; e < ne; e += bd) { // the chunk's sums: sub-chunks in order
+        const int j = e / hd, ii = e - j * hd;
         float a = 0.f;
-        for (int c = 0; c < nsub; c++) a = __fadd_rn(a, sub[c * hd + threadIdx.x]);
-        partial[((size_t)h * nchunks + b) * hd + threadIdx.x] = a;
+        for (int c = 0; c < nsub; c++) a = __fadd_rn(a, sub[((size_t)c * group + j) * hd + ii]);
+        partial[((size_t)(kvh * group + j) * nchunks + b) * hd + ii] = a;
     }
     __syncthreads(); // every thread's partial store before the arrival
-    if (threadIdx.x == 0) last = att_arrive_last(count + h, (unsigned)nb) ? 1 : 0;
+    if (tid == 0) last = att_arrive_last(count + kvh, (unsigned)nb) ? 1 : 0;
     __syncthreads();
     if (!last) return;
-    for (int j = threadIdx.x; j < hd; j += blockDim.x) {
+    for (int e = tid; e < ne; e += bd) { // chunk sums in chunk order, 16 loads in flight
+        const int j = e / hd, ii = e - j * hd;
+        const float *pp = partial + (size_t)(kvh * group + j) * nchunks * hd + ii;
         float a = 0.f;
-        for (int c = 0; c < nb; c++) a = __fadd_rn(a, __ldcg(partial + ((size_t)h * nchunks + c) * hd + j));
-        out[h * hd + j] = a;
+        for (int c0 = 0; c0 < nb; c0 += 16) {
+            float pv[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) pv[u] = c0 + u < nb ? __ldcg(pp + (size_t)(c0 + u) * hd) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                if (c0 + u < nb) a = __fadd_rn(a, pv[u]);
+        }
+        out[(size_t)(kvh * group + j) * hd + ii] = a;
     }
 }
 
@@ -377,12 +458,12 @@ struct AttScratch {
     double *scores = nullptr, *stats = nullptr;
     float *partial = nullptr;
     unsigned *count = nullptr;
-    int ctx = 0, nchunks = 0;
+    int ctx = 0, nchunks = 0, nschunks = 0;
 };
 
 inline size_t att_scratch_bytes(int heads, int ctx, int hd) {
-    const int nc = (ctx + kAttChunk - 1) / kAttChunk;
-    return sizeof(double) * (size_t)heads * ctx + sizeof(double) * 2 * (size_t)heads * nc +
+    const int nc = (ctx + kAttChunk - 1) / kAttChunk, ns = (ctx + kAttSChunk - 1) / kAttSChunk;
+    return sizeof(double) * (size_t)heads * ctx + sizeof(double) * 2 * (size_t)heads * ns +
            sizeof(float) * (size_t)heads * nc * hd + sizeof(unsigned) * (size_t)heads;
 }
 
@@ -391,23 +472,40 @@ inline size_t att_scratch_bytes(int heads, int ctx, int hd) {
 inline cudaError_t att_scratch(void *buf, int heads, int ctx, int hd, cudaStream_t st, AttScratch *a) {
     a->ctx = ctx;
     a->nchunks = (ctx + kAttChunk - 1) / kAttChunk;
+    a->nschunks = (ctx + kAttSChunk - 1) / kAttSChunk;
     a->scores = static_cast<double *>(buf);
     a->stats = a->scores + (size_t)heads * ctx;
-    a->partial = reinterpret_cast<float *>(a->stats + 2 * (size_t)heads * a->nchunks);
+    a->partial = reinterpret_cast<float *>(a->stats + 2 * (size_t)heads * a->nschunks);
     a->count = reinterpret_cast<unsigned *>(a->partial + (size_t)heads * a->nchunks * hd);
     return cudaMemsetAsync(a->count, 0, sizeof(unsigned) * heads, st);
+}
+
+// Lets both passes take their shared memory on the current device (once per
+// engine build); fails for shapes the kernels do not take.
+inline cudaError_t att_setup(int hd, int group) {
+    if (hd % 32 || hd > kAttMaxHd || kAttWThreads % hd || group < 1 || group > kAttMaxGroup)
+        return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(att_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)att_scores_smem(hd, group));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(att_weighted_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)att_weighted_smem(hd, group));
+    return e;
 }
 
 // The decode-step attention of q (heads x hd) over cached positions 0..state[1].
 inline cudaError_t decode_attention(const float *q, const float *kc, const float *vc, int kvstride, float *out,
                                     const int *state, int heads, int hd, int group, double scale, const AttScratch &a,
                                     cudaStream_t st, const AttRope &rope = AttRope()) {
-    if (hd % 32 || hd > kAttMaxHd || kAttWThreads % hd) return cudaErrorInvalidValue;
-    cudaError_t e = step_launch(att_scores_kernel, dim3(heads, a.nchunks), dim3(kAttChunk), 0, st, q, kc, kvstride,
-                                state, hd, group, scale, a.scores, a.stats, a.ctx, a.nchunks, rope);
+    if (hd % 32 || hd > kAttMaxHd || kAttWThreads % hd || group < 1 || group > kAttMaxGroup || heads % group)
+        return cudaErrorInvalidValue;
+    cudaError_t e = step_launch(att_scores_kernel, dim3(heads / group, a.nschunks), dim3(32 * group),
+                                att_scores_smem(hd, group), st, q, kc, kvstride, state, hd, group, scale, a.scores,
+                                a.stats, a.ctx, a.nschunks, rope);
     if (e == cudaSuccess)
-        e = step_launch(att_weighted_kernel, dim3(heads, a.nchunks), dim3(kAttWThreads), 0, st, vc, kvstride, state, hd,
-                        group, a.scores, a.stats, a.partial, a.count, out, a.ctx, a.nchunks);
+        e = step_launch(att_weighted_kernel, dim3(heads / group, a.nchunks), dim3(kAttWThreads),
+                        att_weighted_smem(hd, group), st, vc, kvstride, state, hd, group, a.scores, a.stats,
+                        a.partial, a.count, out, a.ctx, a.nchunks, a.nschunks);
     return e;
 }
 

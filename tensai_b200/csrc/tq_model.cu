@@ -308,6 +308,7 @@ cudaError_t build(Gpt2 &m, uint64_t seed, float sigma, int *rc) {
     void *ab = nullptr;
     TRY(dalloc(m, &ab, att_scratch_bytes(c.n_head, c.ctx, d / c.n_head)));
     TRY(att_scratch(ab, c.n_head, c.ctx, d / c.n_head, m.st, &m.att_scr));
+    TRY(att_setup(d / c.n_head, 1));
     TRY(dalloc(m, (void **)&m.tokens, sizeof(int) * (size_t)(c.ctx + 1)));
     if ((*rc = tq_scratch_for(m.device, m.st, &m.scr, 1)) != TQ_OK) return cudaErrorMemoryAllocation;
     const size_t smem = attn_smem(m);

@@ -144,6 +144,33 @@ __global__ void rmsnorm_kernel(float *x, const float *y, const float *w, float *
     constexpr int B = kNormBatch;
     const int bd = blockDim.x;
     double ss = 0;
+    if (n <= B * bd) { // one batch per thread: the new x stays in registers, w comes with the first loads
+        float a[B], b[B], c[B];
+#pragma unroll
+        for (int u = 0; u < B; u++) {
+            const int i = threadIdx.x + u * bd;
+            a[u] = i < n ? x[i] : 0.f;
+            b[u] = i < n && y ? y[i] : 0.f;
+            c[u] = i < n ? w[i] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < B; u++) {
+            const int i = threadIdx.x + u * bd;
+            if (i < n) {
+                if (y) a[u] = __fadd_rn(a[u], b[u]);
+                if (y) x[i] = a[u];
+                ss = __dadd_rn(ss, __dmul_rn((double)a[u], (double)a[u]));
+            }
+        }
+        ss = block_reduce_d(ss, sh, 0);
+        const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)n), eps)));
+#pragma unroll
+        for (int u = 0; u < B; u++) {
+            const int i = threadIdx.x + u * bd;
+            if (i < n) out[i] = __fmul_rn((float)__dmul_rn((double)a[u], inv), c[u]);
+        }
+        return;
+    }
     for (int i0 = threadIdx.x; i0 < n; i0 += B * bd) {
         float a[B], b[B];
 #pragma unroll
@@ -466,6 +493,18 @@ __global__ void __launch_bounds__(1024) ar_rmsnorm_kernel(ArLink L, float *x, co
     const unsigned e = s_e;
     const int bd = blockDim.x, np = L.world - 1;
     const size_t par = (size_t)(e & 1) * L.world * L.cap;
+    // n <= kArKeep * blockDim.x: x and w are loaded before the wait and the new x kept in registers
+    constexpr int kArKeep = 4;
+    const bool keep = n <= kArKeep * bd;
+    float xs[kArKeep], ws[kArKeep];
+    if (keep) {
+#pragma unroll
+        for (int u = 0; u < kArKeep; u++) {
+            const int i = threadIdx.x + u * bd;
+            xs[u] = i < n ? x[i] : 0.f;
+            ws[u] = i < n ? w[i] : 0.f;
+        }
+    }
     for (int i = threadIdx.x; i < n; i += bd) {
         const unsigned long long wd = ((unsigned long long)e << 32) | __float_as_uint(y[i]);
         for (int k = 1; k <= np; k++) {
@@ -498,21 +537,45 @@ __global__ void __launch_bounds__(1024) ar_rmsnorm_kernel(ArLink L, float *x, co
         }
     }
     __syncthreads();
-    double ss = 0;
-    for (int i = threadIdx.x; i < n; i += bd) {
+    // the rank-order sum of element i, own partial y[i] included
+    auto total_at = [&](int i) {
         float s = 0.f;
         for (int r = 0; r < L.world; r++) {
             const int k = r > L.rank ? r - L.rank - 1 : r + L.world - L.rank - 1;
             const float t = r == L.rank ? y[i] : recv[(size_t)k * n + i];
             s = r == 0 ? t : __fadd_rn(s, t);
         }
-        const float xv = __fadd_rn(x[i], s);
-        x[i] = xv;
-        ss = __dadd_rn(ss, __dmul_rn((double)xv, (double)xv));
+        return s;
+    };
+    double ss = 0;
+    if (keep) {
+#pragma unroll
+        for (int u = 0; u < kArKeep; u++) {
+            const int i = threadIdx.x + u * bd;
+            if (i < n) {
+                xs[u] = __fadd_rn(xs[u], total_at(i));
+                x[i] = xs[u];
+                ss = __dadd_rn(ss, __dmul_rn((double)xs[u], (double)xs[u]));
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += bd) {
+            const float xv = __fadd_rn(x[i], total_at(i));
+            x[i] = xv;
+            ss = __dadd_rn(ss, __dmul_rn((double)xv, (double)xv));
+        }
     }
     ss = block_reduce_d(ss, sh, 0);
     const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)n), eps)));
-    for (int i = threadIdx.x; i < n; i += bd) out[i] = __fmul_rn((float)__dmul_rn((double)x[i], inv), w[i]);
+    if (keep) {
+#pragma unroll
+        for (int u = 0; u < kArKeep; u++) {
+            const int i = threadIdx.x + u * bd;
+            if (i < n) out[i] = __fmul_rn((float)__dmul_rn((double)xs[u], inv), ws[u]);
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += bd) out[i] = __fmul_rn((float)__dmul_rn((double)x[i], inv), w[i]);
+    }
     if (threadIdx.x == 0) L.ctl[0] = e; // every thread read s_e before block_reduce_d's barriers
 }
 
@@ -740,6 +803,7 @@ cudaError_t build(Qwen &m, uint64_t seed, float sigma, int *rc) {
     void *ab = nullptr;
     TRY(dalloc(m, &ab, att_scratch_bytes(m.nq, c.ctx, m.hd)));
     TRY(att_scratch(ab, m.nq, c.ctx, m.hd, m.st, &m.att_scr));
+    TRY(att_setup(m.hd, m.group));
     TRY(dalloc(m, (void **)&m.rope, sizeof(double) * m.hd));
     if ((*rc = tq_scratch_for(m.device, m.st, &m.scr, 1)) != TQ_OK) return cudaErrorMemoryAllocation;
     return cudaSuccess;
