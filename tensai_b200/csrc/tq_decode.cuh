@@ -418,9 +418,20 @@ __global__ void __launch_bounds__(kAttWThreads) att_weighted_kernel(const float 
             float *sj = sub + ((size_t)sq * group + j) * hd + i;
             float a = tt == ta ? 0.f : *sj;
             const float *pj = ps + (size_t)j * kAttChunk + (tt - t0);
+            if (tb - tt >= 32) { // a whole batch: p by float4 (16-byte aligned: tt - t0 is a multiple of 32)
 #pragma unroll
-            for (int u = 0; u < 32; u++)
-                if (tt + u < tb) a = __fadd_rn(a, __fmul_rn(pj[u], vv[u]));
+                for (int u0 = 0; u0 < 32; u0 += 4) {
+                    const float4 p4 = *reinterpret_cast<const float4 *>(pj + u0);
+                    a = __fadd_rn(a, __fmul_rn(p4.x, vv[u0]));
+                    a = __fadd_rn(a, __fmul_rn(p4.y, vv[u0 + 1]));
+                    a = __fadd_rn(a, __fmul_rn(p4.z, vv[u0 + 2]));
+                    a = __fadd_rn(a, __fmul_rn(p4.w, vv[u0 + 3]));
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < 32; u++)
+                    if (tt + u < tb) a = __fadd_rn(a, __fmul_rn(pj[u], vv[u]));
+            }
             *sj = a;
         }
     }
