@@ -624,7 +624,10 @@ def run_gpu(args, rank: int, world: int):
         side["F2 Qwen2.5-7B int4 quantize-on-load from BF16"] = measure_quant_load(world == 1 and not args.no_cpu_baseline)
     qwen = None
     if not args.no_side_configs and not args.side_config:
-        qwen = measure_qwen(rank, world, load_peak()[0], cpu=world == 1 and not args.no_cpu_baseline)  # collective
+        try:
+            qwen = measure_qwen(rank, world, load_peak()[0], cpu=world == 1 and not args.no_cpu_baseline)  # collective
+        except Exception as e:  # reported in the line; the headline stands on its own
+            qwen = {"tp": world, "error": str(e)[:300]}
         if side is not None:
             side[f"C5 Qwen2.5-7B int4 greedy decode TP={world}"] = qwen
     if rank == 0:
