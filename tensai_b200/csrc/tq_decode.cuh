@@ -45,6 +45,12 @@ __device__ __forceinline__ void step_entry_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #endif
 }
+// Lets the next kernel on the stream be scheduled now when it is launched
+// with programmatic stream serialization (the matvecs are): its CTAs stream
+// their weights while this kernel runs and wait on griddepcontrol.wait before
+// reading anything this kernel writes. For the small kernels right before a
+// matvec (norms, the attention's value pass).
+__device__ __forceinline__ void step_release_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 template <typename... KArgs, typename... Args>
 inline cudaError_t step_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                                Args... args) {
@@ -365,6 +371,7 @@ __global__ void __launch_bounds__(kAttWThreads) att_weighted_kernel(const float 
                                                                     unsigned *count, float *out, int ctx,
                                                                     int nchunks, int nschunks) {
     step_entry_wait();
+    step_release_next(); // the o_proj matvec streams its weights meanwhile
     extern __shared__ __align__(16) float att_sm[];
     __shared__ double ml[kAttMaxGroup][2];
     __shared__ int last;

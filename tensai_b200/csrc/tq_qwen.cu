@@ -94,6 +94,7 @@ constexpr int kNormBatch = 8;
 __global__ void embed_norm_kernel(const float *embed, const int *state, float *x, const float *w, float *out, int d,
                                   double eps, double *cs, int hd, double theta) {
     step_entry();
+    step_release_next();
     __shared__ double sh[32];
     rope_table(cs, state[1], hd, theta);
     const float *row = embed + (size_t)state[0] * d;
@@ -137,6 +138,7 @@ __global__ void embed_norm_kernel(const float *embed, const int *state, float *x
 // of [gridDim.x][n] x, y and out (one row in the decode step).
 __global__ void rmsnorm_kernel(float *x, const float *y, const float *w, float *out, int n, double eps) {
     step_entry();
+    step_release_next();
     __shared__ double sh[32];
     x += (size_t)blockIdx.x * n;
     out += (size_t)blockIdx.x * n;
@@ -476,6 +478,7 @@ __device__ __noinline__ unsigned long long ar_wait(const unsigned long long *p, 
 __global__ void __launch_bounds__(1024) ar_rmsnorm_kernel(ArLink L, float *x, const float *y, const float *w,
                                                           float *out, int n, double eps, unsigned *status) {
     step_entry();
+    step_release_next();
     extern __shared__ float recv[]; // [world-1][n], peers in the order rank+1, rank+2, …
     __shared__ double sh[32];
     __shared__ unsigned long long *slot[kArMaxWorld];
