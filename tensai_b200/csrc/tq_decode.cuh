@@ -51,6 +51,28 @@ __device__ __forceinline__ void step_entry_wait() {
 // reading anything this kernel writes. For the small kernels right before a
 // matvec (norms, the attention's value pass).
 __device__ __forceinline__ void step_release_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Waits until the previous kernel on the stream has completed and its writes
+// are visible; returns at once for a kernel launched without programmatic
+// stream serialization.
+__device__ __forceinline__ void step_wait_prev() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// A launch with programmatic stream serialization whatever TQ_DECODE_PDL is:
+// for a small kernel that starts with step_wait_prev, so that it is resident
+// (and its launch latency spent) when its predecessor completes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t step_launch_early(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                     Args... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 template <typename... KArgs, typename... Args>
 inline cudaError_t step_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                                Args... args) {

@@ -138,6 +138,7 @@ __global__ void embed_norm_kernel(const float *embed, const int *state, float *x
 // of [gridDim.x][n] x, y and out (one row in the decode step).
 __global__ void rmsnorm_kernel(float *x, const float *y, const float *w, float *out, int n, double eps) {
     step_entry();
+    step_wait_prev(); // launched early in the decode step (step_launch_early)
     step_release_next();
     __shared__ double sh[32];
     x += (size_t)blockIdx.x * n;
@@ -910,8 +911,12 @@ cudaError_t step(Qwen &m, int n_prompt) {
         if (m.ar_on)
             return step_launch(ar_rmsnorm_kernel, dim3(1), dim3(1024), m.ar_smem, m.st, m.ar, m.x, m.y, m.ones, m.a,
                                d, m.c.eps, m.scr.status);
-        if (m.world > 1) TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
-        return step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, m.y, m.ones, m.a, d, m.c.eps);
+        if (m.world > 1) {
+            TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
+            return step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, m.y, m.ones, m.a, d, m.c.eps);
+        }
+        // 512 threads: small enough to be resident beside the matvec before it, ready when it completes
+        return step_launch_early(rmsnorm_kernel, dim3(1), dim3(512), 0, m.st, m.x, m.y, m.ones, m.a, d, m.c.eps);
     };
     bool pending = false; // the previous down_proj output is still to be added to x
     for (Layer &ly : m.L) {
