@@ -352,6 +352,19 @@ TQ_EXPORT int tq_qwen_free(uint64_t model);
  * over world GPUs. Needs no GPU. */
 TQ_EXPORT int tq_qwen_shard_plan(const tq_qwen_config *cfg, int world, int rank, int *plan);
 
+/* The examples' sample step (_example/gpt2/main.go:78-105, the same
+ * function as _example/qwen/main.go:115-150) on the current device, for the
+ * host logits[0..n): temp <= 0 gives the first index of the largest logit;
+ * otherwise p_i = exp(float64(logits_i - max) / temp), the candidates sorted
+ * by p descending, r = u * sum(p), and *token = the first candidate at which
+ * r -= p reaches <= 0 (else the first candidate). u is the caller's uniform
+ * draw, rng.Float64() in the Go code (used only when temp > 0; must lie in
+ * [0, 1]). Equal weights are taken in ascending id order (Go's unstable sort
+ * leaves them unspecified); the sum of p is added in a fixed tree order, not
+ * index order, so r can differ from the Go code's in the last bits.
+ * Synchronous. TQ_ERR_ARG for n < 1, a NaN temperature or u out of range. */
+TQ_EXPORT int tq_sample(const float *logits, int n, double temp, double u, int *token);
+
 /* Seeded uniform token ids in [0, vocab) on the host: id i =
  * mix64(key + (i+1)*0x9E3779B97F4A7C15) % vocab with the generator key of
  * (seed, stream 3). A stand-in for a tokenized prompt. */

@@ -11,6 +11,7 @@ The functions restate mattn/tensai's Go code (file:line in tq_oracle.c):
   q4_matmul   -> (*Q4Matrix).MatVec        quant4.go:93-119 (+ :126-154 / quant4_simd.go:17-57)
   gpt2_generate -> GPT-2 -q8 greedy loop   _example/gpt2/model.go:179-401, main.go:69-77,163-170
   qwen_generate -> Qwen2 -q4 greedy loop   _example/qwen/model.go:182-307, main.go:225-240
+  sample        -> sample (temperature)    _example/gpt2/main.go:78-105 (= _example/qwen/main.go:115-150)
 """
 from __future__ import annotations
 
@@ -64,6 +65,8 @@ def lib():
         L.tqo_qwen_time_steps.restype = I
         L.tqo_synth_tokens.argtypes = [P, I, I, U64]
         L.tqo_synth_tokens.restype = None
+        L.tqo_sample.argtypes = [P, I, ctypes.c_double, ctypes.c_double]
+        L.tqo_sample.restype = I
         _lib = L
     return _lib
 
@@ -167,6 +170,13 @@ class Gpt2Cfg(ctypes.Structure):
 
 
 GPT2_SMALL = dict(n_layer=12, n_head=12, d=768, ffn=3072, vocab=50257, ctx=1024)
+
+
+def sample(logits, temp: float, u: float) -> int:
+    """The examples' sample step (_example/gpt2/main.go:78-105) with the
+    caller's uniform draw u (rng.Float64()); ties in p go to the lower id."""
+    v = np.ascontiguousarray(logits, np.float32)
+    return int(lib().tqo_sample(_p(v), len(v), float(temp), float(u)))
 
 
 def synth_tokens(n: int, vocab: int, seed: int) -> np.ndarray:

@@ -258,6 +258,58 @@ static int argmax(const float *v, int n, float *margin) {
     return best;
 }
 
+/* The examples' sample step (_example/gpt2/main.go:78-105 and
+ * _example/qwen/main.go:115-150 are the same function): temp <= 0 is the
+ * greedy scan; otherwise p_i = exp(float64(v_i - maxl) / temp) (the
+ * difference in float32, as Go evaluates v-maxl), the sum in index order,
+ * the candidates sorted by p descending, r = u * sum and the first
+ * candidate at which r -= p reaches <= 0, else the first candidate. u is
+ * the caller's rng.Float64(). Go's sort.Slice is not stable: among equal p
+ * it leaves the order to its pattern-defeating quicksort, so here ties go to
+ * the lower id (a choice, not Go's). */
+typedef struct {
+    double p;
+    int id;
+} tqo_cand;
+static int cand_cmp(const void *a, const void *b) {
+    const tqo_cand *x = a, *y = b;
+    if (x->p > y->p) return -1;
+    if (x->p < y->p) return 1;
+    return (x->id > y->id) - (x->id < y->id);
+}
+TQO_EXPORT int tqo_sample(const float *logits, int n, double temp, double u) {
+    if (n <= 0) return -1;
+    if (temp <= 0) {
+        int best = 0;
+        for (int i = 0; i < n; i++)
+            if (logits[i] > logits[best]) best = i;
+        return best;
+    }
+    tqo_cand *c = malloc(sizeof(tqo_cand) * (size_t)n);
+    float maxl = logits[0];
+    for (int i = 0; i < n; i++)
+        if (logits[i] > maxl) maxl = logits[i];
+    double sum = 0;
+    for (int i = 0; i < n; i++) {
+        const float d = logits[i] - maxl;
+        c[i].p = exp((double)d / temp);
+        c[i].id = i;
+        sum += c[i].p;
+    }
+    qsort(c, (size_t)n, sizeof(tqo_cand), cand_cmp);
+    double r = u * sum;
+    int id = c[0].id;
+    for (int i = 0; i < n; i++) {
+        r -= c[i].p;
+        if (r <= 0) {
+            id = c[i].id;
+            break;
+        }
+    }
+    free(c);
+    return id;
+}
+
 static float *synth(size_t n, uint64_t seed, uint64_t stream, float sigma) {
     float *p = malloc(sizeof(float) * (n ? n : 1));
     tqo_synth_fill(p, n, seed, stream, sigma);

@@ -72,6 +72,17 @@ class Gpt2:
 QWEN_7B = dict(n_layer=28, n_head=28, n_kv=4, d=3584, ffn=18944, vocab=152064, ctx=2560, eps=1e-6, theta=1e6)
 
 
+def sample(logits, temp: float, u: float) -> int:
+    """The examples' sample (_example/gpt2/main.go:78-105) on the GPU
+    (tq_sample): greedy at temp <= 0, else a draw from the tempered
+    distribution with the caller's uniform u (rng.Float64() in the Go code)."""
+    v = np.ascontiguousarray(logits, np.float32)
+    tok = ctypes.c_int()
+    _lib.check(_lib.load().tq_sample(v.ctypes.data_as(ctypes.c_void_p), len(v), float(temp), float(u),
+                                     ctypes.byref(tok)))
+    return tok.value
+
+
 class QwenConfig(ctypes.Structure):
     _fields_ = [("n_layer", ctypes.c_int), ("n_head", ctypes.c_int), ("n_kv", ctypes.c_int), ("d", ctypes.c_int),
                 ("ffn", ctypes.c_int), ("vocab", ctypes.c_int), ("ctx", ctypes.c_int), ("eps", ctypes.c_double),
