@@ -270,6 +270,14 @@ TQ_EXPORT int tq_gpt2_create(const tq_gpt2_config *cfg, uint64_t seed, float sig
 TQ_EXPORT int tq_gpt2_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen, int *tokens,
                                float *times_ms);
 
+/* How tq_gpt2_generate picks each generated token: temp <= 0 (the default)
+ * greedy; temp > 0 the examples' sample step (main.go:78-105, tq_sample)
+ * with draws[k], the caller's rng.Float64() for generated token k, so
+ * tq_gpt2_generate then needs n_gen <= n_draws (the draws are copied; every
+ * generate call starts again from draws[0]). TQ_ERR_ARG for a NaN
+ * temperature or temp > 0 without draws in [0, 1]. */
+TQ_EXPORT int tq_gpt2_set_sampling(uint64_t model, double temp, const double *draws, int n_draws);
+
 /* Releases a model (a second call is a no-op). */
 TQ_EXPORT int tq_gpt2_free(uint64_t model);
 
@@ -323,6 +331,12 @@ TQ_EXPORT int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, 
  * than KV heads) or the context exceeds the batched attention's shared
  * memory. */
 TQ_EXPORT int tq_qwen_set_prefill(uint64_t model, int rows);
+
+/* tq_gpt2_set_sampling for a Qwen2 model (main.go:115-150); one GPU only
+ * (TQ_ERR_UNSUPPORTED when world > 1: the lm head is split by vocabulary).
+ * During a token-by-token prompt every step runs the sample step too (its
+ * result is discarded until the prompt's last position). */
+TQ_EXPORT int tq_qwen_set_sampling(uint64_t model, double temp, const double *draws, int n_draws);
 
 /* How the ranks of a tensor-parallel model exchange partial sums in the
  * decode step: *kind = TQ_EXCHANGE_NONE (world 1), TQ_EXCHANGE_NCCL (NCCL

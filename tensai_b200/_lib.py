@@ -64,6 +64,8 @@ SIGNATURES = {
     "tq_qwen_set_prefill": (I, [U64, I]),
     "tq_qwen_exchange": (I, [U64, ctypes.POINTER(ctypes.c_int)]),
     "tq_sample": (I, [P, I, ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_int)]),
+    "tq_gpt2_set_sampling": (I, [U64, ctypes.c_double, P, I]),
+    "tq_qwen_set_sampling": (I, [U64, ctypes.c_double, P, I]),
     "tq_qwen_free": (I, [U64]),
     "tq_qwen_shard_plan": (I, [P, I, I, P]),
     "tq_chain_create": (I, [P, I, PU64]),

@@ -38,5 +38,24 @@ int tq_alloc_matrix(int bits, int rows, int cols, TqMatrixDev *m, cudaStream_t s
 void tq_release_matrix(TqMatrixDev *m);
 // Reads and clears a scratch's status word, ORing it into *out (synchronous on st).
 cudaError_t tq_read_status(const TqScratch &scr, cudaStream_t st, unsigned *out);
+// Temperature sampling of device logits (tq_sample.cu): the examples' sample
+// step (tq_sample in the header). Buffers for up to cap logits.
+struct TqSampler {
+    int cap = 0;
+    double *kin = nullptr, *kout = nullptr, *partial = nullptr;
+    int *iin = nullptr, *iout = nullptr;
+    float *maxl = nullptr;
+    void *tmp = nullptr;
+    size_t tmp_bytes = 0;
+};
+cudaError_t tq_sampler_alloc(TqSampler *s, int n);
+void tq_sampler_free(TqSampler *s);
+// The token picked from logits[0..n) into *id_out (device), with the draw
+// draws[*at] (draws[0] when at is null) for temp > 0; asynchronous on st.
+cudaError_t tq_launch_sample(const TqSampler &s, const float *logits, int n, double temp, const double *draws,
+                             const int *at, int *id_out, cudaStream_t st);
+// Checks sampling settings: a NaN temperature, or temp > 0 without n_draws >= 1
+// draws in [0, 1], fail with TQ_ERR_ARG (message set).
+int tq_check_draws(double temp, const double *draws, int n_draws);
 // Seeded uniform token ids on the host (tq_quantize.cu).
 void tq_host_synth_tokens(int *out, int n, int vocab, uint64_t seed);

@@ -206,6 +206,11 @@ struct Gpt2 {
     AttScratch att_scr;
     cudaGraphExec_t graph = nullptr;
     std::vector<void *> allocs;
+    // tq_gpt2_set_sampling: temp > 0 draws generated token k with draws[k]
+    double temp = 0;
+    double *draws = nullptr;
+    int n_draws = 0;
+    TqSampler smp;
 };
 
 std::mutex g_models_mu;
@@ -237,6 +242,9 @@ void destroy(Gpt2 &m) {
     tq_release_matrix(&m.wteT.q);
     for (void *p : m.allocs) cudaFree(p);
     m.allocs.clear();
+    tq_sampler_free(&m.smp);
+    if (m.draws) cudaFree(m.draws);
+    m.draws = nullptr;
     if (m.st) tq_scratch_release(m.device, m.st);
     if (m.st) cudaStreamDestroy(m.st);
     m.st = nullptr;
@@ -362,7 +370,12 @@ cudaError_t prefill(Gpt2 &m, const int *prompt, int T) {
     }
     layernorm_kernel<<<1, kThreads, 0, m.st>>>(m.X + (size_t)(T - 1) * d, m.lnfw, m.lnfb, m.xn, d);
     TRY(sgemm(m.xn, m.wteT.w, m.logits, 1, m.c.vocab, d, m.st));
-    argmax_kernel<<<1, 1024, 0, m.st>>>(m.logits, m.c.vocab, 0, m.cand, m.state, m.tokens, T, 1);
+    if (m.temp > 0) { // main.go:78-105 with the caller's draw for generated token state[2]
+        TRY(tq_launch_sample(m.smp, m.logits, m.c.vocab, m.temp, m.draws, m.state + 2, m.cand + 1, m.st));
+        pick_kernel<<<1, 32, 0, m.st>>>(m.cand, 1, m.state, m.tokens, T);
+    } else {
+        argmax_kernel<<<1, 1024, 0, m.st>>>(m.logits, m.c.vocab, 0, m.cand, m.state, m.tokens, T, 1);
+    }
     return cudaGetLastError();
 }
 
@@ -388,6 +401,10 @@ cudaError_t decode_step(Gpt2 &m) {
     }
     TRY(step_launch(layernorm_kernel, dim3(1), dim3(kThreads), 0, m.st, m.x, m.lnfw, m.lnfb, m.xn, d, pend, pendb));
     TRY(tq_launch_matmul(m.wteT.q, m.xn, m.logits, 1, m.scr, m.st));
+    if (m.temp > 0) {
+        TRY(tq_launch_sample(m.smp, m.logits, m.c.vocab, m.temp, m.draws, m.state + 2, m.cand + 1, m.st));
+        return step_launch(pick_kernel, dim3(1), dim3(32), 0, m.st, (const int *)m.cand, 1, m.state, m.tokens, -1);
+    }
     return greedy_pick(m.logits, m.c.vocab, 0, m.part, m.cand, m.state, m.tokens, -1, 1, m.st);
 }
 
@@ -451,6 +468,8 @@ int tq_gpt2_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen,
     for (int i = 0; i < n_prompt; i++)
         if (prompt[i] < 0 || prompt[i] >= m->c.vocab)
             return tq_fail(TQ_ERR_ARG, "tensai: prompt token %d out of range [0, %d)", prompt[i], m->c.vocab);
+    if (m->temp > 0 && n_gen > m->n_draws)
+        return tq_fail(TQ_ERR_ARG, "tensai: %d tokens to sample but %d draws set", n_gen, m->n_draws);
     cudaError_t e = cudaSetDevice(m->device);
     cudaEvent_t ev[3] = {};
     for (int i = 0; i < 3 && e == cudaSuccess; i++) e = cudaEventCreate(&ev[i]);
@@ -475,6 +494,28 @@ int tq_gpt2_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen,
     if ((e = tq_read_status(m->scr, m->st, &status)) != cudaSuccess) return tq_cuda_fail(e, "status read");
     if (status & TQ_STATUS_TIMEOUT) return tq_fail(TQ_ERR_TIMEOUT, "tensai: a kernel timed out during decode");
     return TQ_OK;
+}
+
+int tq_gpt2_set_sampling(uint64_t model, double temp, const double *draws, int n_draws) {
+    int rc = TQ_OK;
+    auto m = find_model(model, &rc);
+    if (!m) return rc;
+    if ((rc = tq_check_draws(temp, draws, n_draws)) != TQ_OK) return rc;
+    cudaError_t e = cudaSetDevice(m->device);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
+    if (m->graph) cudaGraphExecDestroy(m->graph); // the graph holds the previous pick
+    m->graph = nullptr;
+    if (m->draws) cudaFree(m->draws);
+    m->draws = nullptr;
+    m->n_draws = 0;
+    m->temp = 0;
+    if (e == cudaSuccess && temp > 0) {
+        e = tq_dev_malloc((void **)&m->draws, sizeof(double) * n_draws);
+        if (e == cudaSuccess) e = cudaMemcpy(m->draws, draws, sizeof(double) * n_draws, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = tq_sampler_alloc(&m->smp, m->c.vocab);
+        if (e == cudaSuccess) m->temp = temp, m->n_draws = n_draws;
+    }
+    return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "sampling set-up");
 }
 
 int tq_gpt2_free(uint64_t model) {

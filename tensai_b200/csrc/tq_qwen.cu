@@ -670,6 +670,11 @@ struct Qwen {
     ArLink ar{};
     unsigned long long *ar_area = nullptr; // this rank's slot area (exported by IPC)
     size_t ar_smem = 0;                    // ar_rmsnorm_kernel's dynamic shared memory
+    // tq_qwen_set_sampling (one GPU): temp > 0 draws generated token k with draws[k]
+    double temp = 0;
+    double *draws = nullptr;
+    int n_draws = 0;
+    TqSampler smp;
 };
 
 std::mutex g_q_mu;
@@ -710,6 +715,9 @@ void destroy(Qwen &m) {
     tq_release_matrix(&m.lm);
     for (void *p : m.allocs) cudaFree(p);
     m.allocs.clear();
+    tq_sampler_free(&m.smp);
+    if (m.draws) cudaFree(m.draws);
+    m.draws = nullptr;
     if (m.st) tq_scratch_release(m.device, m.st);
     if (m.st) cudaStreamDestroy(m.st);
     m.st = nullptr;
@@ -814,6 +822,14 @@ cudaError_t build(Qwen &m, uint64_t seed, float sigma, int *rc) {
 }
 
 cudaError_t nccl_err(ncclResult_t r) { return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown; }
+
+// This rank's candidate (value, id) for the next token into cand: the greedy
+// pick of its logits, or (one GPU, tq_qwen_set_sampling) the sample step of
+// main.go:115-150 with the draw of generated token state[2] (the id only).
+cudaError_t pick_next(Qwen &m) {
+    if (m.temp > 0) return tq_launch_sample(m.smp, m.logits, m.vcols, m.temp, m.draws, m.state + 2, m.cand + 1, m.st);
+    return greedy_pick(m.logits, m.vcols, m.voff, m.part, m.cand, m.state, m.tokens, -1, 0, m.st);
+}
 
 // Each rank's value of v gathered over NCCL (host ints, a few bytes each).
 cudaError_t gather_host(Qwen &m, const void *v, size_t bytes, void *all) {
@@ -935,7 +951,7 @@ cudaError_t step(Qwen &m, int n_prompt) {
     }
     if (pending) TRY(add_norm());
     TRY(tq_launch_matmul(m.lm, m.a, m.logits, 1, m.scr, m.st));
-    TRY(greedy_pick(m.logits, m.vcols, m.voff, m.part, m.cand, m.state, m.tokens, -1, 0, m.st));
+    TRY(pick_next(m));
     if (m.ar_on)
         return step_launch(ar_advance_kernel, dim3(1), dim3(32), 0, m.st, m.ar, m.cand, m.cands, m.state, m.tokens,
                            m.prompt, n_prompt, m.scr.status);
@@ -995,7 +1011,7 @@ cudaError_t prefill(Qwen &m, int n_prompt) {
     rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.px + (size_t)last * d, m.py + (size_t)last * d, m.ones, m.a, d, m.c.eps);
     TRY(cudaGetLastError());
     TRY(tq_launch_matmul(m.lm, m.a, m.logits, 1, m.scr, m.st));
-    TRY(greedy_pick(m.logits, m.vcols, m.voff, m.part, m.cand, m.state, m.tokens, -1, 0, m.st));
+    TRY(pick_next(m));
     if (m.world > 1)
         TRY(nccl_err(g_nccl.allGather(m.cand, m.cands, 2, ncclInt32, m.comm, m.st)));
     else
@@ -1124,6 +1140,8 @@ int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen,
     for (int i = 0; i < n_prompt; i++)
         if (prompt[i] < 0 || prompt[i] >= m->c.vocab)
             return tq_fail(TQ_ERR_ARG, "tensai: prompt token %d out of range [0, %d)", prompt[i], m->c.vocab);
+    if (m->temp > 0 && n_gen > m->n_draws)
+        return tq_fail(TQ_ERR_ARG, "tensai: %d tokens to sample but %d draws set", n_gen, m->n_draws);
     cudaError_t e = cudaSetDevice(m->device);
     if (e == cudaSuccess && n_prompt > m->prompt_cap) {
         if (m->graph) cudaGraphExecDestroy(m->graph); // the graph holds the old prompt buffer
@@ -1180,6 +1198,31 @@ int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen,
     if ((e = tq_read_status(m->scr, m->st, &status)) != cudaSuccess) return tq_cuda_fail(e, "status read");
     if (status & TQ_STATUS_TIMEOUT) return tq_fail(TQ_ERR_TIMEOUT, "tensai: a kernel timed out during decode");
     return TQ_OK;
+}
+
+int tq_qwen_set_sampling(uint64_t model, double temp, const double *draws, int n_draws) {
+    int rc = TQ_OK;
+    auto m = find(model, &rc);
+    if (!m) return rc;
+    if ((rc = tq_check_draws(temp, draws, n_draws)) != TQ_OK) return rc;
+    if (temp > 0 && m->world > 1)
+        return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: sampling needs the whole vocabulary on one GPU (world %d)",
+                       m->world);
+    cudaError_t e = cudaSetDevice(m->device);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
+    if (m->graph) cudaGraphExecDestroy(m->graph); // the graph holds the previous pick
+    m->graph = nullptr;
+    if (m->draws) cudaFree(m->draws);
+    m->draws = nullptr;
+    m->n_draws = 0;
+    m->temp = 0;
+    if (e == cudaSuccess && temp > 0) {
+        e = tq_dev_malloc((void **)&m->draws, sizeof(double) * n_draws);
+        if (e == cudaSuccess) e = cudaMemcpy(m->draws, draws, sizeof(double) * n_draws, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = tq_sampler_alloc(&m->smp, m->vcols);
+        if (e == cudaSuccess) m->temp = temp, m->n_draws = n_draws;
+    }
+    return e == cudaSuccess ? TQ_OK : tq_cuda_fail(e, "sampling set-up");
 }
 
 int tq_qwen_exchange(uint64_t model, int *kind) {

@@ -87,12 +87,14 @@ __global__ void __launch_bounds__(kPThreads) sample_weights_kernel(const float *
     }
 }
 
-// One warp: the total of the block sums, r = u * total, then r -= p over the
-// sorted weights until r <= 0 (every lane holds the same r: the weights are
-// broadcast one at a time, the next 32 loaded while the current are walked).
+// One warp: the total of the block sums, r = u * total with u = draws[*at]
+// (draws[0] without at), then r -= p over the sorted weights until r <= 0
+// (every lane holds the same r: the weights are broadcast one at a time, the
+// next 32 loaded while the current are walked).
 __global__ void sample_pick_kernel(const double *keys, const int *ids, int n, const double *partial, int np,
-                                   double u, int *token) {
+                                   const double *draws, const int *at, int *token) {
     const int lane = threadIdx.x;
+    const double u = draws[at ? *at : 0];
     double s = 0;
     for (int b = lane; b < np; b += 32) s = __dadd_rn(s, partial[b]);
     for (int o = 16; o; o >>= 1) s = __dadd_rn(s, __shfl_down_sync(0xffffffffu, s, o));
@@ -115,56 +117,83 @@ __global__ void sample_pick_kernel(const double *keys, const int *ids, int n, co
     if (lane == 0) *token = ids[found >= 0 ? found : 0];
 }
 
-// Per-device buffers, grown to the largest n seen.
-struct SampleBuf {
-    int cap = 0;
-    float *v = nullptr, *maxl = nullptr;
-    double *kin = nullptr, *kout = nullptr, *partial = nullptr;
-    int *iin = nullptr, *iout = nullptr, *arg = nullptr, *tok = nullptr;
-    void *tmp = nullptr;
-    size_t tmp_bytes = 0;
-    cudaStream_t st = nullptr;
-};
-std::mutex g_sample_mu;
-std::unordered_map<int, SampleBuf> g_sample;
+} // namespace
 
-void release(SampleBuf &b) {
-    for (void *p : {(void *)b.v, (void *)b.maxl, (void *)b.kin, (void *)b.kout, (void *)b.partial, (void *)b.iin,
-                    (void *)b.iout, (void *)b.arg, (void *)b.tok, b.tmp})
-        if (p) cudaFree(p);
-    const cudaStream_t st = b.st;
-    b = SampleBuf{};
-    b.st = st;
-}
-
-cudaError_t grow(SampleBuf &b, int n) {
-    if (n <= b.cap) return cudaSuccess;
-    release(b);
+cudaError_t tq_sampler_alloc(TqSampler *s, int n) {
+    if (n <= s->cap) return cudaSuccess;
+    tq_sampler_free(s);
     cudaError_t e = cudaSuccess;
     auto get = [&](void **p, size_t bytes) {
         if (e == cudaSuccess) e = tq_dev_malloc(p, bytes);
     };
-    get((void **)&b.v, sizeof(float) * n);
-    get((void **)&b.kin, sizeof(double) * n);
-    get((void **)&b.kout, sizeof(double) * n);
-    get((void **)&b.iin, sizeof(int) * n);
-    get((void **)&b.iout, sizeof(int) * n);
-    get((void **)&b.partial, sizeof(double) * kPBlocks);
-    get((void **)&b.maxl, sizeof(float));
-    get((void **)&b.arg, sizeof(int));
-    get((void **)&b.tok, sizeof(int));
+    get((void **)&s->kin, sizeof(double) * n);
+    get((void **)&s->kout, sizeof(double) * n);
+    get((void **)&s->iin, sizeof(int) * n);
+    get((void **)&s->iout, sizeof(int) * n);
+    get((void **)&s->partial, sizeof(double) * kPBlocks);
+    get((void **)&s->maxl, sizeof(float));
     if (e == cudaSuccess)
-        e = cub::DeviceRadixSort::SortPairsDescending(nullptr, b.tmp_bytes, b.kin, b.kout, b.iin, b.iout, n);
-    get(&b.tmp, b.tmp_bytes);
+        e = cub::DeviceRadixSort::SortPairsDescending(nullptr, s->tmp_bytes, s->kin, s->kout, s->iin, s->iout, n);
+    get(&s->tmp, s->tmp_bytes);
     if (e != cudaSuccess) {
-        release(b);
+        tq_sampler_free(s);
         return e;
     }
-    b.cap = n;
+    s->cap = n;
     return cudaSuccess;
 }
 
+void tq_sampler_free(TqSampler *s) {
+    for (void *p : {(void *)s->kin, (void *)s->kout, (void *)s->iin, (void *)s->iout, (void *)s->partial,
+                    (void *)s->maxl, s->tmp})
+        if (p) cudaFree(p);
+    *s = TqSampler{};
+}
+
+cudaError_t tq_launch_sample(const TqSampler &s, const float *logits, int n, double temp, const double *draws,
+                             const int *at, int *id_out, cudaStream_t st) {
+    if (n < 1 || n > s.cap) return cudaErrorInvalidValue;
+    if (temp <= 0) { // the greedy scan
+        sample_max_kernel<<<1, kMaxThreads, 0, st>>>(logits, n, s.maxl, id_out);
+        return cudaGetLastError();
+    }
+    sample_max_kernel<<<1, kMaxThreads, 0, st>>>(logits, n, s.maxl, s.iout);
+    sample_weights_kernel<<<kPBlocks, kPThreads, 0, st>>>(logits, n, s.maxl, temp, s.kin, s.iin, s.partial);
+    cudaError_t e = cudaGetLastError();
+    size_t bytes = s.tmp_bytes;
+    if (e == cudaSuccess)
+        e = cub::DeviceRadixSort::SortPairsDescending(s.tmp, bytes, s.kin, s.kout, s.iin, s.iout, n, 0,
+                                                      (int)sizeof(double) * 8, st);
+    if (e == cudaSuccess) {
+        sample_pick_kernel<<<1, 32, 0, st>>>(s.kout, s.iout, n, s.partial, kPBlocks, draws, at, id_out);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+namespace {
+// Per-device state of the host-pointer call.
+struct SampleDev {
+    TqSampler smp;
+    float *v = nullptr;
+    int vcap = 0;
+    double *u = nullptr;
+    int *tok = nullptr;
+    cudaStream_t st = nullptr;
+};
+std::mutex g_sample_mu;
+std::unordered_map<int, SampleDev> g_sample;
 } // namespace
+
+int tq_check_draws(double temp, const double *draws, int n_draws) {
+    if (temp != temp) return tq_fail(TQ_ERR_ARG, "tensai: sampling temperature is NaN");
+    if (temp <= 0) return TQ_OK;
+    if (!draws || n_draws < 1) return tq_fail(TQ_ERR_ARG, "tensai: temperature %g needs at least one draw", temp);
+    for (int i = 0; i < n_draws; i++)
+        if (!(draws[i] >= 0 && draws[i] <= 1))
+            return tq_fail(TQ_ERR_ARG, "tensai: draw %d (%g) outside [0, 1]", i, draws[i]);
+    return TQ_OK;
+}
 
 extern "C" int tq_sample(const float *logits, int n, double temp, double u, int *token) {
     if (!logits || !token) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
@@ -175,30 +204,23 @@ extern "C" int tq_sample(const float *logits, int n, double temp, double u, int 
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return tq_cuda_fail(e, "sample");
-    SampleBuf &b = g_sample[dev];
+    SampleDev &b = g_sample[dev];
     if (!b.st && (e = cudaStreamCreateWithFlags(&b.st, cudaStreamNonBlocking)) != cudaSuccess)
         return tq_cuda_fail(e, "sample stream");
-    if ((e = grow(b, n)) != cudaSuccess) return tq_cuda_fail(e, "sample buffers");
+    if (!b.u && (e = tq_dev_malloc((void **)&b.u, sizeof(double))) != cudaSuccess) return tq_cuda_fail(e, "sample");
+    if (!b.tok && (e = tq_dev_malloc((void **)&b.tok, sizeof(int))) != cudaSuccess) return tq_cuda_fail(e, "sample");
+    if (n > b.vcap) {
+        if (b.v) cudaFree(b.v);
+        b.v = nullptr;
+        b.vcap = 0;
+        if ((e = tq_dev_malloc((void **)&b.v, sizeof(float) * n)) != cudaSuccess) return tq_cuda_fail(e, "sample");
+        b.vcap = n;
+    }
+    if ((e = tq_sampler_alloc(&b.smp, n)) != cudaSuccess) return tq_cuda_fail(e, "sample buffers");
     e = cudaMemcpyAsync(b.v, logits, sizeof(float) * n, cudaMemcpyHostToDevice, b.st);
-    if (e == cudaSuccess) {
-        sample_max_kernel<<<1, kMaxThreads, 0, b.st>>>(b.v, n, b.maxl, b.arg);
-        e = cudaGetLastError();
-    }
-    if (e == cudaSuccess && temp <= 0) {
-        e = cudaMemcpyAsync(token, b.arg, sizeof(int), cudaMemcpyDeviceToHost, b.st);
-    } else if (e == cudaSuccess) {
-        sample_weights_kernel<<<kPBlocks, kPThreads, 0, b.st>>>(b.v, n, b.maxl, temp, b.kin, b.iin, b.partial);
-        e = cudaGetLastError();
-        size_t bytes = b.tmp_bytes;
-        if (e == cudaSuccess)
-            e = cub::DeviceRadixSort::SortPairsDescending(b.tmp, bytes, b.kin, b.kout, b.iin, b.iout, n, 0,
-                                                          (int)sizeof(double) * 8, b.st);
-        if (e == cudaSuccess) {
-            sample_pick_kernel<<<1, 32, 0, b.st>>>(b.kout, b.iout, n, b.partial, kPBlocks, u, b.tok);
-            e = cudaGetLastError();
-        }
-        if (e == cudaSuccess) e = cudaMemcpyAsync(token, b.tok, sizeof(int), cudaMemcpyDeviceToHost, b.st);
-    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b.u, &u, sizeof(double), cudaMemcpyHostToDevice, b.st);
+    if (e == cudaSuccess) e = tq_launch_sample(b.smp, b.v, n, temp, b.u, nullptr, b.tok, b.st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(token, b.tok, sizeof(int), cudaMemcpyDeviceToHost, b.st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b.st);
     if (e != cudaSuccess) return tq_cuda_fail(e, "sample");
     return TQ_OK;

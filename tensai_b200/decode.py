@@ -53,6 +53,13 @@ class Gpt2:
         self.last_times_ms = (t[0], t[1])
         return out
 
+    def set_sampling(self, temp: float, draws=None) -> None:
+        """temp <= 0: greedy (the default); temp > 0: generated token k is
+        drawn by the sample step with draws[k] (tq_gpt2_set_sampling)."""
+        d = np.ascontiguousarray(draws if draws is not None else [], np.float64)
+        _lib.check(_lib.load().tq_gpt2_set_sampling(self.handle, float(temp), d.ctypes.data_as(ctypes.c_void_p) if len(d)
+                                                    else None, len(d)))
+
     def free(self) -> None:
         if self.handle:
             _lib.load().tq_gpt2_free(self.handle)
@@ -148,6 +155,12 @@ class Qwen:
         way, the parity mode); 16..64: in chunks of that many rows on the tf32
         tensor-core matmul (tq_qwen_set_prefill)."""
         _lib.check(_lib.load().tq_qwen_set_prefill(self.handle, rows))
+
+    def set_sampling(self, temp: float, draws=None) -> None:
+        """As Gpt2.set_sampling (tq_qwen_set_sampling; one GPU only)."""
+        d = np.ascontiguousarray(draws if draws is not None else [], np.float64)
+        _lib.check(_lib.load().tq_qwen_set_sampling(self.handle, float(temp), d.ctypes.data_as(ctypes.c_void_p) if len(d)
+                                                    else None, len(d)))
 
     @property
     def exchange(self) -> str:
