@@ -1,4 +1,4 @@
-// tq_model.cu — greedy decode engine of tensai's GPT-2 example
+// tq_model.cu — decode engine of tensai's GPT-2 example
 // (_example/gpt2/model.go, main.go) on one B200: fp32 prefill with the
 // unquantized weights, then int8 weight-only decode, weights and the fp32 KV
 // cache resident in HBM, one CUDA graph per generated token.
@@ -10,13 +10,14 @@
 // and add, positions in order; prefill matmuls as tensai's dotRows (one fused
 // multiply-add chain per output over k in order, zero activations skipped);
 // decode matvecs on the library's int8 kernels; argmax with a strict > (ties
-// to the lowest id). Only reduction orders of the float64 sums differ from
-// the sequential Go loops.
+// to the lowest id), or the sample step with the caller's draws
+// (tq_gpt2_set_sampling, main.go:78-105). Only reduction orders of the
+// float64 sums differ from the sequential Go loops.
 //
 // Device state (int[3]): the token to feed, its position, tokens generated.
 // Every kernel of a decode step reads the position from there, so one
-// captured graph serves every step; the argmax kernel writes the next token
-// and advances the state.
+// captured graph serves every step; the pick (argmax or sample) writes the
+// next token and advances the state.
 #include <cstdio>
 #include <memory>
 #include <mutex>
@@ -344,7 +345,7 @@ cudaError_t sgemm(const float *A, const float *B, float *C, int M, int N, int K,
 }
 
 
-// prefill (model.go:361-401) of T prompt tokens, then the first greedy pick.
+// prefill (model.go:361-401) of T prompt tokens, then the first pick.
 cudaError_t prefill(Gpt2 &m, const int *prompt, int T) {
     const int d = m.c.d, ffn = m.c.ffn, hd = d / m.c.n_head;
     TRY(ensure_prefill(m, T));

@@ -1,4 +1,4 @@
-// tq_qwen.cu — greedy decode engine of tensai's Qwen2 example
+// tq_qwen.cu — decode engine of tensai's Qwen2 example
 // (_example/qwen/model.go:182-307, main.go:225-240) with int4 group-64
 // weights, tensor-parallel over 1, 2, 4 or 8 GPUs of one node, one process
 // per GPU.
@@ -14,14 +14,18 @@
 //   down      row shard of ffn/world rows;
 //   lm head   column shard of vocab/world, greedy pick per shard, then the
 //             candidates (value, id) of all GPUs gathered, ties to the lower id.
-// The o_proj and down partial sums meet in an NCCL all-reduce (sum), the only
-// exchange of the step; NCCL is resolved at run time from the process (the
-// library torch loaded), so the whole step, collectives included, is one
-// CUDA graph replayed per token.
+// The o_proj and down partial sums meet in the step's exchanges: one kernel
+// each that stores this GPU's partial into every peer's memory over NVLink
+// and adds all ranks' partials in rank order, fused with the residual add and
+// RMSNorm after it (the candidates likewise, in the advance kernel); NCCL's
+// all-reduce where peer memory cannot be mapped, and for the batched
+// prefill. NCCL is resolved at run time from the process (the library torch
+// loaded). The whole step is one CUDA graph replayed per token.
 //
 // The prompt goes through the same step one token at a time (main.go:229-231):
 // the step's last kernel feeds the next prompt id while the prompt lasts and
-// the greedy pick after it.
+// the picked token after it (greedy, or the sample step with the caller's
+// draws: tq_qwen_set_sampling); tq_qwen_set_prefill batches it instead.
 //
 // Numerics as the Go code: RMSNorm, RoPE, attention scores, softmax and SiLU
 // in float64, residuals and the value sum in float32, products unfused.
