@@ -92,3 +92,23 @@ def test_missing_library_fails_loudly(tmp_path):
     r = subprocess.run(["python", "-c", code, str(tmp_path / "nope.so")], capture_output=True, text=True,
                        cwd=_lib._HERE + "/..")
     assert "IMPORTERROR" in r.stdout
+
+
+def test_sample_argument_checks_need_no_gpu(L):
+    """tq_sample rejects its bad arguments before any CUDA call (the sample
+    step of _example/gpt2/main.go:78-105 takes a non-empty logit slice)."""
+    v = np.zeros(4, np.float32)
+    tok = ctypes.c_int(-7)
+    p = v.ctypes.data_as(ctypes.c_void_p)
+    assert L.tq_sample(p, 0, 1.0, 0.5, ctypes.byref(tok)) == _lib.TQ_ERR_ARG
+    assert "at least one logit" in L.tq_last_error().decode()
+    assert L.tq_sample(p, 4, float("nan"), 0.5, ctypes.byref(tok)) == _lib.TQ_ERR_ARG
+    assert L.tq_sample(p, 4, 1.0, -0.1, ctypes.byref(tok)) == _lib.TQ_ERR_ARG
+    assert L.tq_sample(None, 4, 1.0, 0.5, ctypes.byref(tok)) == _lib.TQ_ERR_ARG
+    assert tok.value == -7  # nothing written on an error
+
+
+def test_sampling_settings_of_an_unknown_model_are_an_error(L):
+    d = (ctypes.c_double * 1)(0.5)
+    assert L.tq_gpt2_set_sampling(98765, 1.0, d, 1) == _lib.TQ_ERR_HANDLE
+    assert L.tq_qwen_set_sampling(98765, 1.0, d, 1) == _lib.TQ_ERR_HANDLE
