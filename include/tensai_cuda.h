@@ -320,6 +320,25 @@ TQ_EXPORT int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sig
 TQ_EXPORT int tq_qwen_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen, int *tokens,
                                float *times_ms);
 
+/* A one-GPU Qwen2 model whose weights come from a checkpoint instead of the
+ * random-init generator: matrices zeroed, norm weights 1, biases 0, until
+ * tq_qwen_load_tensor fills them (loadQwen, _example/qwen/model.go:95-177). */
+TQ_EXPORT int tq_qwen_create_empty(const tq_qwen_config *cfg, uint64_t *model);
+
+/* One checkpoint tensor, by its Hugging Face name, from device memory in its
+ * stored layout and type (TQ_LINEAR_F32 / F16 / BF16; Linear weights
+ * [out, in] = rows x cols, vectors 1 x n): model.embed_tokens.weight (widened
+ * to float32), lm_head.weight (a tied checkpoint passes the embedding under
+ * this name), model.norm.weight, and per layer model.layers.N. +
+ * self_attn.{q,k,v}_proj.{weight,bias}, self_attn.o_proj.weight,
+ * mlp.{gate,up,down}_proj.weight, input_layernorm.weight,
+ * post_attention_layernorm.weight. Linear weights are quantized on the device
+ * as QuantizeMatrix4 of Matrix().T() (the q|k|v and gate|up parts once all of
+ * a fused matrix arrived). Synchronous; the caller may free data on return.
+ * TQ_ERR_SHAPE for a wrong shape, TQ_ERR_ARG for an unknown name or a model
+ * made by tq_qwen_create. */
+TQ_EXPORT int tq_qwen_load_tensor(uint64_t model, const char *name, const void *data, int dtype, int rows, int cols);
+
 /* How tq_qwen_generate processes the prompt. rows = 0 (the default) feeds it
  * token by token through the decode step, as the reference does
  * (_example/qwen/main.go:229-231): the parity mode. rows in 16..64 runs it in

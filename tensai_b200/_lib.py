@@ -63,6 +63,8 @@ SIGNATURES = {
     "tq_qwen_generate": (I, [U64, P, I, I, P, P]),
     "tq_qwen_set_prefill": (I, [U64, I]),
     "tq_qwen_exchange": (I, [U64, ctypes.POINTER(ctypes.c_int)]),
+    "tq_qwen_create_empty": (I, [P, PU64]),
+    "tq_qwen_load_tensor": (I, [U64, ctypes.c_char_p, P, I, I, I]),
     "tq_sample": (I, [P, I, ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_int)]),
     "tq_gpt2_set_sampling": (I, [U64, ctypes.c_double, P, I]),
     "tq_qwen_set_sampling": (I, [U64, ctypes.c_double, P, I]),

@@ -29,12 +29,15 @@
 //
 // Numerics as the Go code: RMSNorm, RoPE, attention scores, softmax and SiLU
 // in float64, residuals and the value sum in float32, products unfused.
+#include <cuda_fp16.h>
 #include <dlfcn.h>
 #include <nccl.h>
 
 #include <cstdlib>
+#include <cstdio>
 #include <cstring>
 #include <memory>
+#include <string>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -426,6 +429,20 @@ __global__ void copy_cols_kernel(const float *in, int in_cols, int in_col0, floa
     }
 }
 
+// dst[i] = float32 of src[i] (TQ_LINEAR_F32, F16 or BF16; both widenings exact).
+__global__ void widen_kernel(const void *src, int dtype, float *dst, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v;
+        if (dtype == TQ_LINEAR_F32)
+            v = static_cast<const float *>(src)[i];
+        else if (dtype == TQ_LINEAR_F16)
+            v = __half2float(static_cast<const __half *>(src)[i]);
+        else
+            v = __uint_as_float((unsigned)static_cast<const unsigned short *>(src)[i] << 16);
+        dst[i] = v;
+    }
+}
+
 // ---- one-shot exchange over NVLink peer memory -----------------------------------
 // Each rank owns a slot area of [2 parities][world][cap] 8-byte words in its
 // own HBM, mapped into every other rank by CUDA IPC. Exchange call e (1, 2, …
@@ -646,6 +663,12 @@ __global__ void ar_advance_kernel(ArLink L, const int *cand, int *cands, int *st
 struct Layer {
     TqMatrixDev qkv{}, o{}, gu{}, down{};
     float *kc = nullptr, *vc = nullptr; // [ctx][kvd]
+    // norm weights (input, post-attention) and the q|k|v bias of this GPU's
+    // heads: the engine's ones / zeros for random-init weights
+    float *ln1 = nullptr, *ln2 = nullptr, *qkvb = nullptr;
+    // checkpoint loading: q|k|v and gate|up rows staged until all parts came
+    void *stage_qkv = nullptr, *stage_gu = nullptr;
+    int got_qkv = 0, got_gu = 0, stage_dtype = -1;
 };
 
 struct Qwen {
@@ -657,6 +680,8 @@ struct Qwen {
     TqScratch scr{};
     ncclComm_t comm = nullptr;
     float *embed = nullptr, *ones = nullptr, *zeros = nullptr;
+    float *normw = nullptr; // the final norm's weight
+    bool loaded = false;          // tq_qwen_create_empty: weights come from tq_qwen_load_tensor
     std::vector<Layer> L;
     TqMatrixDev lm{};
     float *x, *a, *qkv, *att, *y, *h, *logits;
@@ -714,8 +739,12 @@ void destroy(Qwen &m) {
     m.ar_on = false;
     if (m.comm) g_nccl.commDestroy(m.comm);
     m.comm = nullptr;
-    for (Layer &l : m.L)
+    for (Layer &l : m.L) {
         for (TqMatrixDev *w : {&l.qkv, &l.o, &l.gu, &l.down}) tq_release_matrix(w);
+        for (void *p : {l.stage_qkv, l.stage_gu})
+            if (p) cudaFree(p);
+        l.stage_qkv = l.stage_gu = nullptr;
+    }
     tq_release_matrix(&m.lm);
     for (void *p : m.allocs) cudaFree(p);
     m.allocs.clear();
@@ -740,19 +769,52 @@ cudaError_t copy_cols(Qwen &m, const float *in, int in_cols, int in_col0, float 
     return cudaGetLastError();
 }
 
+cudaError_t buffers(Qwen &m, int *rc);
+
 cudaError_t build(Qwen &m, uint64_t seed, float sigma, int *rc) {
     const tq_qwen_config &c = m.c;
     const int d = c.d, ffn = c.ffn;
     const int kv_full = c.n_kv * m.hd;
     TRY(cudaStreamCreateWithFlags(&m.st, cudaStreamNonBlocking));
     TRY(dalloc(m, (void **)&m.embed, sizeof(float) * (size_t)c.vocab * d));
-    TRY(tq_launch_synth(m.embed, (size_t)c.vocab * d, seed, 1, sigma, m.st));
+    if (m.loaded)
+        TRY(cudaMemsetAsync(m.embed, 0, sizeof(float) * (size_t)c.vocab * d, m.st));
+    else
+        TRY(tq_launch_synth(m.embed, (size_t)c.vocab * d, seed, 1, sigma, m.st));
     const size_t vec = (size_t)(d > m.qd + 2 * m.kvd ? d : m.qd + 2 * m.kvd);
     TRY(dalloc(m, (void **)&m.ones, sizeof(float) * vec));
     TRY(dalloc(m, (void **)&m.zeros, sizeof(float) * vec));
     fill_kernel<<<grid_for(vec), kThreads, 0, m.st>>>(m.ones, 1.f, vec);
     fill_kernel<<<grid_for(vec), kThreads, 0, m.st>>>(m.zeros, 0.f, vec);
     TRY(cudaGetLastError());
+    m.normw = m.ones;
+    if (m.loaded) { // checkpoint weights: zeroed matrices, per-layer norm weights (1) and biases (0) to fill
+        const int qkvc = m.qd + 2 * m.kvd;
+        auto vec_of = [&](float v, int n, float **out) -> cudaError_t {
+            float *p = nullptr;
+            TRY(dalloc(m, (void **)&p, sizeof(float) * n));
+            fill_kernel<<<grid_for(n), kThreads, 0, m.st>>>(p, v, (size_t)n);
+            *out = p;
+            return cudaGetLastError();
+        };
+        TRY(vec_of(1.f, d, &m.normw));
+        m.L.resize(c.n_layer);
+        for (Layer &ly : m.L) {
+            if ((*rc = tq_alloc_matrix(4, d, qkvc, &ly.qkv, m.st)) != TQ_OK ||
+                (*rc = tq_alloc_matrix(4, m.orows, d, &ly.o, m.st)) != TQ_OK ||
+                (*rc = tq_alloc_matrix(4, d, 2 * m.fcols, &ly.gu, m.st)) != TQ_OK ||
+                (*rc = tq_alloc_matrix(4, m.fcols, d, &ly.down, m.st)) != TQ_OK)
+                return cudaErrorMemoryAllocation;
+            TRY(vec_of(1.f, d, &ly.ln1));
+            TRY(vec_of(1.f, d, &ly.ln2));
+            TRY(vec_of(0.f, qkvc, &ly.qkvb));
+            TRY(dalloc(m, (void **)&ly.kc, sizeof(float) * (size_t)c.ctx * m.kvd));
+            TRY(dalloc(m, (void **)&ly.vc, sizeof(float) * (size_t)c.ctx * m.kvd));
+        }
+        if ((*rc = tq_alloc_matrix(4, d, m.vcols, &m.lm, m.st)) != TQ_OK) return cudaErrorMemoryAllocation;
+        TRY(cudaStreamSynchronize(m.st));
+        return buffers(m, rc);
+    }
     // fp32 scratch: the largest full matrix, and the largest (fused) shard
     size_t full = (size_t)d * c.vocab, shard = (size_t)d * m.vcols;
     for (size_t n : {(size_t)d * d, (size_t)d * kv_full, (size_t)d * ffn}) full = n > full ? n : full;
@@ -768,6 +830,8 @@ cudaError_t build(Qwen &m, uint64_t seed, float sigma, int *rc) {
         m.L.resize(c.n_layer);
         for (int l = 0; l < c.n_layer; l++) {
             Layer &ly = m.L[l];
+            ly.ln1 = ly.ln2 = m.ones;
+            ly.qkvb = m.zeros;
             const uint64_t s0 = 32 + 16 * (uint64_t)l;
             const int qkvc = m.qd + 2 * m.kvd;
             // q | k | v columns of this GPU's attention heads
@@ -804,6 +868,13 @@ cudaError_t build(Qwen &m, uint64_t seed, float sigma, int *rc) {
     cudaFree(wfull);
     cudaFree(wshard);
     TRY(e);
+    return buffers(m, rc);
+}
+
+// The step's activation, state and scratch buffers (after the weights).
+cudaError_t buffers(Qwen &m, int *rc) {
+    const tq_qwen_config &c = m.c;
+    const int d = c.d;
     TRY(dalloc(m, (void **)&m.x, sizeof(float) * d));
     TRY(dalloc(m, (void **)&m.a, sizeof(float) * d));
     TRY(dalloc(m, (void **)&m.qkv, sizeof(float) * (m.qd + 2 * m.kvd)));
@@ -917,43 +988,43 @@ cudaError_t ar_setup(Qwen &m) {
 // was also let in early beside it).
 cudaError_t step(Qwen &m, int n_prompt) {
     const int d = m.c.d;
-    TRY(step_launch(embed_norm_kernel, dim3(1), dim3(1024), 0, m.st, m.embed, m.state, m.x, m.ones, m.a, d, m.c.eps,
-                    m.rope, m.hd, m.c.theta));
+    TRY(step_launch(embed_norm_kernel, dim3(1), dim3(1024), 0, m.st, m.embed, m.state, m.x, m.L[0].ln1, m.a, d,
+                    m.c.eps, m.rope, m.hd, m.c.theta));
     AttRope rope;
     rope.cs = m.rope;
     rope.k = m.qkv + m.qd;
     rope.v = m.qkv + m.qd + m.kvd;
-    rope.qbias = m.zeros;
-    rope.kbias = m.zeros + m.qd;
-    rope.vbias = m.zeros + m.qd + m.kvd;
-    // x += the all-reduced y (an o_proj or down_proj output), then a = RMSNorm(x)
-    auto add_norm = [&]() -> cudaError_t {
+    // x += the all-reduced y (an o_proj or down_proj output), then a = RMSNorm(x) * w
+    auto add_norm = [&](const float *w) -> cudaError_t {
         if (m.ar_on)
-            return step_launch(ar_rmsnorm_kernel, dim3(1), dim3(1024), m.ar_smem, m.st, m.ar, m.x, m.y, m.ones, m.a,
-                               d, m.c.eps, m.scr.status);
+            return step_launch(ar_rmsnorm_kernel, dim3(1), dim3(1024), m.ar_smem, m.st, m.ar, m.x, m.y, w, m.a, d,
+                               m.c.eps, m.scr.status);
         if (m.world > 1) {
             TRY(nccl_err(g_nccl.allReduce(m.y, m.y, d, ncclFloat32, ncclSum, m.comm, m.st)));
-            return step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, m.y, m.ones, m.a, d, m.c.eps);
+            return step_launch(rmsnorm_kernel, dim3(1), dim3(1024), 0, m.st, m.x, m.y, w, m.a, d, m.c.eps);
         }
         // 512 threads: small enough to be resident beside the matvec before it, ready when it completes
-        return step_launch_early(rmsnorm_kernel, dim3(1), dim3(512), 0, m.st, m.x, m.y, m.ones, m.a, d, m.c.eps);
+        return step_launch_early(rmsnorm_kernel, dim3(1), dim3(512), 0, m.st, m.x, m.y, w, m.a, d, m.c.eps);
     };
     bool pending = false; // the previous down_proj output is still to be added to x
     for (Layer &ly : m.L) {
-        if (pending) TRY(add_norm());
+        if (pending) TRY(add_norm(ly.ln1));
         TRY(tq_launch_matmul(ly.qkv, m.a, m.qkv, 1, m.scr, m.st));
+        rope.qbias = ly.qkvb;
+        rope.kbias = ly.qkvb + m.qd;
+        rope.vbias = ly.qkvb + m.qd + m.kvd;
         rope.kc = ly.kc;
         rope.vc = ly.vc;
         TRY(decode_attention(m.qkv, ly.kc, ly.vc, m.kvd, m.att, m.state, m.nq, m.hd, m.group,
                              1.0 / sqrt((double)m.hd), m.att_scr, m.st, rope));
         TRY(tq_launch_matmul(ly.o, m.att + m.arow, m.y, 1, m.scr, m.st));
-        TRY(add_norm()); // x += o_proj, then norm
+        TRY(add_norm(ly.ln2)); // x += o_proj, then norm
         TRY(tq_launch_cmv_epi(ly.gu, m.a, m.h, m.scr, m.st, TQ_EPI_SWIGLU, tq_matvec_uses_tmv()));
         TRY(tq_launch_matmul(ly.down, m.h, m.y, 1, m.scr, m.st));
         pending = true;
         TRY(cudaGetLastError());
     }
-    if (pending) TRY(add_norm());
+    if (pending) TRY(add_norm(m.normw));
     TRY(tq_launch_matmul(m.lm, m.a, m.logits, 1, m.scr, m.st));
     TRY(pick_next(m));
     if (m.ar_on)
@@ -982,24 +1053,24 @@ cudaError_t prefill(Qwen &m, int n_prompt) {
     const size_t pf_smem = prefill_attention_smem(m.hd, n_prompt);
     for (int c0 = 0; c0 < n_prompt; c0 += R) {
         const int rows = n_prompt - c0 < R ? n_prompt - c0 : R;
-        embed_rows_kernel<<<rows, 1024, 0, m.st>>>(m.embed, m.prompt, c0, m.px, m.ones, m.pa, d, m.c.eps);
+        embed_rows_kernel<<<rows, 1024, 0, m.st>>>(m.embed, m.prompt, c0, m.px, m.L[0].ln1, m.pa, d, m.c.eps);
         TRY(cudaGetLastError());
         for (size_t l = 0; l < m.L.size(); l++) {
             Layer &ly = m.L[l];
             if (l > 0) { // x += the previous layer's down_proj, then the norm
-                rmsnorm_kernel<<<rows, 1024, 0, m.st>>>(m.px, m.py, m.ones, m.pa, d, m.c.eps);
+                rmsnorm_kernel<<<rows, 1024, 0, m.st>>>(m.px, m.py, ly.ln1, m.pa, d, m.c.eps);
                 TRY(cudaGetLastError());
             }
             TRY(tq_launch_matmul(ly.qkv, m.pa, m.pqkv, rows, m.scr, m.st));
-            rope_rows_kernel<<<rows, 256, 0, m.st>>>(m.pqkv, qkvc, m.nq, m.nkv, m.hd, c0, m.c.theta, m.zeros,
-                                                     m.zeros + m.qd, m.zeros + m.qd + m.kvd, ly.kc, ly.vc);
+            rope_rows_kernel<<<rows, 256, 0, m.st>>>(m.pqkv, qkvc, m.nq, m.nkv, m.hd, c0, m.c.theta, ly.qkvb,
+                                                     ly.qkvb + m.qd, ly.qkvb + m.qd + m.kvd, ly.kc, ly.vc);
             prefill_attention_kernel<<<dim3(m.nq, (rows + kPfRows - 1) / kPfRows), kPfThreads, pf_smem, m.st>>>(
                 m.pqkv, qkvc, ly.kc, ly.vc, m.kvd, m.patt, m.qd, m.hd, m.group, scale, c0, rows, n_prompt);
             TRY(cudaGetLastError());
             TRY(tq_launch_matmul(ly.o, m.patt, m.py, rows, m.scr, m.st));
             if (m.world > 1)
                 TRY(nccl_err(g_nccl.allReduce(m.py, m.py, (size_t)rows * d, ncclFloat32, ncclSum, m.comm, m.st)));
-            rmsnorm_kernel<<<rows, 1024, 0, m.st>>>(m.px, m.py, m.ones, m.pa, d, m.c.eps); // x += o_proj, then norm
+            rmsnorm_kernel<<<rows, 1024, 0, m.st>>>(m.px, m.py, ly.ln2, m.pa, d, m.c.eps); // x += o_proj, then norm
             TRY(cudaGetLastError());
             TRY(tq_launch_matmul(ly.gu, m.pa, m.pgu, rows, m.scr, m.st));
             swiglu_rows_kernel<<<grid_for((size_t)rows * m.fcols), kThreads, 0, m.st>>>(m.pgu, m.ph, m.fcols, rows);
@@ -1012,7 +1083,7 @@ cudaError_t prefill(Qwen &m, int n_prompt) {
     // the prompt's last row: its final residual add and norm, the lm head, the pick
     const int last = (n_prompt - 1) % R;
     set_state_kernel<<<1, 1, 0, m.st>>>(m.state, 0, n_prompt - 1, 0);
-    rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.px + (size_t)last * d, m.py + (size_t)last * d, m.ones, m.a, d, m.c.eps);
+    rmsnorm_kernel<<<1, 1024, 0, m.st>>>(m.px + (size_t)last * d, m.py + (size_t)last * d, m.normw, m.a, d, m.c.eps);
     TRY(cudaGetLastError());
     TRY(tq_launch_matmul(m.lm, m.a, m.logits, 1, m.scr, m.st));
     TRY(pick_next(m));
@@ -1084,8 +1155,8 @@ int tq_nccl_unique_id(void *id) {
     return TQ_OK;
 }
 
-int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sigma, int rank, int world, const void *nccl_id,
-                   uint64_t *model) {
+static int qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sigma, int rank, int world,
+                       const void *nccl_id, bool loaded, uint64_t *model) {
     if (!cfg || !model) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
     const tq_qwen_config &c = *cfg;
     ShardPlan sp;
@@ -1112,6 +1183,7 @@ int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sigma, int ra
     m->fcols = sp.fcols;
     m->vcols = sp.vcols;
     m->voff = sp.voff;
+    m->loaded = loaded;
     int rc = TQ_OK;
     cudaError_t e = cudaGetDevice(&m->device);
     if (e == cudaSuccess && world > 1) {
@@ -1130,6 +1202,112 @@ int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sigma, int ra
     std::lock_guard<std::mutex> lk(g_q_mu);
     *model = g_next_qwen++;
     g_qwens[*model] = m;
+    return TQ_OK;
+}
+
+int tq_qwen_create(const tq_qwen_config *cfg, uint64_t seed, float sigma, int rank, int world, const void *nccl_id,
+                   uint64_t *model) {
+    return qwen_create(cfg, seed, sigma, rank, world, nccl_id, false, model);
+}
+
+int tq_qwen_create_empty(const tq_qwen_config *cfg, uint64_t *model) {
+    return qwen_create(cfg, 0, 0.f, 0, 1, nullptr, true, model);
+}
+
+int tq_qwen_load_tensor(uint64_t model, const char *name, const void *data, int dtype, int rows, int cols) {
+    if (!name || !data) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    if (dtype != TQ_LINEAR_F32 && dtype != TQ_LINEAR_F16 && dtype != TQ_LINEAR_BF16)
+        return tq_fail(TQ_ERR_ARG, "tensai: unknown tensor type %d", dtype);
+    int rc = TQ_OK;
+    auto m = find(model, &rc);
+    if (!m) return rc;
+    if (!m->loaded) return tq_fail(TQ_ERR_ARG, "tensai: %s: the model holds random-init weights", name);
+    const tq_qwen_config &c = m->c;
+    const int d = c.d, qd = m->qd, kvd = m->kvd, ffn = c.ffn;
+    const size_t es = dtype == TQ_LINEAR_F32 ? 4 : 2;
+    cudaError_t e = cudaSetDevice(m->device);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "tensor load");
+    auto shape = [&](int r, int cc) {
+        return rows == r && cols == cc ? TQ_OK
+                                       : tq_fail(TQ_ERR_SHAPE, "tensai: %s is %d x %d, expected %d x %d", name, rows,
+                                                 cols, r, cc);
+    };
+    auto widen = [&](float *dst) {
+        widen_kernel<<<grid_for((size_t)rows * cols), kThreads, 0, m->st>>>(data, dtype, dst, (size_t)rows * cols);
+        return cudaGetLastError();
+    };
+    // rows [row0, row0 + rows) of a fused [total x d] matrix staged in *stage;
+    // once every part (bit) arrived, quantized into w and the stage freed
+    auto stage = [&](Layer &ly, void **st, int *got, int bit, int all, int row0, int total, TqMatrixDev &w) {
+        if (ly.stage_dtype >= 0 && ly.stage_dtype != dtype)
+            return tq_fail(TQ_ERR_ARG, "tensai: %s: the parts of a fused matrix differ in type", name);
+        cudaError_t err = cudaSuccess;
+        if (!*st) err = tq_dev_malloc(st, es * (size_t)total * d);
+        if (err == cudaSuccess)
+            err = cudaMemcpyAsync(static_cast<char *>(*st) + es * (size_t)row0 * d, data, es * (size_t)rows * cols,
+                                  cudaMemcpyDeviceToDevice, m->st);
+        if (err != cudaSuccess) return tq_cuda_fail(err, "tensor staging");
+        ly.stage_dtype = dtype;
+        *got |= bit;
+        if (*got == all) {
+            err = tq_launch_quantize_linear(w, *st, dtype, m->st);
+            if (err == cudaSuccess) err = cudaStreamSynchronize(m->st);
+            cudaFree(*st);
+            *st = nullptr;
+            *got = 0;
+            if (err != cudaSuccess) return tq_cuda_fail(err, "tensor quantize");
+        }
+        return TQ_OK;
+    };
+    auto linear = [&](TqMatrixDev &w) {
+        cudaError_t err = tq_launch_quantize_linear(w, data, dtype, m->st);
+        return err == cudaSuccess ? TQ_OK : tq_cuda_fail(err, "tensor quantize");
+    };
+    const std::string n(name);
+    int l = -1, used = 0;
+    char rest[96] = {};
+    if (n == "model.embed_tokens.weight") {
+        if ((rc = shape(c.vocab, d)) == TQ_OK && (e = widen(m->embed)) != cudaSuccess) rc = tq_cuda_fail(e, "embed");
+    } else if (n == "model.norm.weight") {
+        if ((rc = shape(1, d)) == TQ_OK && (e = widen(m->normw)) != cudaSuccess) rc = tq_cuda_fail(e, "norm");
+    } else if (n == "lm_head.weight") {
+        if ((rc = shape(c.vocab, d)) == TQ_OK) rc = linear(m->lm);
+    } else if (std::sscanf(name, "model.layers.%d.%95s%n", &l, rest, &used) == 2 && (size_t)used == n.size() &&
+               l >= 0 && l < c.n_layer) {
+        Layer &ly = m->L[l];
+        const std::string r(rest);
+        const int qkvc = qd + 2 * kvd;
+        if (r == "self_attn.q_proj.weight") {
+            if ((rc = shape(qd, d)) == TQ_OK) rc = stage(ly, &ly.stage_qkv, &ly.got_qkv, 1, 7, 0, qkvc, ly.qkv);
+        } else if (r == "self_attn.k_proj.weight") {
+            if ((rc = shape(kvd, d)) == TQ_OK) rc = stage(ly, &ly.stage_qkv, &ly.got_qkv, 2, 7, qd, qkvc, ly.qkv);
+        } else if (r == "self_attn.v_proj.weight") {
+            if ((rc = shape(kvd, d)) == TQ_OK)
+                rc = stage(ly, &ly.stage_qkv, &ly.got_qkv, 4, 7, qd + kvd, qkvc, ly.qkv);
+        } else if (r == "self_attn.q_proj.bias" || r == "self_attn.k_proj.bias" || r == "self_attn.v_proj.bias") {
+            const int off = r[10] == 'q' ? 0 : r[10] == 'k' ? qd : qd + kvd, len = r[10] == 'q' ? qd : kvd;
+            if ((rc = shape(1, len)) == TQ_OK && (e = widen(ly.qkvb + off)) != cudaSuccess)
+                rc = tq_cuda_fail(e, "bias");
+        } else if (r == "self_attn.o_proj.weight") {
+            if ((rc = shape(d, qd)) == TQ_OK) rc = linear(ly.o);
+        } else if (r == "mlp.gate_proj.weight") {
+            if ((rc = shape(ffn, d)) == TQ_OK) rc = stage(ly, &ly.stage_gu, &ly.got_gu, 1, 3, 0, 2 * ffn, ly.gu);
+        } else if (r == "mlp.up_proj.weight") {
+            if ((rc = shape(ffn, d)) == TQ_OK) rc = stage(ly, &ly.stage_gu, &ly.got_gu, 2, 3, ffn, 2 * ffn, ly.gu);
+        } else if (r == "mlp.down_proj.weight") {
+            if ((rc = shape(d, ffn)) == TQ_OK) rc = linear(ly.down);
+        } else if (r == "input_layernorm.weight") {
+            if ((rc = shape(1, d)) == TQ_OK && (e = widen(ly.ln1)) != cudaSuccess) rc = tq_cuda_fail(e, "norm");
+        } else if (r == "post_attention_layernorm.weight") {
+            if ((rc = shape(1, d)) == TQ_OK && (e = widen(ly.ln2)) != cudaSuccess) rc = tq_cuda_fail(e, "norm");
+        } else {
+            rc = tq_fail(TQ_ERR_ARG, "tensai: unknown Qwen2 tensor %s", name);
+        }
+    } else {
+        rc = tq_fail(TQ_ERR_ARG, "tensai: unknown Qwen2 tensor %s", name);
+    }
+    if (rc != TQ_OK) return rc;
+    if ((e = cudaStreamSynchronize(m->st)) != cudaSuccess) return tq_cuda_fail(e, "tensor load");
     return TQ_OK;
 }
 

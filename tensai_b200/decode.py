@@ -141,6 +141,54 @@ class Qwen:
         self.handle = h.value
         self.last_times_ms = (0.0, 0.0)
 
+    @classmethod
+    def from_checkpoint(cls, cfg: dict, path: str) -> "Qwen":
+        """A one-GPU model with a Hugging Face Qwen2 checkpoint's weights
+        (loadQwen, _example/qwen/model.go:95-177): `path` is a .safetensors
+        file or a model.safetensors.index.json. Each tensor goes to the GPU in
+        its stored type and is quantized there (tq_qwen_create_empty,
+        tq_qwen_load_tensor); a checkpoint without lm_head.weight ties it to
+        the embedding."""
+        from . import safetensors as ST
+        self = cls.__new__(cls)
+        self.cfg = dict(cfg)
+        c = QwenConfig(**self.cfg)
+        h = ctypes.c_uint64()
+        _lib.check(_lib.load().tq_qwen_create_empty(ctypes.byref(c), ctypes.byref(h)))
+        self.handle = h.value
+        self.last_times_ms = (0.0, 0.0)
+        src = ST.OpenSharded(path) if path.endswith(".json") else ST.Open(path)
+
+        def dev(name):
+            return (src.File(name) if isinstance(src, ST.Shards) else src).DeviceTensor(name)
+
+        try:
+            names = src.Names()
+            for name in names:
+                if name.endswith("rotary_emb.inv_freq"):
+                    continue  # recomputed from theta
+                self.load_tensor(name, dev(name))
+            if "lm_head.weight" not in names:
+                self.load_tensor("lm_head.weight", dev("model.embed_tokens.weight"))
+        except BaseException:
+            self.free()
+            raise
+        finally:
+            src.Close()
+        return self
+
+    def load_tensor(self, name: str, t) -> None:
+        """One checkpoint tensor (a CUDA tensor of float32, float16 or
+        bfloat16, in the checkpoint's layout) by its name (tq_qwen_load_tensor)."""
+        import torch
+        kinds = {torch.float32: _lib.TQ_LINEAR_F32, torch.float16: _lib.TQ_LINEAR_F16,
+                 torch.bfloat16: _lib.TQ_LINEAR_BF16}
+        if t.dtype not in kinds or t.dim() not in (1, 2) or not t.is_contiguous():
+            raise ValueError(f"tensai: {name}: a contiguous 1-D or 2-D float32, float16 or bfloat16 tensor is required")
+        rows, cols = (1, t.shape[0]) if t.dim() == 1 else (t.shape[0], t.shape[1])
+        _lib.check(_lib.load().tq_qwen_load_tensor(self.handle, name.encode(), ctypes.c_void_p(t.data_ptr()),
+                                                   kinds[t.dtype], rows, cols))
+
     def generate(self, prompt, n: int) -> np.ndarray:
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.empty(n, np.int32)

@@ -2,6 +2,7 @@
 C ABI. Bar: identical greedy token ids (the -q4 loop of _example/qwen,
 restated in oracle/tq_model.c) on small models, on the Qwen2.5-7B-shaped
 config against committed golden ids, and over 2/4/8 GPUs when present."""
+import ctypes
 import glob
 import os
 
@@ -222,3 +223,85 @@ def test_tensor_parallel_qwen7b_shape_matches_golden_tokens(world):
         assert isinstance(ids, list), ids
         assert kind == "peer"
         assert np.array_equal(ids, z["tokens"]), (r, _diverge(ids, z["tokens"], z["margins"]))
+
+
+# ---- checkpoint loading (tq_qwen_create_empty / tq_qwen_load_tensor) -----------
+
+def _checkpoint(cfg, seed, sigma, scale_proj=1.0, norm=1.0):
+    """The random-init model's weights in a Hugging Face Qwen2 checkpoint's
+    names and [out, in] layout (F32), from the generator streams the engine
+    draws them from; norm weights `norm`, biases 0; scale_proj multiplies the
+    matrices that follow a norm (q, k, v, gate, up, lm head)."""
+    d, ffn, vocab = cfg["d"], cfg["ffn"], cfg["vocab"]
+    kv = cfg["n_kv"] * (d // cfg["n_head"])
+    f32 = np.float32
+    t = {"model.embed_tokens.weight": O.synth((vocab, d), seed, 1, sigma),
+         "lm_head.weight": np.ascontiguousarray(O.synth((d, vocab), seed, 2, sigma).T) * f32(scale_proj),
+         "model.norm.weight": np.full(d, norm, f32)}
+    for l in range(cfg["n_layer"]):
+        s0, p = 32 + 16 * l, f"model.layers.{l}."
+        T = lambda shape, k: np.ascontiguousarray(O.synth(shape, seed, s0 + k, sigma).T)  # noqa: E731
+        t[p + "self_attn.q_proj.weight"] = T((d, d), 0) * f32(scale_proj)
+        t[p + "self_attn.k_proj.weight"] = T((d, kv), 1) * f32(scale_proj)
+        t[p + "self_attn.v_proj.weight"] = T((d, kv), 2) * f32(scale_proj)
+        t[p + "self_attn.o_proj.weight"] = T((d, d), 3)
+        t[p + "mlp.gate_proj.weight"] = T((d, ffn), 4) * f32(scale_proj)
+        t[p + "mlp.up_proj.weight"] = T((d, ffn), 5) * f32(scale_proj)
+        t[p + "mlp.down_proj.weight"] = T((ffn, d), 6)
+        for b, n in (("q", d), ("k", kv), ("v", kv)):
+            t[p + f"self_attn.{b}_proj.bias"] = np.zeros(n, f32)
+        t[p + "input_layernorm.weight"] = np.full(d, norm, f32)
+        t[p + "post_attention_layernorm.weight"] = np.full(d, norm, f32)
+    return t
+
+
+def test_checkpoint_of_the_random_weights_gives_the_same_ids(tmp_path):
+    """Loading, as checkpoint tensors, exactly the weights the random-init
+    engine draws yields the same model: the same greedy ids, token by token
+    and with the batched prefill."""
+    from tensai_b200 import safetensors as ST
+    p = str(tmp_path / "tiny.safetensors")
+    ST.SaveFile(p, _checkpoint(TINY, 4, 0.02))
+    prompt = synth_tokens(20, TINY["vocab"], 4)
+    with Qwen(TINY, 4, 0.02) as ref, Qwen.from_checkpoint(TINY, p) as got:
+        assert np.array_equal(got.generate(prompt, 24), ref.generate(prompt, 24))
+        ref.set_prefill(16)
+        got.set_prefill(16)
+        assert np.array_equal(got.generate(prompt, 24), ref.generate(prompt, 24))
+
+
+def test_checkpoint_norm_weights_feed_their_matrices(tmp_path):
+    """Norm weights of 2 (every input, post-attention and final norm) against
+    the matrices after them doubled: powers of two pass exactly through the
+    int4 scales and the activation digits, so both checkpoints are the same
+    model bit for bit if each norm weight reaches its own matrices."""
+    from tensai_b200 import safetensors as ST
+    pa, pb = str(tmp_path / "a.safetensors"), str(tmp_path / "b.safetensors")
+    ST.SaveFile(pa, _checkpoint(TINY, 5, 0.02, norm=2.0))
+    ST.SaveFile(pb, _checkpoint(TINY, 5, 0.02, scale_proj=2.0))
+    prompt = synth_tokens(16, TINY["vocab"], 5)
+    with Qwen.from_checkpoint(TINY, pa) as a, Qwen.from_checkpoint(TINY, pb) as b:
+        assert np.array_equal(a.generate(prompt, 24), b.generate(prompt, 24))
+
+
+def test_checkpoint_loading_errors():
+    import torch
+    c = TINY["d"]
+    with Qwen(TINY, 1, 0.02) as m:
+        with pytest.raises(_lib.TensaiError, match="random-init"):
+            m.load_tensor("model.norm.weight", torch.ones(c, device="cuda"))
+    m = Qwen.__new__(Qwen)
+    h = ctypes.c_uint64()
+    from tensai_b200.decode import QwenConfig
+    _lib.check(_lib.load().tq_qwen_create_empty(ctypes.byref(QwenConfig(**TINY)), ctypes.byref(h)))
+    m.handle, m.cfg, m.last_times_ms = h.value, dict(TINY), (0.0, 0.0)
+    try:
+        with pytest.raises(_lib.TensaiError, match="unknown Qwen2 tensor"):
+            m.load_tensor("model.layers.0.self_attn.rotary.weight", torch.ones(c, device="cuda"))
+        with pytest.raises(_lib.TensaiError, match="unknown Qwen2 tensor"):
+            m.load_tensor("model.layers.9.input_layernorm.weight", torch.ones(c, device="cuda"))
+        with pytest.raises(_lib.TensaiError, match="expected"):
+            m.load_tensor("model.norm.weight", torch.ones(c + 1, device="cuda"))
+        m.load_tensor("model.norm.weight", torch.ones(c, device="cuda", dtype=torch.bfloat16))
+    finally:
+        m.free()
