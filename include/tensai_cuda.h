@@ -270,6 +270,24 @@ TQ_EXPORT int tq_gpt2_create(const tq_gpt2_config *cfg, uint64_t seed, float sig
 TQ_EXPORT int tq_gpt2_generate(uint64_t model, const int *prompt, int n_prompt, int n_gen, int *tokens,
                                float *times_ms);
 
+/* A GPT-2 model whose weights come from a checkpoint instead of the
+ * random-init generator: zeros, layer-norm weights 1, biases 0, until
+ * tq_gpt2_load_tensor fills them (the example's loader, _example/gpt2/model.go:
+ * 83-131). */
+TQ_EXPORT int tq_gpt2_create_empty(const tq_gpt2_config *cfg, uint64_t *model);
+
+/* One checkpoint tensor by the example's name, from device memory as stored
+ * (TQ_LINEAR_F32 / F16 / BF16; matrices rows x cols, vectors 1 x n): wte.weight
+ * (the embedding; the tied head wte^T is rebuilt from it, fp32 and int8),
+ * wpe.weight (the first ctx positions kept), ln_f.{weight,bias}, and per
+ * layer h.N. + ln_1.{weight,bias}, ln_2.{weight,bias},
+ * attn.c_attn.{weight,bias}, attn.c_proj.{weight,bias}, mlp.c_fc.{weight,bias},
+ * mlp.c_proj.{weight,bias}: Conv1D weights [in, out] kept in fp32 for the
+ * prefill and quantized to int8 (QuantizeMatrix) for the decode steps.
+ * Synchronous. TQ_ERR_SHAPE for a wrong shape, TQ_ERR_ARG for an unknown
+ * name or a model made by tq_gpt2_create. */
+TQ_EXPORT int tq_gpt2_load_tensor(uint64_t model, const char *name, const void *data, int dtype, int rows, int cols);
+
 /* How tq_gpt2_generate picks each generated token: temp <= 0 (the default)
  * greedy; temp > 0 the examples' sample step (main.go:78-105, tq_sample)
  * with draws[k], the caller's rng.Float64() for generated token k, so

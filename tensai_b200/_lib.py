@@ -67,6 +67,8 @@ SIGNATURES = {
     "tq_qwen_load_tensor": (I, [U64, ctypes.c_char_p, P, I, I, I]),
     "tq_sample": (I, [P, I, ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_int)]),
     "tq_gpt2_set_sampling": (I, [U64, ctypes.c_double, P, I]),
+    "tq_gpt2_create_empty": (I, [P, PU64]),
+    "tq_gpt2_load_tensor": (I, [U64, ctypes.c_char_p, P, I, I, I]),
     "tq_qwen_set_sampling": (I, [U64, ctypes.c_double, P, I]),
     "tq_qwen_free": (I, [U64]),
     "tq_qwen_shard_plan": (I, [P, I, I, P]),

@@ -5,6 +5,7 @@
 // that the Go code (gc at GOAMD64=v1) does not fuse.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -216,6 +217,21 @@ __global__ void attention_kernel(const float *q, int qstride, const float *kc, c
 }
 
 inline size_t attention_smem(int ctx) { return (sizeof(double) + sizeof(float)) * (size_t)ctx; }
+
+// dst[i] = float32 of src[i], a checkpoint tensor of type dtype (0 float32,
+// 1 float16, 2 bfloat16: TQ_LINEAR_*); both widenings are exact.
+__global__ void widen_kernel(const void *src, int dtype, float *dst, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v;
+        if (dtype == 0)
+            v = static_cast<const float *>(src)[i];
+        else if (dtype == 1)
+            v = __half2float(static_cast<const __half *>(src)[i]);
+        else
+            v = __uint_as_float((unsigned)static_cast<const unsigned short *>(src)[i] << 16);
+        dst[i] = v;
+    }
+}
 
 // ---- split-K decode attention -------------------------------------------------------
 // The attention of the decode step's single query row, spread over chunks of

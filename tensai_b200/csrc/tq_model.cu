@@ -20,6 +20,7 @@
 // next token and advances the state.
 #include <cstdio>
 #include <memory>
+#include <string>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -207,6 +208,7 @@ struct Gpt2 {
     AttScratch att_scr;
     cudaGraphExec_t graph = nullptr;
     std::vector<void *> allocs;
+    bool loaded = false; // tq_gpt2_create_empty: weights come from tq_gpt2_load_tensor
     // tq_gpt2_set_sampling: temp > 0 draws generated token k with draws[k]
     double temp = 0;
     double *draws = nullptr;
@@ -263,7 +265,10 @@ size_t attn_smem(const Gpt2 &m) { return attention_smem(m.c.ctx); }
 cudaError_t make_weight(Gpt2 &m, Weight &w, int rows, int cols, uint64_t seed, uint64_t stream, float sigma, int *rc) {
     w.rows = rows, w.cols = cols;
     TRY(dalloc(m, (void **)&w.w, sizeof(float) * (size_t)rows * cols));
-    TRY(tq_launch_synth(w.w, (size_t)rows * cols, seed, stream, sigma, m.st));
+    if (m.loaded) // filled by tq_gpt2_load_tensor
+        TRY(cudaMemsetAsync(w.w, 0, sizeof(float) * (size_t)rows * cols, m.st));
+    else
+        TRY(tq_launch_synth(w.w, (size_t)rows * cols, seed, stream, sigma, m.st));
     if ((*rc = tq_alloc_matrix(8, rows, cols, &w.q, m.st)) != TQ_OK) return cudaErrorMemoryAllocation;
     return tq_launch_quantize(w.q, w.w, m.st);
 }
@@ -274,8 +279,13 @@ cudaError_t build(Gpt2 &m, uint64_t seed, float sigma, int *rc) {
     TRY(cudaStreamCreateWithFlags(&m.st, cudaStreamNonBlocking));
     TRY(dalloc(m, (void **)&m.wte, sizeof(float) * (size_t)c.vocab * d));
     TRY(dalloc(m, (void **)&m.wpe, sizeof(float) * (size_t)c.ctx * d));
-    TRY(tq_launch_synth(m.wte, (size_t)c.vocab * d, seed, 1, sigma, m.st));
-    TRY(tq_launch_synth(m.wpe, (size_t)c.ctx * d, seed, 2, sigma, m.st));
+    if (m.loaded) {
+        TRY(cudaMemsetAsync(m.wte, 0, sizeof(float) * (size_t)c.vocab * d, m.st));
+        TRY(cudaMemsetAsync(m.wpe, 0, sizeof(float) * (size_t)c.ctx * d, m.st));
+    } else {
+        TRY(tq_launch_synth(m.wte, (size_t)c.vocab * d, seed, 1, sigma, m.st));
+        TRY(tq_launch_synth(m.wpe, (size_t)c.ctx * d, seed, 2, sigma, m.st));
+    }
     // wteT = wte^T (model.go:122), fp32 for the prefill head and its int8 twin.
     m.wteT.rows = d, m.wteT.cols = c.vocab;
     TRY(dalloc(m, (void **)&m.wteT.w, sizeof(float) * (size_t)d * c.vocab));
@@ -291,6 +301,15 @@ cudaError_t build(Gpt2 &m, uint64_t seed, float sigma, int *rc) {
     TRY(fill(ones, 1.f, vec, m.st));
     TRY(fill(zeros, 0.f, vec, m.st));
     m.lnfw = ones, m.lnfb = zeros;
+    // a checkpoint model gets its own norm weights and biases (1 and 0 until loaded)
+    auto vec_of = [&](float v, size_t n, float **out) -> cudaError_t {
+        TRY(dalloc(m, (void **)out, sizeof(float) * n));
+        return fill(*out, v, n, m.st);
+    };
+    if (m.loaded) {
+        TRY(vec_of(1.f, d, &m.lnfw));
+        TRY(vec_of(0.f, d, &m.lnfb));
+    }
     m.b.resize(c.n_layer);
     for (int l = 0; l < c.n_layer; l++) {
         Block &bl = m.b[l];
@@ -301,6 +320,16 @@ cudaError_t build(Gpt2 &m, uint64_t seed, float sigma, int *rc) {
         TRY(make_weight(m, bl.fc2, ffn, d, seed, s0 + 3, sigma, rc));
         bl.ln1w = bl.ln2w = ones;
         bl.ln1b = bl.ln2b = bl.attnB = bl.projB = bl.fcB = bl.fc2B = zeros;
+        if (m.loaded) {
+            TRY(vec_of(1.f, d, &bl.ln1w));
+            TRY(vec_of(1.f, d, &bl.ln2w));
+            TRY(vec_of(0.f, d, &bl.ln1b));
+            TRY(vec_of(0.f, d, &bl.ln2b));
+            TRY(vec_of(0.f, 3 * (size_t)d, &bl.attnB));
+            TRY(vec_of(0.f, d, &bl.projB));
+            TRY(vec_of(0.f, ffn, &bl.fcB));
+            TRY(vec_of(0.f, d, &bl.fc2B));
+        }
         TRY(dalloc(m, (void **)&bl.kc, sizeof(float) * (size_t)c.ctx * d));
         TRY(dalloc(m, (void **)&bl.vc, sizeof(float) * (size_t)c.ctx * d));
     }
@@ -435,7 +464,7 @@ std::shared_ptr<Gpt2> find_model(uint64_t h, int *rc) {
 
 extern "C" {
 
-int tq_gpt2_create(const tq_gpt2_config *cfg, uint64_t seed, float sigma, uint64_t *model) {
+static int gpt2_create(const tq_gpt2_config *cfg, uint64_t seed, float sigma, bool loaded, uint64_t *model) {
     if (!cfg || !model) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
     const tq_gpt2_config &c = *cfg;
     if (c.n_layer < 1 || c.n_head < 1 || c.d < 1 || c.ffn < 1 || c.vocab < 1 || c.ctx < 1 || c.d % c.n_head ||
@@ -445,6 +474,7 @@ int tq_gpt2_create(const tq_gpt2_config *cfg, uint64_t seed, float sigma, uint64
     if (c.ctx > 8192) return tq_fail(TQ_ERR_UNSUPPORTED, "tensai: context %d exceeds 8192", c.ctx);
     auto m = std::make_shared<Gpt2>();
     m->c = c;
+    m->loaded = loaded;
     cudaError_t e = cudaGetDevice(&m->device);
     int rc = TQ_OK;
     if (e == cudaSuccess) e = build(*m, seed, sigma, &rc);
@@ -455,6 +485,91 @@ int tq_gpt2_create(const tq_gpt2_config *cfg, uint64_t seed, float sigma, uint64
     std::lock_guard<std::mutex> lk(g_models_mu);
     *model = g_next_model++;
     g_models[*model] = m;
+    return TQ_OK;
+}
+
+int tq_gpt2_create(const tq_gpt2_config *cfg, uint64_t seed, float sigma, uint64_t *model) {
+    return gpt2_create(cfg, seed, sigma, false, model);
+}
+
+int tq_gpt2_create_empty(const tq_gpt2_config *cfg, uint64_t *model) { return gpt2_create(cfg, 0, 0.f, true, model); }
+
+int tq_gpt2_load_tensor(uint64_t model, const char *name, const void *data, int dtype, int rows, int cols) {
+    if (!name || !data) return tq_fail(TQ_ERR_ARG, "tensai: null pointer argument");
+    if (dtype != TQ_LINEAR_F32 && dtype != TQ_LINEAR_F16 && dtype != TQ_LINEAR_BF16)
+        return tq_fail(TQ_ERR_ARG, "tensai: unknown tensor type %d", dtype);
+    int rc = TQ_OK;
+    auto m = find_model(model, &rc);
+    if (!m) return rc;
+    if (!m->loaded) return tq_fail(TQ_ERR_ARG, "tensai: %s: the model holds random-init weights", name);
+    const tq_gpt2_config &c = m->c;
+    const int d = c.d, ffn = c.ffn;
+    cudaError_t e = cudaSetDevice(m->device);
+    if (e != cudaSuccess) return tq_cuda_fail(e, "tensor load");
+    auto shape = [&](int r, int cc) {
+        return rows == r && cols == cc ? TQ_OK
+                                       : tq_fail(TQ_ERR_SHAPE, "tensai: %s is %d x %d, expected %d x %d", name, rows,
+                                                 cols, r, cc);
+    };
+    auto widen = [&](float *dst, size_t n) {
+        widen_kernel<<<grid_for(n), kThreads, 0, m->st>>>(data, dtype, dst, n);
+        return cudaGetLastError();
+    };
+    // a Conv1D weight [in, out] (model.go:126-129): the fp32 prefill copy and its int8 twin
+    auto weight = [&](Weight &w) {
+        if ((rc = shape(w.rows, w.cols)) != TQ_OK) return rc;
+        cudaError_t err = widen(w.w, (size_t)w.rows * w.cols);
+        if (err == cudaSuccess) err = tq_launch_quantize(w.q, w.w, m->st);
+        return err == cudaSuccess ? TQ_OK : tq_cuda_fail(err, "tensor quantize");
+    };
+    auto vec = [&](float *dst, int n) {
+        if ((rc = shape(1, n)) != TQ_OK) return rc;
+        const cudaError_t err = widen(dst, (size_t)n);
+        return err == cudaSuccess ? TQ_OK : tq_cuda_fail(err, "tensor load");
+    };
+    const std::string n(name);
+    int l = -1, used = 0;
+    char rest[96] = {};
+    if (n == "wte.weight") { // the embedding and the tied head wte^T (model.go:106-119)
+        if ((rc = shape(c.vocab, d)) != TQ_OK) return rc;
+        e = widen(m->wte, (size_t)c.vocab * d);
+        if (e == cudaSuccess) {
+            transpose_kernel<<<dim3((d + 31) / 32, (c.vocab + 31) / 32), dim3(32, 8), 0, m->st>>>(m->wte, m->wteT.w,
+                                                                                                   c.vocab, d);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = tq_launch_quantize(m->wteT.q, m->wteT.w, m->st);
+        if (e != cudaSuccess) rc = tq_cuda_fail(e, "embedding");
+    } else if (n == "wpe.weight") { // positions beyond the model's context are not kept
+        if (cols != d || rows < c.ctx)
+            return tq_fail(TQ_ERR_SHAPE, "tensai: %s is %d x %d, expected at least %d x %d", name, rows, cols, c.ctx, d);
+        if ((e = widen(m->wpe, (size_t)c.ctx * d)) != cudaSuccess) rc = tq_cuda_fail(e, "positions");
+    } else if (n == "ln_f.weight") {
+        rc = vec(m->lnfw, d);
+    } else if (n == "ln_f.bias") {
+        rc = vec(m->lnfb, d);
+    } else if (std::sscanf(name, "h.%d.%95s%n", &l, rest, &used) == 2 && (size_t)used == n.size() && l >= 0 &&
+               l < c.n_layer) {
+        Block &b = m->b[l];
+        const std::string r(rest);
+        if (r == "ln_1.weight") rc = vec(b.ln1w, d);
+        else if (r == "ln_1.bias") rc = vec(b.ln1b, d);
+        else if (r == "ln_2.weight") rc = vec(b.ln2w, d);
+        else if (r == "ln_2.bias") rc = vec(b.ln2b, d);
+        else if (r == "attn.c_attn.weight") rc = weight(b.attn);
+        else if (r == "attn.c_attn.bias") rc = vec(b.attnB, 3 * d);
+        else if (r == "attn.c_proj.weight") rc = weight(b.proj);
+        else if (r == "attn.c_proj.bias") rc = vec(b.projB, d);
+        else if (r == "mlp.c_fc.weight") rc = weight(b.fc);
+        else if (r == "mlp.c_fc.bias") rc = vec(b.fcB, ffn);
+        else if (r == "mlp.c_proj.weight") rc = weight(b.fc2);
+        else if (r == "mlp.c_proj.bias") rc = vec(b.fc2B, d);
+        else rc = tq_fail(TQ_ERR_ARG, "tensai: unknown GPT-2 tensor %s", name);
+    } else {
+        rc = tq_fail(TQ_ERR_ARG, "tensai: unknown GPT-2 tensor %s", name);
+    }
+    if (rc != TQ_OK) return rc;
+    if ((e = cudaStreamSynchronize(m->st)) != cudaSuccess) return tq_cuda_fail(e, "tensor load");
     return TQ_OK;
 }
 

@@ -429,20 +429,6 @@ __global__ void copy_cols_kernel(const float *in, int in_cols, int in_col0, floa
     }
 }
 
-// dst[i] = float32 of src[i] (TQ_LINEAR_F32, F16 or BF16; both widenings exact).
-__global__ void widen_kernel(const void *src, int dtype, float *dst, size_t n) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        float v;
-        if (dtype == TQ_LINEAR_F32)
-            v = static_cast<const float *>(src)[i];
-        else if (dtype == TQ_LINEAR_F16)
-            v = __half2float(static_cast<const __half *>(src)[i]);
-        else
-            v = __uint_as_float((unsigned)static_cast<const unsigned short *>(src)[i] << 16);
-        dst[i] = v;
-    }
-}
-
 // ---- one-shot exchange over NVLink peer memory -----------------------------------
 // Each rank owns a slot area of [2 parities][world][cap] 8-byte words in its
 // own HBM, mapped into every other rank by CUDA IPC. Exchange call e (1, 2, …

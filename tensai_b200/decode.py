@@ -31,8 +31,32 @@ def synth_tokens(n: int, vocab: int, seed: int) -> np.ndarray:
     return out
 
 
+def _checkpoint_tensors(path: str):
+    """(name, CUDA tensor in its stored type) for each tensor of a .safetensors
+    file or a model.safetensors.index.json, one at a time."""
+    from . import safetensors as ST
+    src = ST.OpenSharded(path) if path.endswith(".json") else ST.Open(path)
+    try:
+        for name in src.Names():
+            f = src.File(name) if isinstance(src, ST.Shards) else src
+            yield name, f.DeviceTensor(name)
+    finally:
+        src.Close()
+
+
+def _load_into(fn, handle: int, name: str, t) -> None:
+    """tq_*_load_tensor of one CUDA tensor (float32, float16 or bfloat16)."""
+    import torch
+    kinds = {torch.float32: _lib.TQ_LINEAR_F32, torch.float16: _lib.TQ_LINEAR_F16, torch.bfloat16: _lib.TQ_LINEAR_BF16}
+    if t.dtype not in kinds or t.dim() not in (1, 2) or not t.is_contiguous():
+        raise ValueError(f"tensai: {name}: a contiguous 1-D or 2-D float32, float16 or bfloat16 tensor is required")
+    rows, cols = (1, t.shape[0]) if t.dim() == 1 else (t.shape[0], t.shape[1])
+    _lib.check(fn(handle, name.encode(), ctypes.c_void_p(t.data_ptr()), kinds[t.dtype], rows, cols))
+
+
 class Gpt2:
-    """A resident random-init GPT-2 on the current device."""
+    """A resident GPT-2 on the current device: random-init weights from a seed,
+    or a checkpoint's (from_checkpoint)."""
 
     def __init__(self, cfg: dict, seed: int, sigma: float = 0.02):
         self.cfg = dict(cfg)
@@ -41,6 +65,34 @@ class Gpt2:
         _lib.check(_lib.load().tq_gpt2_create(ctypes.byref(c), seed, ctypes.c_float(sigma), ctypes.byref(h)))
         self.handle = h.value
         self.last_times_ms = (0.0, 0.0)
+
+    @classmethod
+    def from_checkpoint(cls, cfg: dict, path: str) -> "Gpt2":
+        """A GPT-2 with a Hugging Face checkpoint's weights (the example's
+        loader, _example/gpt2/model.go:83-131): the tensors go to the GPU in
+        their stored type (tq_gpt2_create_empty, tq_gpt2_load_tensor); a
+        "transformer." name prefix is dropped, and the attention-mask buffers
+        and a tied lm_head.weight are skipped (the head is wte^T)."""
+        self = cls.__new__(cls)
+        self.cfg = dict(cfg)
+        h = ctypes.c_uint64()
+        _lib.check(_lib.load().tq_gpt2_create_empty(ctypes.byref(Gpt2Config(**self.cfg)), ctypes.byref(h)))
+        self.handle = h.value
+        self.last_times_ms = (0.0, 0.0)
+        try:
+            for name, t in _checkpoint_tensors(path):
+                name = name[len("transformer."):] if name.startswith("transformer.") else name
+                if name == "lm_head.weight" or name.endswith(".attn.bias") or name.endswith(".attn.masked_bias"):
+                    continue
+                self.load_tensor(name, t)
+        except BaseException:
+            self.free()
+            raise
+        return self
+
+    def load_tensor(self, name: str, t) -> None:
+        """One checkpoint tensor (a CUDA tensor as stored) by the example's name."""
+        _load_into(_lib.load().tq_gpt2_load_tensor, self.handle, name, t)
 
     def generate(self, prompt, n: int) -> np.ndarray:
         """Greedy ids of the n tokens after the prompt; last_times_ms holds the
@@ -149,7 +201,6 @@ class Qwen:
         its stored type and is quantized there (tq_qwen_create_empty,
         tq_qwen_load_tensor); a checkpoint without lm_head.weight ties it to
         the embedding."""
-        from . import safetensors as ST
         self = cls.__new__(cls)
         self.cfg = dict(cfg)
         c = QwenConfig(**self.cfg)
@@ -157,37 +208,26 @@ class Qwen:
         _lib.check(_lib.load().tq_qwen_create_empty(ctypes.byref(c), ctypes.byref(h)))
         self.handle = h.value
         self.last_times_ms = (0.0, 0.0)
-        src = ST.OpenSharded(path) if path.endswith(".json") else ST.Open(path)
-
-        def dev(name):
-            return (src.File(name) if isinstance(src, ST.Shards) else src).DeviceTensor(name)
-
         try:
-            names = src.Names()
-            for name in names:
+            embed, have_head = None, False
+            for name, t in _checkpoint_tensors(path):
                 if name.endswith("rotary_emb.inv_freq"):
                     continue  # recomputed from theta
-                self.load_tensor(name, dev(name))
-            if "lm_head.weight" not in names:
-                self.load_tensor("lm_head.weight", dev("model.embed_tokens.weight"))
+                self.load_tensor(name, t)
+                have_head = have_head or name == "lm_head.weight"
+                if name == "model.embed_tokens.weight":
+                    embed = t
+            if not have_head and embed is not None:
+                self.load_tensor("lm_head.weight", embed)
         except BaseException:
             self.free()
             raise
-        finally:
-            src.Close()
         return self
 
     def load_tensor(self, name: str, t) -> None:
         """One checkpoint tensor (a CUDA tensor of float32, float16 or
         bfloat16, in the checkpoint's layout) by its name (tq_qwen_load_tensor)."""
-        import torch
-        kinds = {torch.float32: _lib.TQ_LINEAR_F32, torch.float16: _lib.TQ_LINEAR_F16,
-                 torch.bfloat16: _lib.TQ_LINEAR_BF16}
-        if t.dtype not in kinds or t.dim() not in (1, 2) or not t.is_contiguous():
-            raise ValueError(f"tensai: {name}: a contiguous 1-D or 2-D float32, float16 or bfloat16 tensor is required")
-        rows, cols = (1, t.shape[0]) if t.dim() == 1 else (t.shape[0], t.shape[1])
-        _lib.check(_lib.load().tq_qwen_load_tensor(self.handle, name.encode(), ctypes.c_void_p(t.data_ptr()),
-                                                   kinds[t.dtype], rows, cols))
+        _load_into(_lib.load().tq_qwen_load_tensor, self.handle, name, t)
 
     def generate(self, prompt, n: int) -> np.ndarray:
         p = np.ascontiguousarray(prompt, np.int32)

@@ -88,3 +88,77 @@ def test_freed_model_handle_is_rejected():
     rc = L.tq_gpt2_generate(h, p.ctypes.data_as(ctypes.c_void_p), 2, 2, out.ctypes.data_as(ctypes.c_void_p), None)
     assert rc == _lib.TQ_ERR_HANDLE
     assert L.tq_gpt2_free(h) == _lib.TQ_OK
+
+
+# ---- checkpoint loading (tq_gpt2_create_empty / tq_gpt2_load_tensor) -----------
+
+def _gpt2_checkpoint(cfg, seed, sigma, ln=1.0, scale_in=1.0):
+    """The random-init model's weights under the example's tensor names
+    (Conv1D [in, out] layout, F32, a "transformer." prefix and an attention-mask
+    buffer as Hugging Face files carry them); layer-norm weights `ln`, biases
+    0; scale_in multiplies the matrices right after ln_1 and ln_2 (c_attn,
+    c_fc)."""
+    d, ffn, vocab, ctx = cfg["d"], cfg["ffn"], cfg["vocab"], cfg["ctx"]
+    f32 = np.float32
+    t = {"wte.weight": O.synth((vocab, d), seed, 1, sigma), "wpe.weight": O.synth((ctx, d), seed, 2, sigma),
+         "ln_f.weight": np.ones(d, f32), "ln_f.bias": np.zeros(d, f32)}
+    for l in range(cfg["n_layer"]):
+        s0, p = 16 + 8 * l, f"h.{l}."
+        t[p + "attn.c_attn.weight"] = O.synth((d, 3 * d), seed, s0, sigma) * f32(scale_in)
+        t[p + "attn.c_proj.weight"] = O.synth((d, d), seed, s0 + 1, sigma)
+        t[p + "mlp.c_fc.weight"] = O.synth((d, ffn), seed, s0 + 2, sigma) * f32(scale_in)
+        t[p + "mlp.c_proj.weight"] = O.synth((ffn, d), seed, s0 + 3, sigma)
+        for b, n in (("attn.c_attn.bias", 3 * d), ("attn.c_proj.bias", d), ("mlp.c_fc.bias", ffn),
+                     ("mlp.c_proj.bias", d), ("ln_1.bias", d), ("ln_2.bias", d)):
+            t[p + b] = np.zeros(n, f32)
+        t[p + "ln_1.weight"] = np.full(d, ln, f32)
+        t[p + "ln_2.weight"] = np.full(d, ln, f32)
+        t[p + "attn.bias"] = np.ones((1, 1, 4, 4), f32)  # a mask buffer: not a weight
+    return {"transformer." + k: v for k, v in t.items()}
+
+
+def test_gpt2_checkpoint_of_the_random_weights_gives_the_same_ids(tmp_path):
+    from tensai_b200 import safetensors as ST
+    from tensai_b200.decode import Gpt2
+    p = str(tmp_path / "gpt2.safetensors")
+    ST.SaveFile(p, _gpt2_checkpoint(TINY, 8, 0.02))
+    prompt = synth_tokens(16, TINY["vocab"], 8)
+    with Gpt2(TINY, 8, 0.02) as ref, Gpt2.from_checkpoint(TINY, p) as got:
+        assert np.array_equal(got.generate(prompt, 24), ref.generate(prompt, 24))
+
+
+def test_gpt2_checkpoint_layer_norm_weights_feed_their_matrices(tmp_path):
+    """ln_1 / ln_2 weights of 2 against c_attn / c_fc doubled: the same model
+    bit for bit (a power of two passes exactly through the fp32 prefill, the
+    int8 scales and the activations)."""
+    from tensai_b200 import safetensors as ST
+    from tensai_b200.decode import Gpt2
+    pa, pb = str(tmp_path / "a.safetensors"), str(tmp_path / "b.safetensors")
+    ST.SaveFile(pa, _gpt2_checkpoint(TINY, 9, 0.02, ln=2.0))
+    ST.SaveFile(pb, _gpt2_checkpoint(TINY, 9, 0.02, scale_in=2.0))
+    prompt = synth_tokens(16, TINY["vocab"], 9)
+    with Gpt2.from_checkpoint(TINY, pa) as a, Gpt2.from_checkpoint(TINY, pb) as b:
+        assert np.array_equal(a.generate(prompt, 24), b.generate(prompt, 24))
+
+
+def test_gpt2_checkpoint_loading_errors():
+    import torch
+
+    from tensai_b200.decode import Gpt2
+    d = TINY["d"]
+    with Gpt2(TINY, 1, 0.02) as m:
+        with pytest.raises(_lib.TensaiError, match="random-init"):
+            m.load_tensor("ln_f.weight", torch.ones(d, device="cuda"))
+    with pytest.raises(_lib.TensaiError, match="unknown GPT-2 tensor"):
+        Gpt2.from_checkpoint(TINY, _one_tensor_file(d, "h.0.attn.rotary"))
+    with pytest.raises(_lib.TensaiError, match="expected"):
+        Gpt2.from_checkpoint(TINY, _one_tensor_file(d + 1, "ln_f.weight"))
+
+
+def _one_tensor_file(n, name):
+    import tempfile
+
+    from tensai_b200 import safetensors as ST
+    p = tempfile.mktemp(suffix=".safetensors")
+    ST.SaveFile(p, {name: np.ones(n, np.float32)})
+    return p
