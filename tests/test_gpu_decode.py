@@ -141,24 +141,19 @@ def test_gpt2_checkpoint_layer_norm_weights_feed_their_matrices(tmp_path):
         assert np.array_equal(a.generate(prompt, 24), b.generate(prompt, 24))
 
 
-def test_gpt2_checkpoint_loading_errors():
+def test_gpt2_checkpoint_loading_errors(tmp_path):
     import torch
 
+    from tensai_b200 import safetensors as ST
     from tensai_b200.decode import Gpt2
     d = TINY["d"]
     with Gpt2(TINY, 1, 0.02) as m:
         with pytest.raises(_lib.TensaiError, match="random-init"):
             m.load_tensor("ln_f.weight", torch.ones(d, device="cuda"))
+    unknown, short = str(tmp_path / "unknown.safetensors"), str(tmp_path / "short.safetensors")
+    ST.SaveFile(unknown, {"h.0.attn.rotary": np.ones(d, np.float32)})
+    ST.SaveFile(short, {"ln_f.weight": np.ones(d + 1, np.float32)})
     with pytest.raises(_lib.TensaiError, match="unknown GPT-2 tensor"):
-        Gpt2.from_checkpoint(TINY, _one_tensor_file(d, "h.0.attn.rotary"))
+        Gpt2.from_checkpoint(TINY, unknown)
     with pytest.raises(_lib.TensaiError, match="expected"):
-        Gpt2.from_checkpoint(TINY, _one_tensor_file(d + 1, "ln_f.weight"))
-
-
-def _one_tensor_file(n, name):
-    import tempfile
-
-    from tensai_b200 import safetensors as ST
-    p = tempfile.mktemp(suffix=".safetensors")
-    ST.SaveFile(p, {name: np.ones(n, np.float32)})
-    return p
+        Gpt2.from_checkpoint(TINY, short)
