@@ -178,9 +178,10 @@ def broadcast_nccl_id(dist) -> bytes:
 
 
 class Qwen:
-    """This rank's shard of a resident random-init Qwen2 (int4) on the current
-    device. world > 1: every rank builds its shard at the same time with the
-    same nccl_id (see broadcast_nccl_id) and calls generate together."""
+    """This rank's shard of a resident Qwen2 (int4) on the current device:
+    random-init weights from a seed, or (one GPU) a checkpoint's
+    (from_checkpoint). world > 1: every rank builds its shard at the same time
+    with the same nccl_id (see broadcast_nccl_id) and calls generate together."""
 
     def __init__(self, cfg: dict, seed: int, sigma: float = 0.02, rank: int = 0, world: int = 1,
                  nccl_id: bytes | None = None):
