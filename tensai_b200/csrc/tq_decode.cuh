@@ -407,9 +407,9 @@ __global__ void __launch_bounds__(kAttWThreads) att_weighted_kernel(const float 
                                                                     int hd, int group, const double *scores,
                                                                     const double *stats, float *partial,
                                                                     unsigned *count, float *out, int ctx,
-                                                                    int nchunks, int nschunks) {
+                                                                    int nchunks, int nschunks, int release) {
     step_entry_wait();
-    step_release_next(); // the o_proj matvec streams its weights meanwhile
+    if (release) step_release_next(); // the o_proj matvec streams its weights meanwhile
     extern __shared__ __align__(16) float att_sm[];
     __shared__ double ml[kAttMaxGroup][2];
     __shared__ int last;
@@ -550,9 +550,11 @@ inline cudaError_t att_setup(int hd, int group) {
 }
 
 // The decode-step attention of q (heads x hd) over cached positions 0..state[1].
+// release: let the next kernel (the o_proj matvec) be scheduled as the value
+// pass starts (measured faster on one GPU; the tensor-parallel step keeps it off).
 inline cudaError_t decode_attention(const float *q, const float *kc, const float *vc, int kvstride, float *out,
                                     const int *state, int heads, int hd, int group, double scale, const AttScratch &a,
-                                    cudaStream_t st, const AttRope &rope = AttRope()) {
+                                    cudaStream_t st, const AttRope &rope = AttRope(), bool release = true) {
     if (hd % 32 || hd > kAttMaxHd || kAttWThreads % hd || group < 1 || group > kAttMaxGroup || heads % group)
         return cudaErrorInvalidValue;
     cudaError_t e = step_launch(att_scores_kernel, dim3(heads / group, a.nschunks), dim3(32 * group),
@@ -561,7 +563,7 @@ inline cudaError_t decode_attention(const float *q, const float *kc, const float
     if (e == cudaSuccess)
         e = step_launch(att_weighted_kernel, dim3(heads / group, a.nchunks), dim3(kAttWThreads),
                         att_weighted_smem(hd, group), st, vc, kvstride, state, hd, group, a.scores, a.stats,
-                        a.partial, a.count, out, a.ctx, a.nchunks, a.nschunks);
+                        a.partial, a.count, out, a.ctx, a.nchunks, a.nschunks, release ? 1 : 0);
     return e;
 }
 

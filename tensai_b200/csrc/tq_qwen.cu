@@ -486,7 +486,6 @@ __device__ __noinline__ unsigned long long ar_wait(const unsigned long long *p, 
 __global__ void __launch_bounds__(1024) ar_rmsnorm_kernel(ArLink L, float *x, const float *y, const float *w,
                                                           float *out, int n, double eps, unsigned *status) {
     step_entry();
-    step_release_next();
     extern __shared__ float recv[]; // [world-1][n], peers in the order rank+1, rank+2, …
     __shared__ double sh[32];
     __shared__ unsigned long long *slot[kArMaxWorld];
@@ -1002,7 +1001,7 @@ cudaError_t step(Qwen &m, int n_prompt) {
         rope.kc = ly.kc;
         rope.vc = ly.vc;
         TRY(decode_attention(m.qkv, ly.kc, ly.vc, m.kvd, m.att, m.state, m.nq, m.hd, m.group,
-                             1.0 / sqrt((double)m.hd), m.att_scr, m.st, rope));
+                             1.0 / sqrt((double)m.hd), m.att_scr, m.st, rope, m.world == 1));
         TRY(tq_launch_matmul(ly.o, m.att + m.arow, m.y, 1, m.scr, m.st));
         TRY(add_norm(ly.ln2)); // x += o_proj, then norm
         TRY(tq_launch_cmv_epi(ly.gu, m.a, m.h, m.scr, m.st, TQ_EPI_SWIGLU, tq_matvec_uses_tmv()));
