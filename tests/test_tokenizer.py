@@ -91,6 +91,17 @@ TESTS = CORPUS + [
     "",
     " ",
     "\n",
+    "é café ño",  # combining marks (category M)
+    "\U0001F468‍\U0001F469‍\U0001F467 family",  # a zero-width-joiner sequence
+    "no break space and em space",
+    "\r\n\r\nwindows\r\nlines\r\n",
+    "\t\tindent\n\t  mixed \n",
+    "12345678901234567890 and ١٢٣٤٥ and ⅫⅬ",
+    "'quotes'' it''s rock'n'roll ''",
+    "中文字符和English混合123",
+    "!!!\n\n???   ...\r\n",
+    "trailing space ",
+    "   ",
 ]
 
 
